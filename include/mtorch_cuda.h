@@ -1,0 +1,226 @@
+/*
+ * mtorch_cuda.h — C ABI of the B200 (sm_100a) kernel library behind mtorch's `cuda` device.
+ *
+ * Every entry point takes plain device pointers, sizes, strides (in ELEMENTS) and a
+ * `cudaStream_t` passed as `void*` (NULL = legacy default stream).  No C++ or torch types cross
+ * this boundary; the library never allocates device memory on its own behalf: scratch space is
+ * passed in by the caller as a workspace whose size is reported by a `*_workspace_size` query.
+ * Each function returns MT_OK (0) or an `mt_status` code; `mt_cuda_last_error_string()` gives a
+ * human-readable reason for the last failure on the calling thread.
+ *
+ * The functions replace, one for one, the portable CPU op functions of the reference core
+ * (cpp/mtorch/core/tensor.h); the citation above each declaration names the function whose
+ * result the device path reproduces.  The CPython layer (the reference's
+ * cpp/mtorch/python/module.cpp, or this repository's mtorch_b200 package) keeps argument
+ * parsing, broadcasting rules, dtype promotion and error translation; these kernels receive
+ * already-validated descriptors.
+ */
+#ifndef MTORCH_CUDA_H_
+#define MTORCH_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status, dtypes -------------------------------------------------------------------- */
+typedef enum {
+  MT_OK = 0,
+  MT_ERR_INVALID = 1,     /* bad argument (shape, stride, alignment, null pointer)          */
+  MT_ERR_UNSUPPORTED = 2, /* valid request the device path does not implement: caller raises */
+  MT_ERR_LAUNCH = 3,      /* CUDA launch / runtime error                                     */
+  MT_ERR_TIMEOUT = 4,     /* a bounded device-side wait expired (kernel returned early)      */
+  MT_ERR_WORKSPACE = 5    /* workspace missing or smaller than the *_workspace_size query    */
+} mt_status;
+
+/* Element types.  The reference's ScalarType (tensor.h:13-20) has no bfloat16; the device path
+ * adds it (MT_BF16) as a storage/compute type for the Stable-Diffusion configurations. */
+typedef enum { MT_F32 = 0, MT_BF16 = 1, MT_F16 = 2, MT_F64 = 3, MT_I32 = 4, MT_I64 = 5, MT_BOOL = 6 } mt_dtype;
+
+/* Maximum tensor rank handled by the strided elementwise kernels. */
+#define MT_MAX_DIMS 8
+
+const char* mt_cuda_last_error_string(void);
+/* Number of visible devices (0 when there is no driver / GPU). */
+int mt_cuda_device_count(void);
+/* Replaces the reference's device check `require_cpu_device` (tensor.cpp:231-239): makes
+ * `device` current on the calling thread and verifies it is an sm_100 part. */
+int mt_cuda_set_device(int device);
+int mt_cuda_synchronize(void* stream);
+/* Device-side error word written by bounded waits inside kernels (MT_ERR_TIMEOUT); `clear`
+ * resets it.  Returns MT_OK when no kernel reported a problem. */
+int mt_cuda_device_status(int clear);
+
+/* ---- memory movement: replaces `to` (tensor.cpp:8479-8505) and `contiguous` (tensor.cpp:8210) */
+/* kind: 0 = host->device, 1 = device->host, 2 = device->device. */
+int mt_cuda_memcpy(void* dst, const void* src, size_t bytes, int kind, void* stream);
+int mt_cuda_memset(void* dst, int value, size_t bytes, void* stream);
+/* Strided copy with dtype conversion (f32/bf16/f16/f64 <-> each other):
+ * dst[i0..] = cast(src[i0..]) over `ndim` dims of `sizes`, each side with its own strides. */
+int mt_cuda_copy_strided(void* dst, int dst_dtype, const int64_t* dst_strides, const void* src, int src_dtype,
+                         const int64_t* src_strides, const int64_t* sizes, int ndim, void* stream);
+/* Device counterpart of mtorch's uniform_ for contiguous tensors (module.cpp:335-365 with
+ * next_random_u64 / next_uniform_open at module.cpp:76-88): element i receives the (i+1)-th draw
+ * of SplitMix64 after `state`, so results are bit-identical to the host generator.  The caller
+ * advances its host state by `n` draws afterwards. */
+int mt_cuda_fill_uniform(void* dst, int dtype, int64_t n, uint64_t state, double from, double to, void* stream);
+int mt_cuda_fill(void* dst, int dtype, int64_t n, double value, void* stream);
+
+/* ---- elementwise ------------------------------------------------------------------------- */
+typedef enum { MT_UNARY_SILU = 0, MT_UNARY_GELU = 1, MT_UNARY_GELU_TANH = 2, MT_UNARY_NEG = 3,
+               MT_UNARY_EXP = 4, MT_UNARY_SIGMOID = 5, MT_UNARY_RELU = 6 } mt_unary_op;
+/* Replaces `silu` (tensor.cpp:16480-16600) and `gelu` (tensor.cpp:17207-17290).  Contiguous,
+ * n elements; x and y may alias; dtypes may differ (compute in fp32). */
+int mt_cuda_unary(int op, void* y, int y_dtype, const void* x, int x_dtype, int64_t n, void* stream);
+
+typedef enum { MT_BIN_ADD = 0, MT_BIN_SUB = 1, MT_BIN_MUL = 2, MT_BIN_DIV = 3 } mt_binary_op;
+/* Replaces `binary_tensor_tensor` (tensor.cpp:18965-19104): y = a OP b over the broadcast shape
+ * `sizes` (ndim <= MT_MAX_DIMS); each operand gives its strides for that shape (0 on broadcast
+ * dims).  `b` may be NULL, in which case `scalar` is the right operand (binary_tensor_scalar,
+ * tensor.cpp:19106).  Output is written with `y_strides`. */
+int mt_cuda_binary(int op, void* y, int y_dtype, const int64_t* y_strides, const void* a, int a_dtype,
+                   const int64_t* a_strides, const void* b, int b_dtype, const int64_t* b_strides, double scalar,
+                   const int64_t* sizes, int ndim, void* stream);
+/* Fused a*x + b*y + c*z (y, z may be NULL) over contiguous n elements, fp32 math: the DDIM latent
+ * update of the reference's scheduler scenario (tests/compat/benchmarking.py:6148-6168). */
+int mt_cuda_axpby(void* out, int out_dtype, const void* x, int x_dtype, double a, const void* y, int y_dtype,
+                  double b, const void* z, int z_dtype, double c, int64_t n, void* stream);
+
+/* ---- normalisation / softmax ------------------------------------------------------------- */
+/* Replaces `softmax` (tensor.cpp:15145-15213, fp32 kernel 7508-7742) along the innermost,
+ * contiguous dimension: rows x cols, row pitch `ld` (elements). */
+int mt_cuda_softmax(void* y, int y_dtype, const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ld,
+                    int log_output, void* stream);
+/* Replaces `layer_norm` (tensor.cpp:17386-17714) over the last `cols` elements of each row
+ * (weight/bias optional, length cols). */
+int mt_cuda_layer_norm(void* y, int y_dtype, const void* x, int x_dtype, const void* weight, const void* bias,
+                       int wb_dtype, int64_t rows, int64_t cols, double eps, void* stream);
+/* Replaces `group_norm` (tensor.cpp:18643-18963).  Input is [N, C, HW] with element strides
+ * (sn, sc, shw) — NCHW contiguous is (C*HW, HW, 1), channels-last is (HW*C, 1, C); output uses
+ * its own strides.  `fuse_silu` applies x*sigmoid(x) after the affine (the SD ResNet pattern
+ * GroupNorm -> SiLU).  Workspace: mt_cuda_group_norm_workspace_size(). */
+size_t mt_cuda_group_norm_workspace_size(int64_t N, int64_t C, int64_t HW, int64_t groups);
+int mt_cuda_group_norm(void* y, int y_dtype, const int64_t* y_strides, const void* x, int x_dtype,
+                       const int64_t* x_strides, const void* weight, const void* bias, int wb_dtype, int64_t N,
+                       int64_t C, int64_t HW, int64_t groups, double eps, int fuse_silu, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ---- dense contractions on tcgen05 / TMEM ---------------------------------------------- */
+typedef enum {
+  MT_EPI_NONE = 0,
+  MT_EPI_GELU = 1,  /* y = gelu(acc + bias)                                                       */
+  MT_EPI_SILU = 2,  /* y = silu(acc + bias)                                                       */
+  MT_EPI_GEGLU = 3  /* B columns come in (64 value, 64 gate) groups: y[:, j] = v_j * gelu(g_j), N/2 */
+} mt_epilogue;
+
+/*
+ * D[b] = alpha * op(A[b]) @ op(B[b]) + beta * C[b] + bias  (then activation, then + residual)
+ *
+ * Replaces `matmul` (tensor.cpp:24896-25064), `bmm` (25066-25182), `addmm` (25184-25366),
+ * `baddbmm` (25557-25694) and `linear` (31401-31694).  A is M x K, B is K x N (logical).
+ *   a_trans = 0: A stored row-major [M, K] with row pitch lda;  1: stored [K, M] (pitch lda).
+ *   b_trans = 0: B stored row-major [K, N] (pitch ldb, the matmul case);
+ *             1: stored [N, K] (pitch ldb, the linear-weight case, y = x @ W^T).
+ * Batched operands step by stride_* elements per batch (0 broadcasts).  bias is length N
+ * (bias_batch_stride 0) or [batch, N] (stride N).  residual (optional) is [M, N] per batch with
+ * pitch ldr.  dtype: MT_BF16/MT_F16 run kind::f16 with fp32 accumulation; MT_F32 runs three
+ * tf32 tensor-core products (hi*hi + hi*lo + lo*hi, "3xTF32") for ~fp32 accuracy.
+ * Workspace: mt_cuda_gemm_workspace_size(desc).
+ */
+typedef struct {
+  int64_t M, N, K, batch;
+  int dtype;      /* input dtype of A and B                                                 */
+  int out_dtype;  /* dtype of D (and C / residual)                                          */
+  const void* A; int64_t lda, stride_a; int a_trans;
+  const void* B; int64_t ldb, stride_b; int b_trans;
+  void* D; int64_t ldd, stride_d;
+  const void* C; int64_t ldc, stride_c; /* used when beta != 0                             */
+  const void* bias; int bias_dtype; int64_t bias_batch_stride;
+  const void* residual; int64_t ldr, stride_r;
+  float alpha, beta;
+  int epilogue;   /* mt_epilogue */
+  /* MT_F32 only, optional: precomputed low parts (x - tf32_truncate(x)) of A ([M, Kp] per batch)
+   * and B ([N, Kp] per batch), Kp = K rounded up to a multiple of 4, e.g. cached for a constant
+   * weight.  NULL = computed into the workspace on every call. */
+  const void* A_lo; const void* B_lo;
+} mt_gemm_desc;
+size_t mt_cuda_gemm_workspace_size(const mt_gemm_desc* desc);
+int mt_cuda_gemm(const mt_gemm_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * 2-D convolution.  Replaces `conv2d` (tensor.cpp:26490-27528; portable loop 27359-27400).
+ * x is [N, C, H, W] given by element strides (NCHW or channels-last), weight is [K, C, R, S]
+ * (torch layout, contiguous) or pre-packed, output [N, K, P, Q] with its own strides.  bias:
+ * length K, or [N, K] when bias_batch_stride == K (per-sample bias: the SD ResNet time-embedding
+ * add).  residual (optional) has the output's shape and `res_strides`.  groups > 1 is
+ * MT_ERR_UNSUPPORTED.  Stride-1 convolutions with C % 64 == 0 (bf16/f16) or C % 32 == 0 (fp32)
+ * run as implicit GEMM (4-D TMA boxes over channels-last activations, zero padding from TMA
+ * out-of-bounds fill); others go through an explicit im2col gather + the same GEMM.
+ */
+typedef struct {
+  int64_t N, C, H, W, K, R, S, P, Q;
+  int stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, groups;
+  int dtype, out_dtype;
+  const void* x; int64_t x_strides[4];
+  const void* w;
+  /* w_packed = 1: `w` is already [K, R, S, Cp] contiguous (Cp = mt_cuda_conv2d_packed_channels)
+   * from mt_cuda_conv2d_pack_weight and, for MT_F32, `w_lo` its tf32 low part (or NULL). */
+  int w_packed; const void* w_lo;
+  const void* bias; int bias_dtype; int64_t bias_batch_stride;
+  const void* residual; int64_t res_strides[4];
+  void* y; int64_t y_strides[4];
+  int epilogue;
+} mt_conv2d_desc;
+size_t mt_cuda_conv2d_workspace_size(const mt_conv2d_desc* desc);
+int mt_cuda_conv2d(const mt_conv2d_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+/* Repacks a torch-layout weight [K, C, R, S] into [K, R, S, Cp] (Cp = C rounded up to a 16-byte
+ * multiple) and, for MT_F32 with w_lo != NULL, writes the tf32 low part beside it.  Used once
+ * per weight version by the module layer. */
+int64_t mt_cuda_conv2d_packed_channels(int64_t C, int64_t R, int64_t S, int dtype);
+int mt_cuda_conv2d_pack_weight(void* w_packed, void* w_lo, const void* w, int dtype, int64_t K, int64_t C,
+                               int64_t R, int64_t S, void* stream);
+
+/*
+ * Fused attention O = softmax(Q K^T * scale + mask) V.  Replaces
+ * `scaled_dot_product_attention` (tensor.cpp:30930-31324; portable loop 31158-31207).
+ * Q [B, H, Sq, D], K [B, Hkv, Sk, D], V [B, Hkv, Sk, Dv], O [B, H, Sq, Dv], each with element
+ * strides (b, h, s, d); H % Hkv == 0 (grouped-query attention, enable_gqa).  mask_kind 0 = none,
+ * 1 = bool (nonzero keeps, uint8 storage), 2 = additive float in `mask_dtype`; the mask is indexed
+ * with `mask_strides` over (b, h, q, k), zeros for broadcast dims.  causal masks key > query.
+ * bf16/f16 run a flash-style tcgen05 kernel (fp32 online softmax) where the shape allows; f32
+ * and the remaining cases run an fp32 SIMT flash kernel.  Workspace: mt_cuda_sdpa_workspace_size.
+ */
+typedef struct {
+  int64_t B, H, Hkv, Sq, Sk, D, Dv;
+  int dtype;
+  const void* q; int64_t q_strides[4];
+  const void* k; int64_t k_strides[4];
+  const void* v; int64_t v_strides[4];
+  void* o; int64_t o_strides[4];
+  const void* mask; int mask_kind; int mask_dtype; int64_t mask_strides[4];
+  int causal;
+  double scale;
+} mt_sdpa_desc;
+size_t mt_cuda_sdpa_workspace_size(const mt_sdpa_desc* desc);
+int mt_cuda_sdpa(const mt_sdpa_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- host random generator: the reference's RandomState (module.cpp:47-183) ------------- */
+/* SplitMix64 + Marsaglia-polar normal with the odd-count "spare" rule, bit-identical to
+ * mtorch.manual_seed / randn / normal_ / uniform_ on contiguous float tensors.  The state is a
+ * caller-owned struct so Python can keep mtorch's single global generator. */
+typedef struct {
+  uint64_t state;
+  int32_t has_spare;
+  double spare;
+} mt_rng_state;
+void mt_rng_seed(mt_rng_state* rng, uint64_t seed);
+/* dtype MT_F32 or MT_F64 host buffer, n contiguous elements, value = mean + std * N(0,1). */
+void mt_rng_fill_normal(mt_rng_state* rng, void* dst, int dtype, int64_t n, double mean, double std);
+void mt_rng_fill_uniform(mt_rng_state* rng, void* dst, int dtype, int64_t n, double from, double to);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MTORCH_CUDA_H_ */

@@ -1,0 +1,454 @@
+// Memory-bound kernels: strided copy / cast, fills (incl. the SplitMix64 uniform stream),
+// unary activations, broadcast binary ops, the fused DDIM axpby, and the operand packing
+// kernels used by the tensor-core paths (transpose + tf32 split, conv im2col, weight repack).
+#include "runtime.h"
+
+namespace mt {
+
+struct StridedND {
+  int ndim;
+  int64_t sizes[MT_MAX_DIMS];
+  int64_t s0[MT_MAX_DIMS];
+  int64_t s1[MT_MAX_DIMS];
+  int64_t s2[MT_MAX_DIMS];
+};
+
+__device__ __forceinline__ void nd_offsets(const StridedND& nd, int64_t linear, int64_t& o0, int64_t& o1,
+                                           int64_t& o2) {
+  o0 = o1 = o2 = 0;
+  for (int d = nd.ndim - 1; d >= 0; --d) {
+    const int64_t sz = nd.sizes[d];
+    const int64_t c = linear % sz;
+    linear /= sz;
+    o0 += c * nd.s0[d];
+    o1 += c * nd.s1[d];
+    o2 += c * nd.s2[d];
+  }
+}
+
+static int grid_for(int64_t n, int threads) {
+  int64_t blocks = (n + threads - 1) / threads;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+#define MT_GRID_STRIDE(i, n) \
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (n); i += (int64_t)gridDim.x * blockDim.x)
+
+// ---------------------------------------------------------------------------------------------
+__global__ void copy_strided_kernel(void* dst, int dd, const void* src, int sd, StridedND nd, int64_t n) {
+  MT_GRID_STRIDE(i, n) {
+    int64_t od, os, unused;
+    nd_offsets(nd, i, od, os, unused);
+    if (dd == MT_F64 || sd == MT_F64)
+      store_from_f64(dst, od, dd, load_as_f64(src, os, sd));
+    else
+      store_from_f32(dst, od, dd, load_as_f32(src, os, sd));
+  }
+}
+
+// Contiguous same-dtype 16-byte copies.
+__global__ void copy_vec16_kernel(uint4* dst, const uint4* src, int64_t n16) {
+  MT_GRID_STRIDE(i, n16) dst[i] = src[i];
+}
+
+template <typename TD, typename TS>
+__global__ void cast_contig_kernel(TD* dst, const TS* src, int64_t n) {
+  MT_GRID_STRIDE(i, n) dst[i] = from_f32<TD>(to_f32<TS>(src[i]));
+}
+
+static bool is_contig(const int64_t* st, const int64_t* sizes, int ndim) {
+  int64_t expect = 1;
+  for (int d = ndim - 1; d >= 0; --d) {
+    if (sizes[d] != 1 && st[d] != expect) return false;
+    expect *= sizes[d];
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------------------------
+// SplitMix64 stream: the k-th draw after `state` is mix(state + k * golden).  Matches
+// next_random_u64 / next_uniform_open of the reference generator (module.cpp:76-88); the double
+// arithmetic uses explicit round-to-nearest intrinsics so that no FMA contraction changes the last
+// bit relative to the host code.
+__device__ __forceinline__ uint64_t splitmix_draw(uint64_t state, uint64_t k) {
+  uint64_t v = state + k * 0x9E3779B97F4A7C15ULL;
+  v = (v ^ (v >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  v = (v ^ (v >> 27)) * 0x94D049BB133111EBULL;
+  return v ^ (v >> 31);
+}
+__global__ void fill_uniform_kernel(void* dst, int dtype, int64_t n, uint64_t state, double from, double scale) {
+  const double kScale = 1.0 / 9007199254740992.0;
+  MT_GRID_STRIDE(i, n) {
+    double u = __dmul_rn((double)(splitmix_draw(state, (uint64_t)i + 1) >> 11), kScale);
+    if (u <= 0.0) u = kScale;
+    const double v = __dadd_rn(from, __dmul_rn(scale, u));
+    store_from_f64(dst, i, dtype, v);
+  }
+}
+__global__ void fill_kernel(void* dst, int dtype, int64_t n, double value) {
+  MT_GRID_STRIDE(i, n) store_from_f64(dst, i, dtype, value);
+}
+
+__global__ void fill_strided_kernel(void* dst, int dtype, StridedND nd, int64_t n, double value) {
+  MT_GRID_STRIDE(i, n) {
+    int64_t o, u1, u2;
+    nd_offsets(nd, i, o, u1, u2);
+    store_from_f64(dst, o, dtype, value);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float apply_unary(int op, float x) {
+  switch (op) {
+    case MT_UNARY_SILU: return silu_f(x);
+    case MT_UNARY_GELU: return gelu_f(x);
+    case MT_UNARY_GELU_TANH: return gelu_tanh_f(x);
+    case MT_UNARY_NEG: return -x;
+    case MT_UNARY_EXP: return expf(x);
+    case MT_UNARY_SIGMOID: return 1.0f / (1.0f + expf(-x));
+    case MT_UNARY_RELU: return x > 0.f ? x : 0.f;
+    default: return x;
+  }
+}
+__global__ void unary_f32_kernel(int op, float* y, const float* x, int64_t n) {
+  MT_GRID_STRIDE(i, n) y[i] = apply_unary(op, x[i]);
+}
+// bf16 -> bf16, 8 elements per thread.
+__global__ void unary_bf16x8_kernel(int op, uint4* y, const uint4* x, int64_t n8) {
+  MT_GRID_STRIDE(i, n8) {
+    uint4 v = x[i];
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      h[j] = __floats2bfloat162_rn(apply_unary(op, f.x), apply_unary(op, f.y));
+    }
+    y[i] = v;
+  }
+}
+__global__ void unary_generic_kernel(int op, void* y, int yd, const void* x, int xd, int64_t n) {
+  MT_GRID_STRIDE(i, n) store_from_f32(y, i, yd, apply_unary(op, load_as_f32(x, i, xd)));
+}
+
+// ---------------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ T apply_binary(int op, T a, T b) {
+  switch (op) {
+    case MT_BIN_ADD: return a + b;
+    case MT_BIN_SUB: return a - b;
+    case MT_BIN_MUL: return a * b;
+    case MT_BIN_DIV: return a / b;
+    default: return a;
+  }
+}
+// Generic broadcast: fp32 math (fp64 when any operand is f64).
+__global__ void binary_strided_kernel(int op, void* y, int yd, const void* a, int ad, const void* b, int bd,
+                                      double scalar, StridedND nd, int64_t n) {
+  const bool wide = (yd == MT_F64 || ad == MT_F64 || (b && bd == MT_F64));
+  MT_GRID_STRIDE(i, n) {
+    int64_t oy, oa, ob;
+    nd_offsets(nd, i, oy, oa, ob);
+    if (wide) {
+      const double bv = b ? load_as_f64(b, ob, bd) : scalar;
+      store_from_f64(y, oy, yd, apply_binary<double>(op, load_as_f64(a, oa, ad), bv));
+    } else {
+      const float bv = b ? load_as_f32(b, ob, bd) : (float)scalar;
+      store_from_f32(y, oy, yd, apply_binary<float>(op, load_as_f32(a, oa, ad), bv));
+    }
+  }
+}
+// Same-shape contiguous fp32 / bf16 fast paths (vectorised).
+__global__ void binary_f32x4_kernel(int op, float4* y, const float4* a, const float4* b, int64_t n4) {
+  MT_GRID_STRIDE(i, n4) {
+    float4 va = a[i], vb = b[i];
+    y[i] = make_float4(apply_binary<float>(op, va.x, vb.x), apply_binary<float>(op, va.y, vb.y),
+                       apply_binary<float>(op, va.z, vb.z), apply_binary<float>(op, va.w, vb.w));
+  }
+}
+__global__ void binary_bf16x8_kernel(int op, uint4* y, const uint4* a, const uint4* b, int64_t n8) {
+  MT_GRID_STRIDE(i, n8) {
+    uint4 va = a[i], vb = b[i], vy;
+    const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&va);
+    const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&vb);
+    __nv_bfloat162* hy = reinterpret_cast<__nv_bfloat162*>(&vy);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 fa = __bfloat1622float2(ha[j]), fb = __bfloat1622float2(hb[j]);
+      hy[j] = __floats2bfloat162_rn(apply_binary<float>(op, fa.x, fb.x), apply_binary<float>(op, fa.y, fb.y));
+    }
+    y[i] = vy;
+  }
+}
+
+__global__ void axpby_kernel(void* out, int od, const void* x, int xd, float a, const void* y, int yd, float b,
+                             const void* z, int zd, float c, int64_t n) {
+  MT_GRID_STRIDE(i, n) {
+    float v = a * load_as_f32(x, i, xd);
+    if (y) v += b * load_as_f32(y, i, yd);
+    if (z) v += c * load_as_f32(z, i, zd);
+    store_from_f32(out, i, od, v);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Operand packing for the tensor-core paths.  out[b][r][c] = in[b*sb + r*sr + c*sc], written
+// row-major [batch, rows, out_pitch] through a 32x32 shared-memory tile so that both the read
+// (along whichever input axis is unit-stride) and the write are coalesced.  For fp32, `lo`
+// (optional) receives x - tf32_hi(x) (the low half of the 3xTF32 split); `out` (optional)
+// receives x itself.
+template <typename T>
+__global__ void pack2d_kernel(T* out, float* lo, const T* in, int64_t rows, int64_t cols, int64_t sr, int64_t sc,
+                              int64_t sb, int64_t out_pitch) {
+  __shared__ float tile[32][33];
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  const T* src = in + b * sb;
+  const bool read_along_rows = (sr == 1 && sc != 1);
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int i = threadIdx.x;
+    int64_t r, c;
+    if (read_along_rows) { r = r0 + i; c = c0 + j; } else { r = r0 + j; c = c0 + i; }
+    float v = 0.f;
+    if (r < rows && c < cols) v = to_f32<T>(src[r * sr + c * sc]);
+    if (read_along_rows) tile[i][j] = v; else tile[j][i] = v;
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int64_t r = r0 + j, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) {
+      const float v = tile[j][threadIdx.x];
+      const int64_t o = b * rows * out_pitch + r * out_pitch + c;
+      if (out) out[o] = from_f32<T>(v);
+      if (lo) lo[o] = tf32_lo(v);
+    }
+  }
+}
+
+// Conv weight [K, C, R, S] -> [K, R, S, Cp] (zero-filled channels C..Cp), optional tf32 low part.
+template <typename T>
+__global__ void conv_pack_weight_kernel(T* out, float* lo, const T* w, int64_t K, int64_t C, int64_t R, int64_t S,
+                                        int64_t Cp) {
+  const int64_t n = K * R * S * Cp;
+  MT_GRID_STRIDE(i, n) {
+    const int64_t c = i % Cp;
+    int64_t t = i / Cp;
+    const int64_t s = t % S; t /= S;
+    const int64_t r = t % R;
+    const int64_t k = t / R;
+    const float v = c < C ? to_f32<T>(w[((k * C + c) * R + r) * S + s]) : 0.f;
+    if (out) out[i] = from_f32<T>(v);
+    if (lo) lo[i] = tf32_lo(v);
+  }
+}
+
+// im2col for the general convolution path: col[(n*P+p)*Q+q][(r*S+s)*Cp + c] (zero padded in
+// space and channels); x addressed through its own (n, c, h, w) strides.
+template <typename T>
+__global__ void im2col_kernel(T* col, float* lo, const T* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t P,
+                              int64_t Q, int R, int S, int sh, int sw, int ph, int pw, int dh, int dw, int64_t xs0,
+                              int64_t xs1, int64_t xs2, int64_t xs3, int64_t Cp, int64_t Kp) {
+  const int64_t n_total = N * P * Q * Kp;
+  MT_GRID_STRIDE(i, n_total) {
+    const int64_t kk = i % Kp;
+    const int64_t m = i / Kp;
+    float v = 0.f;
+    if (kk < (int64_t)R * S * Cp) {
+      const int64_t c = kk % Cp;
+      const int64_t rs = kk / Cp;
+      const int r = (int)(rs / S), s = (int)(rs % S);
+      const int64_t q = m % Q;
+      const int64_t p = (m / Q) % P;
+      const int64_t nn = m / (P * Q);
+      const int64_t h = p * sh - ph + (int64_t)r * dh;
+      const int64_t w = q * sw - pw + (int64_t)s * dw;
+      if (c < C && h >= 0 && h < H && w >= 0 && w < W) v = to_f32<T>(x[nn * xs0 + c * xs1 + h * xs2 + w * xs3]);
+    }
+    if (col) col[i] = from_f32<T>(v);
+    if (lo) lo[i] = tf32_lo(v);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host launchers.
+int launch_copy_strided(void* dst, int dd, const int64_t* dst_st, const void* src, int sd, const int64_t* src_st,
+                        const int64_t* sizes, int ndim, cudaStream_t st) {
+  if (ndim < 0 || ndim > MT_MAX_DIMS) return fail(MT_ERR_INVALID, "copy_strided: ndim out of range");
+  int64_t n = 1;
+  for (int d = 0; d < ndim; ++d) n *= sizes[d];
+  if (n == 0) return MT_OK;
+  if (dtype_size(dd) == 0 || dtype_size(sd) == 0 || dd > MT_F64 || sd > MT_F64)
+    return fail(MT_ERR_UNSUPPORTED, "copy_strided: dtype");
+  const bool dc = is_contig(dst_st, sizes, ndim), sc = is_contig(src_st, sizes, ndim);
+  if (dc && sc) {
+    if (dd == sd) {
+      const int64_t bytes = n * dtype_size(dd);
+      if (bytes % 16 == 0 && ((uintptr_t)dst % 16 == 0) && ((uintptr_t)src % 16 == 0)) {
+        copy_vec16_kernel<<<grid_for(bytes / 16, 256), 256, 0, st>>>((uint4*)dst, (const uint4*)src, bytes / 16);
+        return check_launch("copy_vec16");
+      }
+      return cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st), "copy");
+    }
+    if (dd == MT_BF16 && sd == MT_F32) {
+      cast_contig_kernel<__nv_bfloat16, float>
+          <<<grid_for(n, 256), 256, 0, st>>>((__nv_bfloat16*)dst, (const float*)src, n);
+      return check_launch("cast");
+    }
+    if (dd == MT_F32 && sd == MT_BF16) {
+      cast_contig_kernel<float, __nv_bfloat16>
+          <<<grid_for(n, 256), 256, 0, st>>>((float*)dst, (const __nv_bfloat16*)src, n);
+      return check_launch("cast");
+    }
+  }
+  StridedND nd{};
+  nd.ndim = ndim;
+  for (int d = 0; d < ndim; ++d) {
+    nd.sizes[d] = sizes[d];
+    nd.s0[d] = dst_st[d];
+    nd.s1[d] = src_st[d];
+  }
+  copy_strided_kernel<<<grid_for(n, 256), 256, 0, st>>>(dst, dd, src, sd, nd, n);
+  return check_launch("copy_strided");
+}
+
+int launch_fill_uniform(void* dst, int dtype, int64_t n, uint64_t state, double from, double to, cudaStream_t st) {
+  if (n <= 0) return MT_OK;
+  fill_uniform_kernel<<<grid_for(n, 256), 256, 0, st>>>(dst, dtype, n, state, from, to - from);
+  return check_launch("fill_uniform");
+}
+int launch_fill(void* dst, int dtype, int64_t n, double value, cudaStream_t st) {
+  if (n <= 0) return MT_OK;
+  fill_kernel<<<grid_for(n, 256), 256, 0, st>>>(dst, dtype, n, value);
+  return check_launch("fill");
+}
+
+int launch_fill_strided_nan(void* dst, int dtype, const int64_t* strides, const int64_t* sizes, cudaStream_t st) {
+  StridedND nd{};
+  nd.ndim = 4;
+  int64_t n = 1;
+  for (int d = 0; d < 4; ++d) {
+    nd.sizes[d] = sizes[d];
+    nd.s0[d] = strides[d];
+    n *= sizes[d];
+  }
+  if (n == 0) return MT_OK;
+  fill_strided_kernel<<<grid_for(n, 256), 256, 0, st>>>(dst, dtype, nd, n, __builtin_nan(""));
+  return check_launch("fill_strided");
+}
+
+int launch_unary(int op, void* y, int yd, const void* x, int xd, int64_t n, cudaStream_t st) {
+  if (n <= 0) return MT_OK;
+  if (yd == MT_BF16 && xd == MT_BF16 && n % 8 == 0 && (uintptr_t)y % 16 == 0 && (uintptr_t)x % 16 == 0) {
+    unary_bf16x8_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>(op, (uint4*)y, (const uint4*)x, n / 8);
+  } else if (yd == MT_F32 && xd == MT_F32) {
+    unary_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(op, (float*)y, (const float*)x, n);
+  } else {
+    unary_generic_kernel<<<grid_for(n, 256), 256, 0, st>>>(op, y, yd, x, xd, n);
+  }
+  return check_launch("unary");
+}
+
+int launch_binary(int op, void* y, int yd, const int64_t* ys, const void* a, int ad, const int64_t* as,
+                  const void* b, int bd, const int64_t* bs, double scalar, const int64_t* sizes, int ndim,
+                  cudaStream_t st) {
+  if (ndim < 0 || ndim > MT_MAX_DIMS) return fail(MT_ERR_INVALID, "binary: ndim out of range");
+  int64_t n = 1;
+  for (int d = 0; d < ndim; ++d) n *= sizes[d];
+  if (n == 0) return MT_OK;
+  if (b && yd == ad && ad == bd && is_contig(ys, sizes, ndim) && is_contig(as, sizes, ndim) &&
+      is_contig(bs, sizes, ndim) && (uintptr_t)y % 16 == 0 && (uintptr_t)a % 16 == 0 && (uintptr_t)b % 16 == 0) {
+    if (yd == MT_F32 && n % 4 == 0) {
+      binary_f32x4_kernel<<<grid_for(n / 4, 256), 256, 0, st>>>(op, (float4*)y, (const float4*)a, (const float4*)b,
+                                                                 n / 4);
+      return check_launch("binary_f32x4");
+    }
+    if (yd == MT_BF16 && n % 8 == 0) {
+      binary_bf16x8_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>(op, (uint4*)y, (const uint4*)a, (const uint4*)b,
+                                                                  n / 8);
+      return check_launch("binary_bf16x8");
+    }
+  }
+  StridedND nd{};
+  nd.ndim = ndim;
+  for (int d = 0; d < ndim; ++d) {
+    nd.sizes[d] = sizes[d];
+    nd.s0[d] = ys[d];
+    nd.s1[d] = as[d];
+    nd.s2[d] = b ? bs[d] : 0;
+  }
+  binary_strided_kernel<<<grid_for(n, 256), 256, 0, st>>>(op, y, yd, a, ad, b, bd, scalar, nd, n);
+  return check_launch("binary");
+}
+
+int launch_axpby(void* out, int od, const void* x, int xd, double a, const void* y, int yd, double b, const void* z,
+                 int zd, double c, int64_t n, cudaStream_t st) {
+  if (n <= 0) return MT_OK;
+  axpby_kernel<<<grid_for(n, 256), 256, 0, st>>>(out, od, x, xd, (float)a, y, yd, (float)b, z, zd, (float)c, n);
+  return check_launch("axpby");
+}
+
+int launch_pack2d(void* out, float* lo, const void* in, int dtype, int64_t batch, int64_t rows, int64_t cols,
+                  int64_t sr, int64_t sc, int64_t sb, int64_t out_pitch, cudaStream_t st) {
+  if (rows == 0 || cols == 0 || batch == 0) return MT_OK;
+  if (batch > 65535 || (rows + 31) / 32 > 65535) return fail(MT_ERR_UNSUPPORTED, "pack2d: grid too large");
+  dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)batch), block(32, 8);
+  switch (dtype) {
+    case MT_F32:
+      pack2d_kernel<float><<<grid, block, 0, st>>>((float*)out, lo, (const float*)in, rows, cols, sr, sc, sb, out_pitch);
+      break;
+    case MT_BF16:
+      pack2d_kernel<__nv_bfloat16><<<grid, block, 0, st>>>((__nv_bfloat16*)out, nullptr, (const __nv_bfloat16*)in,
+                                                            rows, cols, sr, sc, sb, out_pitch);
+      break;
+    case MT_F16:
+      pack2d_kernel<__half><<<grid, block, 0, st>>>((__half*)out, nullptr, (const __half*)in, rows, cols, sr, sc, sb,
+                                                     out_pitch);
+      break;
+    default: return fail(MT_ERR_UNSUPPORTED, "pack2d: dtype");
+  }
+  return check_launch("pack2d");
+}
+
+int launch_conv_pack_weight(void* out, float* lo, const void* w, int dtype, int64_t K, int64_t C, int64_t R,
+                            int64_t S, int64_t Cp, cudaStream_t st) {
+  const int64_t n = K * R * S * Cp;
+  if (n == 0) return MT_OK;
+  switch (dtype) {
+    case MT_F32:
+      conv_pack_weight_kernel<float><<<grid_for(n, 256), 256, 0, st>>>((float*)out, lo, (const float*)w, K, C, R, S, Cp);
+      break;
+    case MT_BF16:
+      conv_pack_weight_kernel<__nv_bfloat16><<<grid_for(n, 256), 256, 0, st>>>(
+          (__nv_bfloat16*)out, nullptr, (const __nv_bfloat16*)w, K, C, R, S, Cp);
+      break;
+    case MT_F16:
+      conv_pack_weight_kernel<__half><<<grid_for(n, 256), 256, 0, st>>>((__half*)out, nullptr, (const __half*)w, K,
+                                                                         C, R, S, Cp);
+      break;
+    default: return fail(MT_ERR_UNSUPPORTED, "conv weight pack: dtype");
+  }
+  return check_launch("conv_pack_weight");
+}
+
+int launch_im2col(void* col, float* lo, const void* x, int dtype, const mt_conv2d_desc& d, int64_t Cp, int64_t Kp,
+                  cudaStream_t st) {
+  const int64_t n = d.N * d.P * d.Q * Kp;
+  if (n == 0) return MT_OK;
+#define MT_IM2COL(T)                                                                                            \
+  im2col_kernel<T><<<grid_for(n, 256), 256, 0, st>>>((T*)col, lo, (const T*)x, d.N, d.C, d.H, d.W, d.P, d.Q,    \
+                                                      (int)d.R, (int)d.S, d.stride_h, d.stride_w, d.pad_h, d.pad_w, \
+                                                      d.dil_h, d.dil_w, d.x_strides[0], d.x_strides[1],         \
+                                                      d.x_strides[2], d.x_strides[3], Cp, Kp)
+  switch (dtype) {
+    case MT_F32: MT_IM2COL(float); break;
+    case MT_BF16: MT_IM2COL(__nv_bfloat16); break;
+    case MT_F16: MT_IM2COL(__half); break;
+    default: return fail(MT_ERR_UNSUPPORTED, "im2col: dtype");
+  }
+#undef MT_IM2COL
+  return check_launch("im2col");
+}
+
+}  // namespace mt

@@ -1,0 +1,851 @@
+// Dense contractions on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// One persistent, warp-specialised kernel serves matmul / bmm / addmm / baddbmm / linear and
+// conv2d (as implicit GEMM):
+//   warp 0      TMA producer: K-major 128-byte-swizzled tiles of A (128 rows x 128 B) and B
+//               (BN rows x 128 B) into a STAGES-deep shared-memory ring (mbarrier full/empty);
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (kind::f16 for bf16/f16, three
+//               kind::tf32 products for fp32) into one of two TMEM accumulators (2 x BN columns);
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane TMEM quarter),
+//               apply alpha / beta*C / bias / activation / residual and store; the TMEM buffer
+//               is then released, so the next tile's MMAs overlap this tile's stores.
+// Convolution: the A tile of output pixels (tn x th x tw = 128) at filter tap (r, s) and channel
+// chunk c is ONE 4-D TMA box over the channels-last activation at coordinates
+// (c, q0 + s*dil - pad, p0 + r*dil - pad, n0); TMA's out-of-bounds zero fill is the padding.
+// No cluster multicast: every CTA loads its own tiles.
+#include <algorithm>
+
+#include "runtime.h"
+
+namespace mt {
+
+MT_STATUS_READER(read_status_gemm)
+
+constexpr int kBM = 128;
+constexpr int kGemmThreads = 192;
+
+struct TileParams {
+  int num_m_tiles, num_n_tiles, batch;
+  int k_iters;
+  int a_batched, b_batched;
+  // implicit convolution
+  int tw, th, tn, tiles_q, tiles_p;
+  int c_chunks, R, S, pad_h, pad_w, dil_h, dil_w;
+  int bk;  // elements per 128-byte K chunk
+};
+
+struct EpiParams {
+  int mode;   // 0 gemm (b, m), 1 conv via im2col (m -> n, p, q), 2 implicit conv (tile coordinates)
+  int64_t M;  // rows (mode 0/1) or images (mode 2)
+  int64_t N;  // GEMM columns (before GEGLU halving)
+  int64_t P, Q;
+  void* D; int out_dtype; int64_t d_s0, d_s1, d_s2;
+  const void* C; int64_t c_s0, c_s1, c_s2; float beta;
+  const void* res; int64_t r_s0, r_s1, r_s2;
+  const void* bias; int bias_dtype; int64_t bias_bstride;
+  float alpha; int act;
+  int vec_ok;  // 16-byte aligned rows of D / C / residual
+};
+
+// 32 consecutive values of one row: load (accumulate scale*x into v) / store, runtime dtype.
+__device__ __forceinline__ void row_load_add(const void* p, int dtype, int64_t off, int nvalid, bool vec, float scale,
+                                             float (&v)[32]) {
+  if (vec && nvalid >= 32) {
+    if (dtype == MT_BF16) {
+      const uint4* q = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p) + off);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 u = q[i];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __bfloat1622float2(h[j]);
+          v[i * 8 + 2 * j] += scale * f.x;
+          v[i * 8 + 2 * j + 1] += scale * f.y;
+        }
+      }
+      return;
+    }
+    if (dtype == MT_F32) {
+      const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + off);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float4 f = q[i];
+        v[4 * i] += scale * f.x;
+        v[4 * i + 1] += scale * f.y;
+        v[4 * i + 2] += scale * f.z;
+        v[4 * i + 3] += scale * f.w;
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nvalid) v[j] += scale * load_as_f32(p, off + j, dtype);
+}
+
+__device__ __forceinline__ void row_store(void* p, int dtype, int64_t off, int nvalid, bool vec, const float (&v)[32]) {
+  if (vec && nvalid >= 32) {
+    if (dtype == MT_BF16) {
+      uint4* q = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p) + off);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        q[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                          pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+      return;
+    }
+    if (dtype == MT_F16) {
+      uint4* q = reinterpret_cast<uint4*>(static_cast<__half*>(p) + off);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        q[i] = make_uint4(pack_f16x2(v[8 * i], v[8 * i + 1]), pack_f16x2(v[8 * i + 2], v[8 * i + 3]),
+                          pack_f16x2(v[8 * i + 4], v[8 * i + 5]), pack_f16x2(v[8 * i + 6], v[8 * i + 7]));
+      return;
+    }
+    if (dtype == MT_F32) {
+      float4* q = reinterpret_cast<float4*>(static_cast<float*>(p) + off);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nvalid) store_from_f32(p, off + j, dtype, v[j]);
+}
+
+__device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b, int& mt, int& nt) {
+  nt = t % tp.num_n_tiles;
+  const int rest = t / tp.num_n_tiles;
+  mt = rest % tp.num_m_tiles;
+  b = rest / tp.num_m_tiles;
+}
+
+template <int BN, bool TF32>
+struct GemmCfg {
+  static constexpr int A_BYTES = kBM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int OPS = TF32 ? 2 : 1;
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * OPS;
+  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
+  static constexpr int TMEM_COLS = (2 * BN <= 32)    ? 32
+                                   : (2 * BN <= 64)  ? 64
+                                   : (2 * BN <= 128) ? 128
+                                   : (2 * BN <= 256) ? 256
+                                                     : 512;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, bool TF32, bool CONV>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmAlo, const __grid_constant__ CUtensorMap tmBlo,
+                      const TileParams tp, const EpiParams ep, const uint32_t idesc) {
+  using Cfg = GemmCfg<BN, TF32>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (TF32) {
+      tma_prefetch_desc(&tmAlo);
+      tma_prefetch_desc(&tmBlo);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_tiles = tp.num_m_tiles * tp.num_n_tiles * tp.batch;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+        int b, mt, nt;
+        decode_tile(tp, t, b, mt, nt);
+        const int n0 = nt * BN;
+        int q0 = 0, p0 = 0, i0 = 0;
+        if (CONV) {
+          q0 = (mt % tp.tiles_q) * tp.tw;
+          p0 = ((mt / tp.tiles_q) % tp.tiles_p) * tp.th;
+          i0 = (mt / (tp.tiles_q * tp.tiles_p)) * tp.tn;
+        }
+        for (int kk = 0; kk < tp.k_iters; ++kk) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, 1, abort_flag)) break;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          uint8_t* salo = sb + Cfg::B_BYTES;
+          uint8_t* sblo = salo + Cfg::A_BYTES;
+          if (CONV) {
+            const int rs = kk / tp.c_chunks, cc = kk - rs * tp.c_chunks;
+            const int r = rs / tp.S, s = rs - r * tp.S;
+            const int cx = cc * tp.bk, wx = q0 + s * tp.dil_w - tp.pad_w, hy = p0 + r * tp.dil_h - tp.pad_h;
+            tma_load_4d(sa, &tmA, &full[stage], cx, wx, hy, i0);
+            tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, 0);
+            if (TF32) {
+              tma_load_4d(salo, &tmAlo, &full[stage], cx, wx, hy, i0);
+              tma_load_3d(sblo, &tmBlo, &full[stage], kk * tp.bk, n0, 0);
+            }
+          } else {
+            const int ab = tp.a_batched ? b : 0, bb = tp.b_batched ? b : 0;
+            tma_load_3d(sa, &tmA, &full[stage], kk * tp.bk, mt * kBM, ab);
+            tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, bb);
+            if (TF32) {
+              tma_load_3d(salo, &tmAlo, &full[stage], kk * tp.bk, mt * kBM, ab);
+              tma_load_3d(sblo, &tmBlo, &full[stage], kk * tp.bk, n0, bb);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t tph = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1, 2, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kk = 0; kk < tp.k_iters; ++kk) {
+          if (!mbar_wait(&full[stage], phase, 3, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+          const uint32_t alo_addr = b_addr + Cfg::B_BYTES;
+          const uint32_t blo_addr = alo_addr + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = sdesc_sw128(a_addr + k * 32), bd = sdesc_sw128(b_addr + k * 32);
+            const uint32_t acc = (kk > 0 || k > 0) ? 1u : 0u;
+            if (TF32) {
+              umma_tf32(d_tmem, ad, bd, idesc, acc);
+              umma_tf32(d_tmem, ad, sdesc_sw128(blo_addr + k * 32), idesc, 1u);
+              umma_tf32(d_tmem, sdesc_sw128(alo_addr + k * 32), bd, idesc, 1u);
+            } else {
+              umma_f16(d_tmem, ad, bd, idesc, acc);
+            }
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        umma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const bool geglu = ep.act == MT_EPI_GEGLU;
+    const int64_t n_out = geglu ? ep.N / 2 : ep.N;
+    int local = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t tph = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[buf], tph, 4, abort_flag)) break;
+      tc_fence_after();
+      int b, mt, nt;
+      decode_tile(tp, t, b, mt, nt);
+      // Map this thread's accumulator row to output coordinates (i0, i1, i2).
+      int64_t i0 = 0, i1 = 0, i2 = 0;
+      bool valid;
+      if (ep.mode == 0) {
+        i0 = b;
+        i1 = (int64_t)mt * kBM + row;
+        valid = i1 < ep.M;
+      } else if (ep.mode == 1) {
+        const int64_t m = (int64_t)mt * kBM + row;
+        valid = m < ep.M;
+        i0 = m / (ep.P * ep.Q);
+        const int64_t rem = m - i0 * ep.P * ep.Q;
+        i1 = rem / ep.Q;
+        i2 = rem - i1 * ep.Q;
+      } else {
+        const int q0 = (mt % tp.tiles_q) * tp.tw;
+        const int p0 = ((mt / tp.tiles_q) % tp.tiles_p) * tp.th;
+        const int n0 = (mt / (tp.tiles_q * tp.tiles_p)) * tp.tn;
+        const int tn_i = row / (tp.th * tp.tw), th_i = (row / tp.tw) % tp.th, tw_i = row % tp.tw;
+        i0 = n0 + tn_i;
+        i1 = p0 + th_i;
+        i2 = q0 + tw_i;
+        valid = i0 < ep.M && i1 < ep.P && i2 < ep.Q;
+      }
+      const int64_t offD = i0 * ep.d_s0 + i1 * ep.d_s1 + i2 * ep.d_s2;
+      const int64_t offC = i0 * ep.c_s0 + i1 * ep.c_s1 + i2 * ep.c_s2;
+      const int64_t offR = i0 * ep.r_s0 + i1 * ep.r_s1 + i2 * ep.r_s2;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+      const bool vec = ep.vec_ok != 0;
+      if (!geglu) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c0, r);
+          tmem_ld_wait();
+          const int64_t col0 = (int64_t)nt * BN + c0;
+          const int64_t remain = n_out - col0;
+          const int nvalid = remain < 32 ? (int)remain : 32;
+          if (valid && nvalid > 0) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
+            if (ep.bias) row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, false, 1.f, v);
+            if (ep.C) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
+            if (ep.act == MT_EPI_GELU) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = gelu_f(v[j]);
+            } else if (ep.act == MT_EPI_SILU) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+            }
+            if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
+            row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
+          }
+        }
+      } else {
+        // (value, gate) 64-column groups: tile columns [g*128, g*128+64) are values, the next
+        // 64 their gates; output column = nt*BN/2 + g*64 + j.
+#pragma unroll 1
+        for (int g = 0; g < BN / 128; ++g) {
+#pragma unroll 1
+          for (int h = 0; h < 64; h += 32) {
+            uint32_t rv[32], rg[32];
+            tmem_ld32(taddr + g * 128 + h, rv);
+            tmem_ld32(taddr + g * 128 + 64 + h, rg);
+            tmem_ld_wait();
+            const int64_t gcol_v = (int64_t)nt * BN + g * 128 + h;
+            const int64_t col0 = (int64_t)nt * (BN / 2) + g * 64 + h;
+            const int64_t remain = n_out - col0;
+            const int nvalid = remain < 32 ? (int)remain : 32;
+            if (valid && nvalid > 0) {
+              float v[32], gt[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                v[j] = ep.alpha * __uint_as_float(rv[j]);
+                gt[j] = ep.alpha * __uint_as_float(rg[j]);
+              }
+              if (ep.bias) {
+                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v, nvalid, false, 1.f, v);
+                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v + 64, nvalid, false, 1.f, gt);
+              }
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = v[j] * gelu_f(gt[j]);
+              if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
+              row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host side.
+
+struct GemmLaunch {
+  CUtensorMap a, b, alo, blo;
+  TileParams tp;
+  EpiParams ep;
+  int kind;  // MT_BF16 / MT_F16 / MT_F32 (tf32 x3)
+  int bn;
+  bool conv;
+};
+
+template <int BN, bool TF32, bool CONV>
+static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
+  using Cfg = GemmCfg<BN, TF32>;
+  auto kern = gemm_sm100_kernel<BN, TF32, CONV>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES),
+                        "gemm smem attribute");
+    if (rc) return rc;
+    attr_set[dev & 63] = true;
+  }
+  const int64_t tiles = (int64_t)L.tp.num_m_tiles * L.tp.num_n_tiles * L.tp.batch;
+  if (tiles > 0x7fffffffLL) return fail(MT_ERR_UNSUPPORTED, "gemm: too many tiles");
+  const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  const int fmt = L.kind == MT_BF16 ? 1 : L.kind == MT_F16 ? 0 : 2;
+  const uint32_t idesc = make_idesc(fmt, kBM, BN);
+  kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, st>>>(L.a, L.b, L.alo, L.blo, L.tp, L.ep, idesc);
+  return check_launch("gemm_sm100");
+}
+
+static int dispatch(const GemmLaunch& L, cudaStream_t st) {
+  if (L.kind == MT_F32) {
+    if (L.conv) return launch_variant<128, true, true>(L, st);
+    if (L.bn == 64) return launch_variant<64, true, false>(L, st);
+    return launch_variant<128, true, false>(L, st);
+  }
+  if (L.conv) {
+    switch (L.bn) {
+      case 64: return launch_variant<64, false, true>(L, st);
+      case 128: return launch_variant<128, false, true>(L, st);
+      case 160: return launch_variant<160, false, true>(L, st);
+      default: return launch_variant<256, false, true>(L, st);
+    }
+  }
+  switch (L.bn) {
+    case 64: return launch_variant<64, false, false>(L, st);
+    case 128: return launch_variant<128, false, false>(L, st);
+    case 160: return launch_variant<160, false, false>(L, st);
+    default: return launch_variant<256, false, false>(L, st);
+  }
+}
+
+// Column-tile width: the widest of {256, 160, 128, 64} that divides N (GEGLU needs a multiple
+// of 128); otherwise the one with the least padding.  fp32 (two operand pairs per stage) and
+// implicit conv with fp32 use 128.
+static int pick_bn(int64_t N, int kind, bool geglu, bool conv) {
+  if (kind == MT_F32) return (N <= 64 && !geglu && !conv) ? 64 : 128;
+  if (geglu) return N % 256 == 0 ? 256 : 128;
+  const int cands[4] = {256, 160, 128, 64};
+  for (int c : cands)
+    if (N % c == 0) return c;
+  if (N <= 64) return 64;
+  int best = 256;
+  int64_t best_pad = INT64_MAX;
+  for (int c : cands) {
+    const int64_t pad = (N + c - 1) / c * c - N;
+    if (pad < best_pad) {
+      best_pad = pad;
+      best = c;
+    }
+  }
+  return best;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// 3-D K-major map: dims {K, rows, batch}, 128-byte-wide box of `box_rows` rows.
+static int map_kmajor(CUtensorMap* m, int dtype, const void* base, int64_t K, int64_t rows, int64_t batch,
+                      int64_t pitch, int64_t bstride, int box_rows) {
+  const int es = dtype_size(dtype);
+  uint64_t dims[3] = {(uint64_t)K, (uint64_t)rows, (uint64_t)std::max<int64_t>(batch, 1)};
+  uint64_t strides[2] = {(uint64_t)(pitch * es), (uint64_t)((batch > 1 ? bstride : rows * pitch) * es)};
+  uint32_t box[3] = {(uint32_t)(128 / es), (uint32_t)box_rows, 1};
+  return make_tensor_map(m, dtype, 3, base, dims, strides, box, 128);
+}
+
+struct WsCursor {
+  char* base;
+  size_t off;
+  void* take(size_t bytes) {
+    off = align_up(off, 256);
+    void* p = base ? base + off : nullptr;
+    off += bytes;
+    return p;
+  }
+};
+
+// Operand plan for a GEMM; with `run == false` it only measures the workspace.
+struct GemmPlan {
+  const void* A; int64_t lda, sa; bool a_batched;
+  const void* B; int64_t ldb, sb; bool b_batched;
+  const void* Alo; const void* Blo;
+  int64_t Kp;
+};
+
+static int plan_gemm(const mt_gemm_desc& d, WsCursor& ws, GemmPlan& p, cudaStream_t st, bool run) {
+  const int es = dtype_size(d.dtype);
+  const int64_t align_elems = 16 / es;
+  p.Kp = (d.K + align_elems - 1) / align_elems * align_elems;
+  const bool tf32 = d.dtype == MT_F32;
+  // A: want [M, K] K-major with a 16-byte aligned pitch.
+  const bool a_ok = !d.a_trans && aligned16(d.A) && (d.lda * es) % 16 == 0 &&
+                    (d.batch == 1 || d.stride_a == 0 || (d.stride_a * es) % 16 == 0);
+  p.a_batched = d.batch > 1 && d.stride_a != 0;
+  const int64_t a_b = p.a_batched ? d.batch : 1;
+  const int64_t asr = d.a_trans ? 1 : d.lda, asc = d.a_trans ? d.lda : 1;
+  if (a_ok) {
+    p.A = d.A; p.lda = d.lda; p.sa = d.stride_a;
+  } else {
+    void* dst = ws.take((size_t)a_b * d.M * p.Kp * es);
+    p.A = dst; p.lda = p.Kp; p.sa = d.M * p.Kp;
+    if (run) {
+      int rc = launch_pack2d(dst, nullptr, d.A, d.dtype, a_b, d.M, d.K, asr, asc, d.stride_a, p.Kp, st);
+      if (rc) return rc;
+    }
+  }
+  p.Alo = nullptr;
+  if (tf32) {
+    if (d.A_lo) {
+      p.Alo = d.A_lo;
+    } else {
+      void* lo = ws.take((size_t)a_b * d.M * p.Kp * 4);
+      p.Alo = lo;
+      if (run) {
+        int rc = launch_pack2d(nullptr, (float*)lo, d.A, d.dtype, a_b, d.M, d.K, asr, asc, d.stride_a, p.Kp, st);
+        if (rc) return rc;
+      }
+    }
+  }
+  // B: want [N, K] K-major.
+  const bool b_ok = d.b_trans && aligned16(d.B) && (d.ldb * es) % 16 == 0 &&
+                    (d.batch == 1 || d.stride_b == 0 || (d.stride_b * es) % 16 == 0);
+  p.b_batched = d.batch > 1 && d.stride_b != 0;
+  const int64_t b_b = p.b_batched ? d.batch : 1;
+  const int64_t bsr = d.b_trans ? d.ldb : 1, bsc = d.b_trans ? 1 : d.ldb;
+  if (b_ok) {
+    p.B = d.B; p.ldb = d.ldb; p.sb = d.stride_b;
+  } else {
+    void* dst = ws.take((size_t)b_b * d.N * p.Kp * es);
+    p.B = dst; p.ldb = p.Kp; p.sb = d.N * p.Kp;
+    if (run) {
+      int rc = launch_pack2d(dst, nullptr, d.B, d.dtype, b_b, d.N, d.K, bsr, bsc, d.stride_b, p.Kp, st);
+      if (rc) return rc;
+    }
+  }
+  p.Blo = nullptr;
+  if (tf32) {
+    if (d.B_lo) {
+      p.Blo = d.B_lo;
+    } else {
+      void* lo = ws.take((size_t)b_b * d.N * p.Kp * 4);
+      p.Blo = lo;
+      if (run) {
+        int rc = launch_pack2d(nullptr, (float*)lo, d.B, d.dtype, b_b, d.N, d.K, bsr, bsc, d.stride_b, p.Kp, st);
+        if (rc) return rc;
+      }
+    }
+  }
+  return MT_OK;
+}
+
+static int validate_gemm(const mt_gemm_desc& d) {
+  if (d.M < 0 || d.N < 0 || d.K < 0 || d.batch < 1) return fail(MT_ERR_INVALID, "gemm: negative size");
+  if (d.dtype != MT_F32 && d.dtype != MT_BF16 && d.dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "gemm: input dtype %d", d.dtype);
+  if (d.out_dtype != MT_F32 && d.out_dtype != MT_BF16 && d.out_dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "gemm: output dtype %d", d.out_dtype);
+  if (d.epilogue < MT_EPI_NONE || d.epilogue > MT_EPI_GEGLU) return fail(MT_ERR_UNSUPPORTED, "gemm: epilogue");
+  if (d.epilogue == MT_EPI_GEGLU && d.N % 128 != 0)
+    return fail(MT_ERR_INVALID, "gemm: GEGLU needs N %% 128 == 0 (interleaved 64-column groups)");
+  if (d.M > 0 && d.N > 0 && d.K == 0) return fail(MT_ERR_UNSUPPORTED, "gemm: K == 0 (caller fills)");
+  if (d.M > 0 && d.N > 0 && (!d.A || !d.B || !d.D)) return fail(MT_ERR_INVALID, "gemm: null operand");
+  if (d.M > INT32_MAX || d.N > INT32_MAX || d.K > INT32_MAX) return fail(MT_ERR_UNSUPPORTED, "gemm: size");
+  return MT_OK;
+}
+
+size_t gemm_workspace(const mt_gemm_desc& d) {
+  if (validate_gemm(d) != MT_OK) return 0;
+  WsCursor ws{nullptr, 0};
+  GemmPlan p;
+  plan_gemm(d, ws, p, nullptr, false);
+  return ws.off;
+}
+
+int run_gemm(const mt_gemm_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st) {
+  int rc = validate_gemm(d);
+  if (rc) return rc;
+  if (d.M == 0 || d.N == 0) return MT_OK;
+  const size_t need = gemm_workspace(d);
+  if (need > 0 && (!wsp || ws_bytes < need)) return fail(MT_ERR_WORKSPACE, "gemm: workspace of %zu bytes required", need);
+  WsCursor ws{(char*)wsp, 0};
+  GemmPlan p;
+  rc = plan_gemm(d, ws, p, st, true);
+  if (rc) return rc;
+
+  GemmLaunch L{};
+  L.kind = d.dtype;
+  L.conv = false;
+  const bool geglu = d.epilogue == MT_EPI_GEGLU;
+  L.bn = pick_bn(d.N, d.dtype, geglu, false);
+  const int64_t a_b = p.a_batched ? d.batch : 1, b_b = p.b_batched ? d.batch : 1;
+  rc = map_kmajor(&L.a, d.dtype, p.A, d.K, d.M, a_b, p.lda, p.sa, kBM);
+  if (!rc) rc = map_kmajor(&L.b, d.dtype, p.B, d.K, d.N, b_b, p.ldb, p.sb, L.bn);
+  if (!rc && d.dtype == MT_F32) {
+    rc = map_kmajor(&L.alo, MT_F32, p.Alo, d.K, d.M, a_b, p.Kp, d.M * p.Kp, kBM);
+    if (!rc) rc = map_kmajor(&L.blo, MT_F32, p.Blo, d.K, d.N, b_b, p.Kp, d.N * p.Kp, L.bn);
+  } else {
+    L.alo = L.a;
+    L.blo = L.b;
+  }
+  if (rc) return rc;
+  TileParams& tp = L.tp;
+  tp.num_m_tiles = (int)((d.M + kBM - 1) / kBM);
+  tp.num_n_tiles = (int)((d.N + L.bn - 1) / L.bn);
+  tp.batch = (int)d.batch;
+  tp.bk = 128 / dtype_size(d.dtype);
+  tp.k_iters = (int)((d.K + tp.bk - 1) / tp.bk);
+  tp.a_batched = p.a_batched;
+  tp.b_batched = p.b_batched;
+  EpiParams& ep = L.ep;
+  ep.mode = 0;
+  ep.M = d.M;
+  ep.N = d.N;
+  ep.D = d.D; ep.out_dtype = d.out_dtype; ep.d_s0 = d.stride_d; ep.d_s1 = d.ldd; ep.d_s2 = 0;
+  ep.C = (d.beta != 0.f) ? d.C : nullptr; ep.c_s0 = d.stride_c; ep.c_s1 = d.ldc; ep.c_s2 = 0; ep.beta = d.beta;
+  ep.res = d.residual; ep.r_s0 = d.stride_r; ep.r_s1 = d.ldr; ep.r_s2 = 0;
+  ep.bias = d.bias; ep.bias_dtype = d.bias_dtype; ep.bias_bstride = d.bias_batch_stride;
+  ep.alpha = d.alpha; ep.act = d.epilogue;
+  const int oes = dtype_size(d.out_dtype);
+  bool vec = aligned16(d.D) && (d.ldd * oes) % 16 == 0 && (d.batch == 1 || (d.stride_d * oes) % 16 == 0);
+  if (ep.C) vec = vec && aligned16(d.C) && (d.ldc * oes) % 16 == 0 && (d.batch == 1 || (d.stride_c * oes) % 16 == 0);
+  if (ep.res)
+    vec = vec && aligned16(d.residual) && (d.ldr * oes) % 16 == 0 && (d.batch == 1 || (d.stride_r * oes) % 16 == 0);
+  ep.vec_ok = vec;
+  return dispatch(L, st);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Convolution.
+
+static bool conv_implicit_ok(const mt_conv2d_desc& d) {
+  const int bk = 128 / dtype_size(d.dtype);
+  return d.stride_h == 1 && d.stride_w == 1 && d.C % bk == 0 && d.groups == 1;
+}
+
+int64_t conv_packed_channels(int64_t C, int64_t R, int64_t S, int dtype) {
+  const int es = dtype_size(dtype);
+  if (es == 0) return C;
+  const int64_t a = 16 / es;
+  return (C + a - 1) / a * a;
+}
+
+static bool is_channels_last(const int64_t* s, int64_t C, int64_t H, int64_t W) {
+  return s[1] == 1 && s[3] == C && s[2] == W * C && s[0] == H * W * C;
+}
+
+static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream_t st, GemmLaunch* L) {
+  const int es = dtype_size(d.dtype);
+  const bool tf32 = d.dtype == MT_F32;
+  const bool implicit = conv_implicit_ok(d);
+  const int64_t Cp = conv_packed_channels(d.C, d.R, d.S, d.dtype);
+  const int64_t Kg = d.R * d.S * Cp;  // GEMM K (16-byte aligned pitch)
+  // Weights -> [K, R, S, Cp].
+  const void* wp = d.w;
+  const void* wlo = d.w_lo;
+  if (!d.w_packed) {
+    void* dst = ws.take((size_t)d.K * Kg * es);
+    void* lo = tf32 ? ws.take((size_t)d.K * Kg * 4) : nullptr;
+    wp = dst;
+    wlo = lo;
+    if (run) {
+      int rc = launch_conv_pack_weight(dst, (float*)lo, d.w, d.dtype, d.K, d.C, d.R, d.S, Cp, st);
+      if (rc) return rc;
+    }
+  } else if (tf32 && !d.w_lo) {
+    void* lo = ws.take((size_t)d.K * Kg * 4);
+    wlo = lo;
+    if (run) {
+      int rc = launch_pack2d(nullptr, (float*)lo, d.w, MT_F32, 1, d.K, Kg, Kg, 1, 0, Kg, st);
+      if (rc) return rc;
+    }
+  }
+  // Output / residual must be channels-last for the epilogue's unit column stride.
+  const bool y_cl = is_channels_last(d.y_strides, d.K, d.P, d.Q) && aligned16(d.y);
+  void* yout = d.y;
+  int64_t ys[4] = {d.y_strides[0], d.y_strides[1], d.y_strides[2], d.y_strides[3]};
+  if (!y_cl) {
+    yout = ws.take((size_t)d.N * d.P * d.Q * d.K * dtype_size(d.out_dtype));
+    ys[0] = d.P * d.Q * d.K; ys[1] = 1; ys[2] = d.Q * d.K; ys[3] = d.K;
+  }
+  const void* res = d.residual;
+  int64_t rs[4] = {d.res_strides[0], d.res_strides[1], d.res_strides[2], d.res_strides[3]};
+  if (res && !is_channels_last(rs, d.K, d.P, d.Q)) {
+    void* dst = ws.take((size_t)d.N * d.P * d.Q * d.K * dtype_size(d.out_dtype));
+    int64_t cl[4] = {d.P * d.Q * d.K, 1, d.Q * d.K, d.K};
+    int64_t sizes[4] = {d.N, d.K, d.P, d.Q};
+    if (run) {
+      int rc = launch_copy_strided(dst, d.out_dtype, cl, d.residual, d.out_dtype, d.res_strides, sizes, 4, st);
+      if (rc) return rc;
+    }
+    res = dst;
+    for (int i = 0; i < 4; ++i) rs[i] = cl[i];
+  }
+  // Activation operand.
+  const void* a = nullptr;
+  const void* alo = nullptr;
+  int64_t M = 0;
+  if (implicit) {
+    const bool x_cl = is_channels_last(d.x_strides, d.C, d.H, d.W) && aligned16(d.x);
+    a = d.x;
+    if (!x_cl) {
+      void* dst = ws.take((size_t)d.N * d.H * d.W * d.C * es);
+      a = dst;
+      if (run) {
+        int64_t cl[4] = {d.H * d.W * d.C, 1, d.W * d.C, d.C};
+        int64_t sizes[4] = {d.N, d.C, d.H, d.W};
+        int rc = launch_copy_strided(dst, d.dtype, cl, d.x, d.dtype, d.x_strides, sizes, 4, st);
+        if (rc) return rc;
+      }
+    }
+    if (tf32) {
+      void* lo = ws.take((size_t)d.N * d.H * d.W * d.C * 4);
+      alo = lo;
+      if (run) {
+        int rc = launch_pack2d(nullptr, (float*)lo, a, MT_F32, 1, d.N * d.H * d.W, d.C, d.C, 1, 0, d.C, st);
+        if (rc) return rc;
+      }
+    }
+  } else {
+    M = d.N * d.P * d.Q;
+    void* col = ws.take((size_t)M * Kg * es);
+    void* lo = tf32 ? ws.take((size_t)M * Kg * 4) : nullptr;
+    a = col;
+    alo = lo;
+    if (run) {
+      int rc = launch_im2col(col, (float*)lo, d.x, d.dtype, d, Cp, Kg, st);
+      if (rc) return rc;
+    }
+  }
+  if (!run) return MT_OK;
+
+  L->kind = d.dtype;
+  L->conv = implicit;
+  L->bn = pick_bn(d.K, d.dtype, false, implicit);
+  TileParams& tp = L->tp;
+  tp.bk = 128 / es;
+  tp.batch = 1;
+  tp.a_batched = tp.b_batched = 0;
+  tp.num_n_tiles = (int)((d.K + L->bn - 1) / L->bn);
+  int rc;
+  if (implicit) {
+    auto pow2_ge = [](int64_t v) {
+      int64_t p = 1;
+      while (p < v) p <<= 1;
+      return p;
+    };
+    const int64_t tw = std::min<int64_t>(128, pow2_ge(d.Q));
+    const int64_t th = std::min<int64_t>(128 / tw, pow2_ge(d.P));
+    const int64_t tn = 128 / (tw * th);
+    tp.tw = (int)tw; tp.th = (int)th; tp.tn = (int)tn;
+    tp.tiles_q = (int)((d.Q + tw - 1) / tw);
+    tp.tiles_p = (int)((d.P + th - 1) / th);
+    const int64_t tiles_n = (d.N + tn - 1) / tn;
+    tp.num_m_tiles = (int)(tiles_n * tp.tiles_q * tp.tiles_p);
+    tp.c_chunks = (int)(d.C / tp.bk);
+    tp.R = (int)d.R; tp.S = (int)d.S;
+    tp.pad_h = d.pad_h; tp.pad_w = d.pad_w; tp.dil_h = d.dil_h; tp.dil_w = d.dil_w;
+    tp.k_iters = (int)(d.R * d.S * tp.c_chunks);
+    uint64_t dims[4] = {(uint64_t)d.C, (uint64_t)d.W, (uint64_t)d.H, (uint64_t)d.N};
+    uint64_t strides[3] = {(uint64_t)(d.C * es), (uint64_t)(d.W * d.C * es), (uint64_t)(d.H * d.W * d.C * es)};
+    uint32_t box[4] = {(uint32_t)tp.bk, (uint32_t)tw, (uint32_t)th, (uint32_t)tn};
+    rc = make_tensor_map(&L->a, d.dtype, 4, a, dims, strides, box, 128);
+    if (!rc && tf32) rc = make_tensor_map(&L->alo, MT_F32, 4, alo, dims, strides, box, 128);
+  } else {
+    tp.num_m_tiles = (int)((M + kBM - 1) / kBM);
+    tp.k_iters = (int)((Kg + tp.bk - 1) / tp.bk);
+    rc = map_kmajor(&L->a, d.dtype, a, Kg, M, 1, Kg, 0, kBM);
+    if (!rc && tf32) rc = map_kmajor(&L->alo, MT_F32, alo, Kg, M, 1, Kg, 0, kBM);
+  }
+  if (!rc) rc = map_kmajor(&L->b, d.dtype, wp, Kg, d.K, 1, Kg, 0, L->bn);
+  if (!rc && tf32) rc = map_kmajor(&L->blo, MT_F32, wlo, Kg, d.K, 1, Kg, 0, L->bn);
+  if (rc) return rc;
+  if (!tf32) {
+    L->alo = L->a;
+    L->blo = L->b;
+  }
+
+  EpiParams& ep = L->ep;
+  ep.mode = implicit ? 2 : 1;
+  ep.M = implicit ? d.N : M;
+  ep.N = d.K;
+  ep.P = d.P; ep.Q = d.Q;
+  ep.D = yout; ep.out_dtype = d.out_dtype; ep.d_s0 = ys[0]; ep.d_s1 = ys[2]; ep.d_s2 = ys[3];
+  ep.C = nullptr; ep.beta = 0.f;
+  ep.res = res; ep.r_s0 = rs[0]; ep.r_s1 = rs[2]; ep.r_s2 = rs[3];
+  ep.bias = d.bias; ep.bias_dtype = d.bias_dtype; ep.bias_bstride = d.bias_batch_stride;
+  ep.alpha = 1.f; ep.act = d.epilogue;
+  const int oes = dtype_size(d.out_dtype);
+  ep.vec_ok = aligned16(yout) && (d.K * oes) % 16 == 0 && (!res || aligned16(res));
+  return MT_OK;
+}
+
+static int validate_conv(const mt_conv2d_desc& d) {
+  if (d.N < 0 || d.C <= 0 || d.H <= 0 || d.W <= 0 || d.K <= 0 || d.R <= 0 || d.S <= 0)
+    return fail(MT_ERR_INVALID, "conv2d: bad sizes");
+  if (d.stride_h <= 0 || d.stride_w <= 0 || d.dil_h <= 0 || d.dil_w <= 0 || d.pad_h < 0 || d.pad_w < 0)
+    return fail(MT_ERR_INVALID, "conv2d: bad stride / dilation / padding");
+  if (d.groups != 1) return fail(MT_ERR_UNSUPPORTED, "conv2d: groups != 1 is not implemented on the device path");
+  if (d.dtype != MT_F32 && d.dtype != MT_BF16 && d.dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "conv2d: dtype %d", d.dtype);
+  if (d.out_dtype != MT_F32 && d.out_dtype != MT_BF16 && d.out_dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "conv2d: output dtype %d", d.out_dtype);
+  const int64_t P = (d.H + 2 * d.pad_h - d.dil_h * (d.R - 1) - 1) / d.stride_h + 1;
+  const int64_t Q = (d.W + 2 * d.pad_w - d.dil_w * (d.S - 1) - 1) / d.stride_w + 1;
+  if (P != d.P || Q != d.Q) return fail(MT_ERR_INVALID, "conv2d: output size mismatch");
+  if (d.epilogue == MT_EPI_GEGLU) return fail(MT_ERR_UNSUPPORTED, "conv2d: GEGLU epilogue");
+  if (d.N > 0 && (!d.x || !d.w || !d.y)) return fail(MT_ERR_INVALID, "conv2d: null operand");
+  return MT_OK;
+}
+
+size_t conv_workspace(const mt_conv2d_desc& d) {
+  if (validate_conv(d) != MT_OK) return 0;
+  WsCursor ws{nullptr, 0};
+  plan_conv(d, ws, false, nullptr, nullptr);
+  return ws.off;
+}
+
+int run_conv2d(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st) {
+  int rc = validate_conv(d);
+  if (rc) return rc;
+  if (d.N == 0 || d.P <= 0 || d.Q <= 0) return MT_OK;
+  const size_t need = conv_workspace(d);
+  if (need > 0 && (!wsp || ws_bytes < need))
+    return fail(MT_ERR_WORKSPACE, "conv2d: workspace of %zu bytes required", need);
+  WsCursor ws{(char*)wsp, 0};
+  GemmLaunch L{};
+  rc = plan_conv(d, ws, true, st, &L);
+  if (rc) return rc;
+  rc = dispatch(L, st);
+  if (rc) return rc;
+  if (L.ep.D != d.y) {
+    int64_t cl[4] = {d.P * d.Q * d.K, 1, d.Q * d.K, d.K};
+    int64_t sizes[4] = {d.N, d.K, d.P, d.Q};
+    rc = launch_copy_strided(d.y, d.out_dtype, d.y_strides, L.ep.D, d.out_dtype, cl, sizes, 4, st);
+  }
+  return rc;
+}
+
+}  // namespace mt

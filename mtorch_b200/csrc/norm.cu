@@ -1,0 +1,377 @@
+// Row softmax, layer norm and group norm (+ fused SiLU).  HBM-bound; fp32 arithmetic with
+// fp64 combination of group-norm partial sums.
+#include "runtime.h"
+
+namespace mt {
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) t += red[i];
+  return t;
+}
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Softmax over contiguous rows.  Rows of up to NT*PER elements stay in registers (one read,
+// one write); longer rows take three passes.
+template <int NT, int PER>
+__global__ void __launch_bounds__(NT) softmax_kernel(void* y, int yd, const void* x, int xd, int64_t cols, int64_t ld,
+                                                     int log_output) {
+  __shared__ float red[NT / 32];
+  const int64_t base = (int64_t)blockIdx.x * ld;
+  const bool cached = cols <= (int64_t)NT * PER;
+  float vals[PER];
+  float m = -INFINITY;
+  if (cached) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int64_t c = threadIdx.x + (int64_t)i * NT;
+      vals[i] = c < cols ? load_as_f32(x, base + c, xd) : -INFINITY;
+      m = fmaxf(m, vals[i]);
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < cols; c += NT) m = fmaxf(m, load_as_f32(x, base + c, xd));
+  }
+  m = block_max<NT>(m, red);
+  float s = 0.f;
+  if (cached) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int64_t c = threadIdx.x + (int64_t)i * NT;
+      if (c < cols) s += expf(vals[i] - m);
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < cols; c += NT) s += expf(load_as_f32(x, base + c, xd) - m);
+  }
+  s = block_sum<NT>(s, red);
+  const float inv = 1.0f / s, ls = logf(s);
+  if (cached) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int64_t c = threadIdx.x + (int64_t)i * NT;
+      if (c < cols) store_from_f32(y, base + c, yd, log_output ? vals[i] - m - ls : expf(vals[i] - m) * inv);
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < cols; c += NT) {
+      const float v = load_as_f32(x, base + c, xd);
+      store_from_f32(y, base + c, yd, log_output ? v - m - ls : expf(v - m) * inv);
+    }
+  }
+}
+
+int launch_softmax(void* y, int yd, const void* x, int xd, int64_t rows, int64_t cols, int64_t ld, int log_output,
+                   cudaStream_t st) {
+  if (rows == 0 || cols == 0) return MT_OK;
+  if (rows > 0x7fffffffLL) return fail(MT_ERR_UNSUPPORTED, "softmax: too many rows");
+  if (cols <= 1024)
+    softmax_kernel<128, 8><<<(unsigned)rows, 128, 0, st>>>(y, yd, x, xd, cols, ld, log_output);
+  else
+    softmax_kernel<256, 16><<<(unsigned)rows, 256, 0, st>>>(y, yd, x, xd, cols, ld, log_output);
+  return check_launch("softmax");
+}
+
+// ---------------------------------------------------------------------------------------------
+// LayerNorm over the last `cols` elements (two-pass mean / variance in registers).
+template <int NT, int PER>
+__global__ void __launch_bounds__(NT) layer_norm_kernel(void* y, int yd, const void* x, int xd, const void* w,
+                                                        const void* b, int wbd, int64_t cols, float eps) {
+  __shared__ float red[NT / 32];
+  const int64_t base = (int64_t)blockIdx.x * cols;
+  const bool cached = cols <= (int64_t)NT * PER;
+  float vals[PER];
+  float s = 0.f;
+  if (cached) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int64_t c = threadIdx.x + (int64_t)i * NT;
+      vals[i] = c < cols ? load_as_f32(x, base + c, xd) : 0.f;
+      s += vals[i];
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < cols; c += NT) s += load_as_f32(x, base + c, xd);
+  }
+  const float mean = block_sum<NT>(s, red) / (float)cols;
+  float q = 0.f;
+  if (cached) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int64_t c = threadIdx.x + (int64_t)i * NT;
+      if (c < cols) q += (vals[i] - mean) * (vals[i] - mean);
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < cols; c += NT) {
+      const float d = load_as_f32(x, base + c, xd) - mean;
+      q += d * d;
+    }
+  }
+  const float var = block_sum<NT>(q, red) / (float)cols;
+  const float inv = rsqrtf(var + eps);
+  if (cached) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int64_t c = threadIdx.x + (int64_t)i * NT;
+      if (c < cols) {
+        float v = (vals[i] - mean) * inv;
+        if (w) v *= load_as_f32(w, c, wbd);
+        if (b) v += load_as_f32(b, c, wbd);
+        store_from_f32(y, base + c, yd, v);
+      }
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < cols; c += NT) {
+      float v = (load_as_f32(x, base + c, xd) - mean) * inv;
+      if (w) v *= load_as_f32(w, c, wbd);
+      if (b) v += load_as_f32(b, c, wbd);
+      store_from_f32(y, base + c, yd, v);
+    }
+  }
+}
+
+int launch_layer_norm(void* y, int yd, const void* x, int xd, const void* w, const void* b, int wbd, int64_t rows,
+                      int64_t cols, double eps, cudaStream_t st) {
+  if (rows == 0 || cols == 0) return MT_OK;
+  if (rows > 0x7fffffffLL) return fail(MT_ERR_UNSUPPORTED, "layer_norm: too many rows");
+  if (cols <= 512)
+    layer_norm_kernel<64, 8><<<(unsigned)rows, 64, 0, st>>>(y, yd, x, xd, w, b, wbd, cols, (float)eps);
+  else
+    layer_norm_kernel<128, 16><<<(unsigned)rows, 128, 0, st>>>(y, yd, x, xd, w, b, wbd, cols, (float)eps);
+  return check_launch("layer_norm");
+}
+
+// ---------------------------------------------------------------------------------------------
+// GroupNorm: (1) per-(image, chunk) partial sums per group, (2) per-(image, group) mean / rstd
+// combined in double in a fixed order, (3) normalise + affine (+ SiLU).  The chunking depends
+// only on the per-image problem, never on N, so an image's result is the same whatever the batch
+// size or its position in the batch.
+//
+// Channels-last input ([N, HW, C] with C contiguous): a CTA walks a chunk of 64 pixels; each
+// (pixel lane, channel) slot is owned by one thread; per-group sums are formed in shared memory.
+// NCHW input ([N, C, HW] with HW contiguous): a CTA reduces a 4096-element slice of one group.
+constexpr int kGnThreads = 256;
+constexpr int kGnMaxChunks = 1024;
+
+__global__ void __launch_bounds__(kGnThreads) gn_partial_cl_kernel(const void* x, int xd, int64_t sn, int64_t spix,
+                                                                   int64_t C, int64_t HW, int64_t G, int chunks,
+                                                                   double* part) {
+  extern __shared__ float gn_sh[];  // [2][slots]
+  const int n = blockIdx.y, chunk = blockIdx.x;
+  const int64_t per = (HW + chunks - 1) / chunks;
+  const int64_t p0 = chunk * per, p1 = min(HW, p0 + per);
+  const int64_t lanes = C >= kGnThreads ? 1 : kGnThreads / C;
+  const int64_t slots = lanes * C;
+  for (int64_t t = threadIdx.x; t < slots; t += kGnThreads) {
+    const int64_t lane = t / C, c = t % C;
+    float s = 0.f, q = 0.f;
+    for (int64_t p = p0 + lane; p < p1; p += lanes) {
+      const float v = load_as_f32(x, n * sn + p * spix + c, xd);
+      s += v;
+      q += v * v;
+    }
+    gn_sh[t] = s;
+    gn_sh[slots + t] = q;
+  }
+  __syncthreads();
+  for (int64_t c = threadIdx.x; c < C; c += kGnThreads) {
+    float s = 0.f, q = 0.f;
+    for (int64_t l = 0; l < lanes; ++l) {
+      s += gn_sh[l * C + c];
+      q += gn_sh[slots + l * C + c];
+    }
+    gn_sh[c] = s;
+    gn_sh[slots + c] = q;
+  }
+  __syncthreads();
+  const int64_t Cg = C / G;
+  for (int64_t g = threadIdx.x; g < G; g += kGnThreads) {
+    double s = 0.0, q = 0.0;
+    for (int64_t c = g * Cg; c < (g + 1) * Cg; ++c) {
+      s += gn_sh[c];
+      q += gn_sh[slots + c];
+    }
+    double* o = part + (((int64_t)n * chunks + chunk) * G + g) * 2;
+    o[0] = s;
+    o[1] = q;
+  }
+}
+
+__global__ void __launch_bounds__(kGnThreads) gn_partial_nchw_kernel(const void* x, int xd, int64_t sn, int64_t sc,
+                                                                     int64_t C, int64_t HW, int64_t G, int chunks,
+                                                                     double* part) {
+  __shared__ double red[2][kGnThreads / 32];
+  const int64_t ng = blockIdx.y;  // n * G + g
+  const int64_t n = ng / G, g = ng % G;
+  const int64_t Cg = C / G;
+  const int64_t len = Cg * HW;
+  const int64_t per = (len + chunks - 1) / chunks;
+  const int64_t e0 = blockIdx.x * per, e1 = min(len, e0 + per);
+  float s = 0.f, q = 0.f;
+  for (int64_t e = e0 + threadIdx.x; e < e1; e += kGnThreads) {
+    const int64_t c = g * Cg + e / HW, p = e % HW;
+    const float v = load_as_f32(x, n * sn + c * sc + p, xd);
+    s += v;
+    q += v * v;
+  }
+  double ds = warp_sum_d((double)s), dq = warp_sum_d((double)q);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    red[0][w] = ds;
+    red[1][w] = dq;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double ts = 0, tq = 0;
+    for (int i = 0; i < kGnThreads / 32; ++i) {
+      ts += red[0][i];
+      tq += red[1][i];
+    }
+    double* o = part + ((n * chunks + blockIdx.x) * G + g) * 2;
+    o[0] = ts;
+    o[1] = tq;
+  }
+}
+
+__global__ void gn_finalize_kernel(const double* part, float* stats, int64_t N, int64_t G, int chunks, double count,
+                                   double eps) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= N * G) return;
+  const int64_t n = i / G, g = i % G;
+  double s = 0, q = 0;
+  for (int c = 0; c < chunks; ++c) {
+    const double* p = part + ((n * chunks + c) * G + g) * 2;
+    s += p[0];
+    q += p[1];
+  }
+  const double mean = s / count;
+  double var = q / count - mean * mean;
+  if (var < 0) var = 0;
+  stats[i * 2] = (float)mean;
+  stats[i * 2 + 1] = (float)(1.0 / sqrt(var + eps));
+}
+
+// Channels-last bf16 apply: 8 channels per thread (16-byte loads / stores).
+__global__ void gn_apply_cl_bf16x8_kernel(__nv_bfloat16* y, const __nv_bfloat16* x, const float* stats,
+                                          const void* w, const void* b, int wbd, int64_t N, int64_t HW, int64_t C,
+                                          int64_t G, int silu) {
+  const int64_t C8 = C / 8, Cg = C / G;
+  const int64_t total = N * HW * C8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c0 = (i % C8) * 8;
+    const int64_t n = i / (HW * C8);
+    uint4 v = reinterpret_cast<const uint4*>(x)[i];
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      float o[2] = {f.x, f.y};
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int64_t c = c0 + 2 * j + k;
+        const float* stt = stats + (n * G + c / Cg) * 2;
+        float r = (o[k] - stt[0]) * stt[1];
+        if (w) r *= load_as_f32(w, c, wbd);
+        if (b) r += load_as_f32(b, c, wbd);
+        if (silu) r = silu_f(r);
+        o[k] = r;
+      }
+      h[j] = __floats2bfloat162_rn(o[0], o[1]);
+    }
+    reinterpret_cast<uint4*>(y)[i] = v;
+  }
+}
+
+// Generic apply: logical [N, C, HW] with separate x / y strides.
+__global__ void gn_apply_generic_kernel(void* y, int yd, int64_t ys0, int64_t ys1, int64_t ys2, const void* x, int xd,
+                                        int64_t xs0, int64_t xs1, int64_t xs2, const float* stats, const void* w,
+                                        const void* b, int wbd, int64_t N, int64_t C, int64_t HW, int64_t G, int silu,
+                                        int channels_inner) {
+  const int64_t total = N * C * HW, Cg = C / G;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t n, c, p;
+    if (channels_inner) {
+      c = i % C; p = (i / C) % HW; n = i / (C * HW);
+    } else {
+      p = i % HW; c = (i / HW) % C; n = i / (C * HW);
+    }
+    const float* stt = stats + (n * G + c / Cg) * 2;
+    float v = (load_as_f32(x, n * xs0 + c * xs1 + p * xs2, xd) - stt[0]) * stt[1];
+    if (w) v *= load_as_f32(w, c, wbd);
+    if (b) v += load_as_f32(b, c, wbd);
+    if (silu) v = silu_f(v);
+    store_from_f32(y, n * ys0 + c * ys1 + p * ys2, yd, v);
+  }
+}
+
+static int gn_chunks(int64_t C, int64_t HW, int64_t G, bool cl) {
+  int64_t chunks = cl ? (HW + 63) / 64 : (C / G * HW + 4095) / 4096;
+  if (chunks < 1) chunks = 1;
+  if (chunks > kGnMaxChunks) chunks = kGnMaxChunks;
+  return (int)chunks;
+}
+
+size_t group_norm_workspace(int64_t N, int64_t C, int64_t HW, int64_t G) {
+  return align_up((size_t)N * kGnMaxChunks * G * 2 * sizeof(double), 256) + (size_t)N * G * 2 * sizeof(float);
+}
+
+int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd, const int64_t* xs, const void* w,
+                      const void* b, int wbd, int64_t N, int64_t C, int64_t HW, int64_t G, double eps, int silu,
+                      void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (G <= 0 || C % G != 0)
+    return fail(MT_ERR_INVALID, "group_norm: channels %lld not divisible by groups %lld", (long long)C, (long long)G);
+  if (N == 0 || C == 0 || HW == 0) return MT_OK;
+  if (!ws || ws_bytes < group_norm_workspace(N, C, HW, G)) return fail(MT_ERR_WORKSPACE, "group_norm: workspace");
+  const bool cl = (xs[1] == 1 && xs[2] == C) && HW > 1;
+  const bool nchw = (xs[2] == 1 && xs[1] == HW) || (HW == 1 && xs[1] == 1);
+  if (!cl && !nchw) return fail(MT_ERR_UNSUPPORTED, "group_norm: input must be NCHW-contiguous or channels-last");
+  if (N > 65535 || (!cl && N * G > 65535)) return fail(MT_ERR_UNSUPPORTED, "group_norm: batch too large");
+  double* part = (double*)ws;
+  float* stats = (float*)((char*)ws + align_up((size_t)N * kGnMaxChunks * G * 2 * sizeof(double), 256));
+  const int chunks = gn_chunks(C, HW, G, cl);
+  if (cl) {
+    const int64_t slots = C >= kGnThreads ? C : (kGnThreads / C) * C;
+    if (2 * slots * sizeof(float) > 48 * 1024) return fail(MT_ERR_UNSUPPORTED, "group_norm: too many channels");
+    gn_partial_cl_kernel<<<dim3(chunks, (unsigned)N), kGnThreads, 2 * slots * sizeof(float), st>>>(
+        x, xd, xs[0], xs[2], C, HW, G, chunks, part);
+  } else {
+    gn_partial_nchw_kernel<<<dim3(chunks, (unsigned)(N * G)), kGnThreads, 0, st>>>(x, xd, xs[0], xs[1], C, HW, G,
+                                                                                  chunks, part);
+  }
+  int rc = check_launch("group_norm partial");
+  if (rc) return rc;
+  gn_finalize_kernel<<<(unsigned)((N * G + 127) / 128), 128, 0, st>>>(part, stats, N, G, chunks,
+                                                                      (double)(C / G) * (double)HW, eps);
+  rc = check_launch("group_norm finalize");
+  if (rc) return rc;
+  const bool ycl = (ys[1] == 1 && ys[2] == C && ys[0] == HW * C);
+  const int64_t total = N * C * HW;
+  if (cl && ycl && xs[0] == HW * C && xd == MT_BF16 && yd == MT_BF16 && C % 8 == 0 && (uintptr_t)x % 16 == 0 &&
+      (uintptr_t)y % 16 == 0) {
+    const int64_t blocks = std::min<int64_t>((total / 8 + 255) / 256, (int64_t)num_sms() * 16);
+    gn_apply_cl_bf16x8_kernel<<<(unsigned)blocks, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, stats, w,
+                                                                b, wbd, N, HW, C, G, silu);
+  } else {
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
+    gn_apply_generic_kernel<<<(unsigned)blocks, 256, 0, st>>>(y, yd, ys[0], ys[1], ys[2], x, xd, xs[0], xs[1], xs[2],
+                                                             stats, w, b, wbd, N, C, HW, G, silu, cl ? 1 : 0);
+  }
+  return check_launch("group_norm apply");
+}
+
+}  // namespace mt
