@@ -1,0 +1,80 @@
+"""mtorch_b200 — the B200 (sm_100a) `cuda` backend for mtorch's Stable-Diffusion hot path.
+
+The public names mirror mtorch's torch-shaped API (mtorch/__init__.py) for the device path:
+``Tensor.to('cuda')``, ``nn.Linear/Conv2d/GroupNorm/LayerNorm``, ``nn.functional.*``
+(``scaled_dot_product_attention``, ``conv2d``, ``linear``, ``group_norm``, ``layer_norm``,
+``softmax``, ``silu``, ``gelu``), ``matmul/bmm/addmm/baddbmm``, ``manual_seed/randn/rand`` (bit-
+compatible with mtorch's generator) and ``cuda.*``.  All device compute runs in
+``libmtorch_cuda.so`` (hand-written sm_100a kernels behind the C ABI of include/mtorch_cuda.h).
+"""
+from __future__ import annotations
+
+import contextlib
+
+from . import _lib
+from .tensor import (Size, Tensor, add, bfloat16, bool_, device, div, double, dtype, empty, empty_like, float,
+                     float16, float32, float64, from_numpy, full, half, int32, int64, long, mul, ones, sub, tensor,
+                     zeros, zeros_like)
+from .random import Generator, default_generator, initial_seed, manual_seed, rand, randn, randn_like
+from .ops import (addmm, baddbmm, bmm, cat, conv2d, gelu, group_norm, layer_norm, linear, log_softmax, matmul, mm,
+                  scaled_dot_product_attention, silu, softmax)
+from . import nn
+
+channels_last = "channels_last"
+contiguous_format = "contiguous_format"
+
+
+@contextlib.contextmanager
+def no_grad():
+    yield
+
+
+@contextlib.contextmanager
+def inference_mode(mode=True):
+    yield
+
+
+def is_grad_enabled():
+    return False
+
+
+class _Cuda:
+    """``mtorch.cuda`` — real device queries (the reference's stubs return False / 0)."""
+
+    @staticmethod
+    def is_available() -> bool:
+        try:
+            return _lib.lib().mt_cuda_device_count() > 0
+        except (ImportError, OSError):
+            return False
+
+    @staticmethod
+    def device_count() -> int:
+        try:
+            return _lib.lib().mt_cuda_device_count()
+        except (ImportError, OSError):
+            return 0
+
+    @staticmethod
+    def synchronize(device=None):
+        _lib.check(_lib.lib().mt_cuda_synchronize(None), "synchronize")
+        _lib.check(_lib.lib().mt_cuda_device_status(1), "device status")
+
+    @staticmethod
+    def is_bf16_supported() -> bool:
+        return _Cuda.is_available()
+
+    @staticmethod
+    def manual_seed(seed):
+        return None
+
+    @staticmethod
+    def current_device() -> int:
+        from .tensor import _t
+
+        return _t().cuda.current_device()
+
+
+cuda = _Cuda()
+
+__all__ = [n for n in dir() if not n.startswith("_")]

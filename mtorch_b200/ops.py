@@ -1,0 +1,522 @@
+"""Device op functions: the `cuda` branch of the reference's hot-path ops.
+
+Each function validates arguments the way the reference does (same error types), computes
+strides / broadcast metadata on the host and calls exactly one C-ABI entry point of
+``libmtorch_cuda.so`` (plus metadata-only views).  CPU tensors raise NotImplementedError:
+compute on the host is mtorch's own CPU backend, never a silent fallback here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+from . import _lib as L
+from .tensor import (Tensor, _new, _require_cuda, _broadcast_shape, bfloat16, float16, float32, to_dtype, workspace,
+                     _contig_strides)
+
+
+def _lib():
+    return L.lib()
+
+
+def _same_dtype(*ts, what):
+    d = ts[0].dtype
+    for t in ts[1:]:
+        if t is not None and t.dtype is not d:
+            raise RuntimeError(f"{what}: expected all tensors to have the same dtype, got {d.name} and {t.dtype.name}")
+    if not d.is_floating_point or d.name == "float64":
+        raise NotImplementedError(f"{what}: dtype {d.name} is not supported on the cuda device")
+
+
+# ---------------------------------------------------------------------------------------------
+# GEMM family: matmul / bmm / addmm / baddbmm / linear (tensor.cpp:24896-25694, 31401-31694)
+
+
+def _mat_layout(t: Tensor):
+    """(ptr-owner tensor, leading dim, trans) for a 2-D [R, C] view, copying if neither axis is
+    unit-stride."""
+    sr, sc = t._strides[-2], t._strides[-1]
+    R, Cc = t._shape[-2], t._shape[-1]
+    if sc == 1 or Cc == 1:
+        return t, max(sr, Cc) if R > 1 else max(Cc, 1), 0
+    if sr == 1 or R == 1:
+        return t, max(sc, R), 1
+    t = t.contiguous()
+    return t, Cc, 0
+
+
+def gemm(a: Tensor, b: Tensor, *, out: Tensor | None = None, bias: Tensor | None = None, bias_batch_stride=0,
+         residual: Tensor | None = None, C_in: Tensor | None = None, alpha=1.0, beta=0.0, epilogue=L.EPI_NONE,
+         out_dtype=None, a_lo=None, b_lo=None) -> Tensor:
+    """Batched D = alpha * a @ b + beta * C_in + bias (act) + residual.  a: [batch?, M, K],
+    b: [batch?, K, N] (either may be 2-D and is then broadcast); all on one cuda device."""
+    _require_cuda(a, b)
+    batch = max(a._shape[0] if a.dim() == 3 else 1, b._shape[0] if b.dim() == 3 else 1)
+    M, K = a._shape[-2], a._shape[-1]
+    K2, N = b._shape[-2], b._shape[-1]
+    if K != K2:
+        raise RuntimeError(f"mat1 and mat2 shapes cannot be multiplied ({M}x{K} and {K2}x{N})")
+    odt = out_dtype or a.dtype
+    n_out = N // 2 if epilogue == L.EPI_GEGLU else N
+    if out is None:
+        out = _new((batch, M, n_out) if (a.dim() == 3 or b.dim() == 3) else (M, n_out), odt, a.device)
+    if K == 0:
+        out.zero_()
+        if bias is not None:
+            out.add_(bias)
+        return out
+    a_t, lda, at = _mat_layout(a)
+    b_t, ldb, bt_stored = _mat_layout(b)
+    # _mat_layout's trans flag: 0 = [rows, cols] row-major.  For B, [K, N] row-major is b_trans=0;
+    # unit stride along K ([N, K] storage) is b_trans=1.
+    d = L.GemmDesc()
+    d.M, d.N, d.K, d.batch = M, N, K, batch
+    d.dtype, d.out_dtype = a.dtype.code, odt.code
+    d.A, d.lda, d.stride_a, d.a_trans = a_t.data_ptr(), lda, (a_t._strides[0] if a_t.dim() == 3 and a_t._shape[0] > 1 else 0), at
+    d.B, d.ldb, d.stride_b, d.b_trans = b_t.data_ptr(), ldb, (b_t._strides[0] if b_t.dim() == 3 and b_t._shape[0] > 1 else 0), bt_stored
+    d.D, d.ldd = out.data_ptr(), out._strides[-2]
+    d.stride_d = out._strides[0] if out.dim() == 3 else 0
+    if C_in is not None and beta != 0.0:
+        Ce = C_in.expand(out.shape) if C_in.dim() <= out.dim() else C_in
+        if Ce._strides[-1] != 1:
+            Ce = Ce.contiguous()
+        d.C, d.ldc, d.stride_c = Ce.data_ptr(), Ce._strides[-2], (Ce._strides[0] if Ce.dim() == 3 else 0)
+    if bias is not None:
+        bias = bias if bias._strides[-1] == 1 else bias.contiguous()
+        d.bias, d.bias_dtype, d.bias_batch_stride = bias.data_ptr(), bias.dtype.code, bias_batch_stride
+    if residual is not None:
+        r = residual if residual._strides[-1] == 1 else residual.contiguous()
+        d.residual, d.ldr, d.stride_r = r.data_ptr(), r._strides[-2], (r._strides[0] if r.dim() == 3 else 0)
+    d.alpha, d.beta, d.epilogue = float(alpha), float(beta), int(epilogue)
+    if a_lo is not None:
+        d.A_lo = a_lo.data_ptr()
+    if b_lo is not None:
+        d.B_lo = b_lo.data_ptr()
+    lib = _lib()
+    need = lib.mt_cuda_gemm_workspace_size(C.byref(d))
+    ws, wsb = workspace(need, a._idx())
+    L.check(lib.mt_cuda_gemm(C.byref(d), ws, wsb, a._stream()), "gemm")
+    out._mark_modified()
+    return out
+
+
+def matmul(a: Tensor, b: Tensor) -> Tensor:
+    """`matmul` (tensor.cpp:24896-25064): dot / mv / vm / mm / broadcast batched mm."""
+    _require_cuda(a, b)
+    _same_dtype(a, b, what="matmul")
+    if a.dim() == 0 or b.dim() == 0:
+        raise RuntimeError("both arguments to matmul need to be at least 1D")
+    squeeze_m = a.dim() == 1
+    squeeze_n = b.dim() == 1
+    if squeeze_m:
+        a = a.unsqueeze(0)
+    if squeeze_n:
+        b = b.unsqueeze(-1)
+    batch_shape = _broadcast_shape(a._shape[:-2], b._shape[:-2])
+    M, K, N = a._shape[-2], a._shape[-1], b._shape[-1]
+    if not batch_shape:
+        out = gemm(a, b)
+    elif b.dim() == 2 and a.is_contiguous():
+        # fold the batch into M (one large GEMM)
+        out = gemm(a.reshape(-1, K), b).reshape(batch_shape + (M, N))
+    else:
+        nb = math.prod(batch_shape)
+        a3 = _fold_batch(a, batch_shape)
+        b3 = _fold_batch(b, batch_shape)
+        out = gemm(a3, b3).reshape(batch_shape + (M, N))
+    if squeeze_n:
+        out = out.squeeze(-1)
+    if squeeze_m:
+        out = out.squeeze(-2)
+    return out
+
+
+def _fold_batch(t: Tensor, batch_shape) -> Tensor:
+    """[*batch, R, C] (broadcast to batch_shape) -> [nb, R, C] with one batch stride (0 if the
+    tensor is broadcast over the whole batch)."""
+    R, Cc = t._shape[-2], t._shape[-1]
+    nb = math.prod(batch_shape)
+    if t.dim() == 2 or all(s == 1 for s in t._shape[:-2]):
+        t2 = t.reshape(R, Cc) if t.dim() > 2 else t
+        return t2._view((nb, R, Cc), (0,) + t2._strides)
+    e = t.expand(tuple(batch_shape) + (R, Cc))
+    # collapsible batch dims?
+    bs = e._strides[:-2]
+    ok = all(bs[i] == bs[i + 1] * batch_shape[i + 1] for i in range(len(bs) - 1)) and 0 not in bs
+    if ok:
+        return e._view((nb, R, Cc), (bs[-1],) + e._strides[-2:])
+    return e.contiguous().reshape(nb, R, Cc)
+
+
+def mm(a, b):
+    if a.dim() != 2 or b.dim() != 2:
+        raise RuntimeError("mm: expected 2D tensors")
+    return matmul(a, b)
+
+
+def bmm(a: Tensor, b: Tensor) -> Tensor:
+    """`bmm` (tensor.cpp:25066-25182)."""
+    if a.dim() != 3 or b.dim() != 3:
+        raise RuntimeError("batch1 and batch2 must be 3D tensors")
+    if a._shape[0] != b._shape[0]:
+        raise RuntimeError("batch1 and batch2 must have same number of batches")
+    _require_cuda(a, b)
+    _same_dtype(a, b, what="bmm")
+    return gemm(a, b)
+
+
+def addmm(inp: Tensor, m1: Tensor, m2: Tensor, beta=1.0, alpha=1.0) -> Tensor:
+    """`addmm` (tensor.cpp:25184-25366): beta * input + alpha * (m1 @ m2)."""
+    _require_cuda(inp, m1, m2)
+    _same_dtype(m1, m2, inp, what="addmm")
+    M, N = m1._shape[0], m2._shape[1]
+    return gemm(m1, m2, C_in=inp.expand((M, N)), alpha=alpha, beta=beta)
+
+
+def baddbmm(inp: Tensor, b1: Tensor, b2: Tensor, beta=1.0, alpha=1.0) -> Tensor:
+    """`baddbmm` (tensor.cpp:25557-25694)."""
+    _require_cuda(inp, b1, b2)
+    _same_dtype(b1, b2, inp, what="baddbmm")
+    shape = (b1._shape[0], b1._shape[1], b2._shape[2])
+    return gemm(b1, b2, C_in=inp.expand(shape), alpha=alpha, beta=beta)
+
+
+def linear(x: Tensor, w: Tensor, bias: Tensor | None = None, *, epilogue=L.EPI_NONE, residual=None,
+           w_lo=None) -> Tensor:
+    """`linear` (tensor.cpp:31401-31694): y = x @ w^T + bias over any leading dims."""
+    _require_cuda(x, w, bias)
+    _same_dtype(x, w, what="linear")
+    K = x._shape[-1]
+    if w._shape[-1] != K:
+        raise RuntimeError(f"mat1 and mat2 shapes cannot be multiplied ({math.prod(x._shape[:-1])}x{K} and "
+                           f"{w._shape[1]}x{w._shape[0]})")
+    lead = x._shape[:-1]
+    x2 = x.reshape(-1, K) if x.dim() != 2 else x
+    wt = w.transpose(0, 1)  # [K, N] view over [N, K] storage: unit stride along K -> b_trans
+    res2 = residual.reshape(-1, residual._shape[-1]) if residual is not None else None
+    y = gemm(x2, wt, bias=bias, residual=res2, epilogue=epilogue, b_lo=w_lo)
+    return y.reshape(lead + (y._shape[-1],))
+
+
+# ---------------------------------------------------------------------------------------------
+# conv2d (tensor.cpp:26490-27528)
+
+
+def _pair(v):
+    return (v, v) if isinstance(v, int) else tuple(v)
+
+
+def conv2d(x: Tensor, w: Tensor, bias: Tensor | None = None, stride=1, padding=0, dilation=1, groups=1, *,
+           residual: Tensor | None = None, bias_batch_stride=0, packed=None, epilogue=L.EPI_NONE,
+           out_channels_last=None) -> Tensor:
+    _require_cuda(x, w, bias, residual)
+    _same_dtype(x, w, what="conv2d")
+    unbatched = x.dim() == 3
+    if unbatched:
+        x = x.unsqueeze(0)
+    if x.dim() != 4 or w.dim() != 4:
+        raise RuntimeError("conv2d: expected 3D (unbatched) or 4D (batched) input and 4D weight")
+    N, Cin, H, W = x._shape
+    K, Cg, R, S = w._shape
+    if Cg * groups != Cin:
+        raise RuntimeError(f"Given groups={groups}, weight of size {tuple(w._shape)}, expected input{tuple(x._shape)} "
+                           f"to have {Cg * groups} channels, but got {Cin} channels instead")
+    sh, sw = _pair(stride)
+    dh, dw = _pair(dilation)
+    if isinstance(padding, str):
+        if padding == "valid":
+            ph = pw = 0
+        elif padding == "same":
+            if (sh, sw) != (1, 1):
+                raise ValueError("padding='same' is not supported for strided convolutions")
+            ph, pw = dh * (R - 1) // 2, dw * (S - 1) // 2
+            if (dh * (R - 1)) % 2 or (dw * (S - 1)) % 2:
+                raise NotImplementedError("asymmetric 'same' padding is not supported on the cuda device")
+        else:
+            raise ValueError(f"Invalid padding string '{padding}'")
+    else:
+        ph, pw = _pair(padding)
+    P = (H + 2 * ph - dh * (R - 1) - 1) // sh + 1
+    Q = (W + 2 * pw - dw * (S - 1) - 1) // sw + 1
+    if P <= 0 or Q <= 0:
+        raise RuntimeError("conv2d: output size is too small")
+    cl = x.is_contiguous("channels_last") and not x.is_contiguous() if out_channels_last is None else out_channels_last
+    y = _new((N, K, P, Q), x.dtype, x.device, channels_last=cl)
+    d = L.Conv2dDesc()
+    d.N, d.C, d.H, d.W, d.K, d.R, d.S, d.P, d.Q = N, Cin, H, W, K, R, S, P, Q
+    d.stride_h, d.stride_w, d.pad_h, d.pad_w, d.dil_h, d.dil_w, d.groups = sh, sw, ph, pw, dh, dw, groups
+    d.dtype = d.out_dtype = x.dtype.code
+    d.x = x.data_ptr()
+    d.x_strides[:] = list(x._strides)
+    if packed is not None:
+        d.w, d.w_packed = packed[0].data_ptr(), 1
+        d.w_lo = packed[1].data_ptr() if packed[1] is not None else None
+    else:
+        wc = w.contiguous()
+        d.w, d.w_packed = wc.data_ptr(), 0
+    if bias is not None:
+        bias = bias.contiguous()
+        d.bias, d.bias_dtype, d.bias_batch_stride = bias.data_ptr(), bias.dtype.code, bias_batch_stride
+    if residual is not None:
+        d.residual = residual.data_ptr()
+        d.res_strides[:] = list(residual.expand(y.shape)._strides)
+    d.y = y.data_ptr()
+    d.y_strides[:] = list(y._strides)
+    d.epilogue = int(epilogue)
+    lib = _lib()
+    need = lib.mt_cuda_conv2d_workspace_size(C.byref(d))
+    ws, wsb = workspace(need, x._idx())
+    L.check(lib.mt_cuda_conv2d(C.byref(d), ws, wsb, x._stream()), "conv2d")
+    return y.squeeze(0) if unbatched else y
+
+
+def pack_conv_weight(w: Tensor):
+    """[K, C, R, S] -> ([K, R, S, Cp] packed, tf32 low part or None) for the implicit-GEMM path."""
+    _require_cuda(w)
+    K, Cin, R, S = w._shape
+    Cp = _lib().mt_cuda_conv2d_packed_channels(Cin, R, S, w.dtype.code)
+    wp = _new((K, R * S * Cp), w.dtype, w.device)
+    lo = _new((K, R * S * Cp), float32, w.device) if w.dtype is float32 else None
+    wc = w.contiguous()
+    L.check(_lib().mt_cuda_conv2d_pack_weight(wp.data_ptr(), lo.data_ptr() if lo is not None else None,
+                                              wc.data_ptr(), w.dtype.code, K, Cin, R, S, w._stream()), "pack weight")
+    return wp, lo
+
+
+# ---------------------------------------------------------------------------------------------
+# attention (tensor.cpp:30930-31324)
+
+
+def scaled_dot_product_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None = None, dropout_p=0.0,
+                                 is_causal=False, scale=None, enable_gqa=False) -> Tensor:
+    _require_cuda(q, k, v, attn_mask)
+    if q.dtype is not k.dtype or q.dtype is not v.dtype:
+        raise ValueError("scaled_dot_product_attention query, key, and value must have the same dtype")
+    if not (0.0 <= dropout_p <= 1.0):
+        raise ValueError("scaled_dot_product_attention dropout_p must be between 0 and 1")
+    if dropout_p not in (0.0, 1.0):
+        raise ValueError("scaled_dot_product_attention dropout_p is only supported when it is 0 or 1")
+    if q.dim() < 2:
+        raise ValueError("scaled_dot_product_attention expects query with at least 2 dims")
+    lead = q._shape[:-2]
+    Lq, E = q._shape[-2], q._shape[-1]
+    Sk, Ev = k._shape[-2], v._shape[-1]
+    out = _new(lead + (Lq, Ev), q.dtype, q.device)
+    if dropout_p == 1.0:
+        return out.zero_()
+
+    def as4(t):
+        if t.dim() == 4:
+            return t
+        if t.dim() == 2:
+            return t._view((1, 1) + t._shape, (0, 0) + t._strides)
+        if t.dim() == 3:
+            return t._view((t._shape[0], 1) + t._shape[1:], (t._strides[0], 0) + t._strides[1:])
+        # fold extra leading dims
+        return t.reshape((-1, t._shape[-3]) + t._shape[-2:])
+
+    q4, k4, v4, o4 = as4(q), as4(k), as4(v), as4(out)
+    B, H = q4._shape[0], q4._shape[1]
+    Hkv = k4._shape[1]
+    if k4._shape[0] != B and k4._shape[0] == 1:
+        k4 = k4.expand((B,) + k4._shape[1:])
+        v4 = v4.expand((B,) + v4._shape[1:])
+    if Hkv != H:
+        if not enable_gqa and Hkv != 1:
+            raise ValueError("scaled_dot_product_attention key/value heads must match query heads unless enable_gqa")
+        if H % Hkv:
+            raise ValueError("number of heads in key/value must divide number of heads in query")
+    d = L.SdpaDesc()
+    d.B, d.H, d.Hkv, d.Sq, d.Sk, d.D, d.Dv = B, H, Hkv, Lq, Sk, E, Ev
+    d.dtype = q.dtype.code
+    d.q, d.k, d.v, d.o = q4.data_ptr(), k4.data_ptr(), v4.data_ptr(), o4.data_ptr()
+    d.q_strides[:], d.k_strides[:], d.v_strides[:], d.o_strides[:] = (list(q4._strides), list(k4._strides),
+                                                                      list(v4._strides), list(o4._strides))
+    if attn_mask is not None:
+        m = attn_mask
+        if m.dtype.name == "bool":
+            d.mask_kind = 1
+        else:
+            d.mask_kind = 2
+            d.mask_dtype = m.dtype.code
+        me = m.expand(_broadcast_shape(m._shape, (B, H, Lq, Sk)))
+        if me.dim() != 4:
+            me = me.reshape(B, H, Lq, Sk)
+        d.mask = me.data_ptr()
+        d.mask_strides[:] = list(me._strides)
+    d.causal = 1 if is_causal else 0
+    d.scale = float(scale) if scale is not None else 1.0 / math.sqrt(E)
+    lib = _lib()
+    need = lib.mt_cuda_sdpa_workspace_size(C.byref(d))
+    ws, wsb = workspace(need, q._idx())
+    L.check(lib.mt_cuda_sdpa(C.byref(d), ws, wsb, q._stream()), "scaled_dot_product_attention")
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# softmax / norms / activations
+
+
+def softmax(x: Tensor, dim=-1, dtype=None) -> Tensor:
+    """`softmax` (tensor.cpp:15145-15213)."""
+    _require_cuda(x)
+    odt = to_dtype(dtype) if dtype is not None else x.dtype
+    dim = dim % x.dim()
+    if dim != x.dim() - 1:
+        perm = list(range(x.dim()))
+        perm[dim], perm[-1] = perm[-1], perm[dim]
+        return softmax(x.permute(perm), -1, dtype).permute(perm).contiguous()
+    xc = x.contiguous()
+    out = _new(x._shape, odt, x.device)
+    cols = x._shape[-1] if x.dim() else 1
+    rows = xc.numel() // max(cols, 1)
+    L.check(_lib().mt_cuda_softmax(out.data_ptr(), odt.code, xc.data_ptr(), xc.dtype.code, rows, cols, cols, 0,
+                                   x._stream()), "softmax")
+    return out
+
+
+def log_softmax(x: Tensor, dim=-1, dtype=None) -> Tensor:
+    _require_cuda(x)
+    odt = to_dtype(dtype) if dtype is not None else x.dtype
+    dim = dim % x.dim()
+    if dim != x.dim() - 1:
+        perm = list(range(x.dim()))
+        perm[dim], perm[-1] = perm[-1], perm[dim]
+        return log_softmax(x.permute(perm), -1, dtype).permute(perm).contiguous()
+    xc = x.contiguous()
+    out = _new(x._shape, odt, x.device)
+    cols = x._shape[-1]
+    L.check(_lib().mt_cuda_softmax(out.data_ptr(), odt.code, xc.data_ptr(), xc.dtype.code, xc.numel() // cols, cols,
+                                   cols, 1, x._stream()), "log_softmax")
+    return out
+
+
+def layer_norm(x: Tensor, normalized_shape, weight=None, bias=None, eps=1e-5) -> Tensor:
+    """`layer_norm` (tensor.cpp:17386-17714)."""
+    _require_cuda(x, weight, bias)
+    ns = (normalized_shape,) if isinstance(normalized_shape, int) else tuple(normalized_shape)
+    if tuple(x._shape[-len(ns):]) != ns:
+        raise RuntimeError(f"Given normalized_shape={list(ns)}, expected input with shape [*, {', '.join(map(str, ns))}]")
+    cols = math.prod(ns)
+    xc = x.contiguous()
+    out = _new(x._shape, x.dtype, x.device)
+    wbd = (weight or bias).dtype.code if (weight is not None or bias is not None) else L.MT_F32
+    wp = weight.contiguous().data_ptr() if weight is not None else None
+    bp = bias.contiguous().data_ptr() if bias is not None else None
+    L.check(_lib().mt_cuda_layer_norm(out.data_ptr(), out.dtype.code, xc.data_ptr(), xc.dtype.code, wp, bp, wbd,
+                                      xc.numel() // max(cols, 1), cols, float(eps), x._stream()), "layer_norm")
+    return out
+
+
+def _nchw_view_strides(x: Tensor):
+    """(sn, sc, shw) if the spatial dims of x collapse to one stride, else None."""
+    sp_shape, sp_str = x._shape[2:], x._strides[2:]
+    for i in range(len(sp_shape) - 1):
+        if sp_shape[i + 1] != 1 and sp_str[i] != sp_str[i + 1] * sp_shape[i + 1]:
+            return None
+    shw = sp_str[-1] if sp_shape else 1
+    return (x._strides[0], x._strides[1], shw)
+
+
+def group_norm(x: Tensor, num_groups: int, weight=None, bias=None, eps=1e-5, *, fuse_silu=False) -> Tensor:
+    """`group_norm` (tensor.cpp:18643-18963); `fuse_silu` adds the SD ResNet SiLU."""
+    _require_cuda(x, weight, bias)
+    if x.dim() < 2:
+        raise RuntimeError("group_norm expects input with at least 2 dims")
+    N, Cc = x._shape[0], x._shape[1]
+    if Cc % num_groups:
+        raise RuntimeError(f"Expected number of channels in input to be divisible by num_groups, but got input of "
+                           f"shape {list(x._shape)} and num_groups={num_groups}")
+    HW = math.prod(x._shape[2:])
+    xs = _nchw_view_strides(x)
+    if xs is None or not ((xs[1] == 1 and xs[2] == Cc) or (xs[2] == 1 and xs[1] == HW)):
+        x = x.contiguous()
+        xs = _nchw_view_strides(x)
+    cl = x.dim() == 4 and x.is_contiguous("channels_last") and not x.is_contiguous()
+    out = _new(x._shape, x.dtype, x.device, channels_last=cl)
+    ys = _nchw_view_strides(out)
+    wbd = (weight if weight is not None else bias).dtype.code if (weight is not None or bias is not None) else L.MT_F32
+    lib = _lib()
+    need = lib.mt_cuda_group_norm_workspace_size(N, Cc, HW, num_groups)
+    ws, wsb = workspace(need, x._idx())
+    L.check(lib.mt_cuda_group_norm(out.data_ptr(), out.dtype.code, L.arr64(ys), x.data_ptr(), x.dtype.code,
+                                   L.arr64(xs), weight.data_ptr() if weight is not None else None,
+                                   bias.data_ptr() if bias is not None else None, wbd, N, Cc, HW, num_groups,
+                                   float(eps), 1 if fuse_silu else 0, ws, wsb, x._stream()), "group_norm")
+    return out
+
+
+def _unary(x: Tensor, op: str) -> Tensor:
+    _require_cuda(x)
+    cl = x.dim() == 4 and x.is_contiguous("channels_last")
+    xc = x if (x.is_contiguous() or cl) else x.contiguous()
+    out = _new(x._shape, x.dtype, x.device, channels_last=cl and not x.is_contiguous())
+    L.check(_lib().mt_cuda_unary(L.UNARY[op], out.data_ptr(), out.dtype.code, xc.data_ptr(), xc.dtype.code,
+                                 xc.numel(), x._stream()), op)
+    return out
+
+
+def silu(x: Tensor) -> Tensor:
+    """`silu` (tensor.cpp:16480-16600)."""
+    return _unary(x, "silu")
+
+
+def gelu(x: Tensor, approximate="none") -> Tensor:
+    """`gelu` (tensor.cpp:17207-17290)."""
+    if approximate not in ("none", "tanh"):
+        raise ValueError("gelu approximate must be 'none' or 'tanh'")
+    return _unary(x, "gelu" if approximate == "none" else "gelu_tanh")
+
+
+def sigmoid(x):
+    return _unary(x, "sigmoid")
+
+
+def relu(x):
+    return _unary(x, "relu")
+
+
+def exp(x):
+    return _unary(x, "exp")
+
+
+# ---------------------------------------------------------------------------------------------
+# cat / interpolate (copies through mt_cuda_copy_strided)
+
+
+def _copy_into(dst: Tensor, src: Tensor):
+    L.check(_lib().mt_cuda_copy_strided(dst.data_ptr(), dst.dtype.code, L.arr64(dst._strides), src.data_ptr(),
+                                        src.dtype.code, L.arr64(src._strides), L.arr64(dst._shape), dst.dim(),
+                                        dst._stream()), "copy")
+
+
+def cat(tensors, dim=0) -> Tensor:
+    """`cat` (tensor.cpp:32141)."""
+    ts = [t for t in tensors if not (t.dim() == 1 and t.numel() == 0)]
+    _require_cuda(*ts)
+    ref = ts[0]
+    dim = dim % ref.dim()
+    shape = list(ref._shape)
+    shape[dim] = sum(t._shape[dim] for t in ts)
+    cl = ref.dim() == 4 and all(t.is_contiguous("channels_last") and not t.is_contiguous() for t in ts)
+    out = _new(shape, ref.dtype, ref.device, channels_last=cl)
+    off = 0
+    for t in ts:
+        _copy_into(out.narrow(dim, off, t._shape[dim]), t)
+        off += t._shape[dim]
+    return out
+
+
+def interpolate_nearest2x(x: Tensor) -> Tensor:
+    """Nearest-neighbour 2x upsample of [N, C, H, W] (interpolate, tensor.cpp:10897): a broadcast
+    view [N, C, H, 2, W, 2] copied once into the output (layout follows the input)."""
+    _require_cuda(x)
+    N, Cc, H, W = x._shape
+    cl = x.is_contiguous("channels_last") and not x.is_contiguous()
+    out = _new((N, Cc, 2 * H, 2 * W), x.dtype, x.device, channels_last=cl)
+    sn, sc, sh, sw = x._strides
+    src = x._view((N, Cc, H, 2, W, 2), (sn, sc, sh, 0, sw, 0))
+    on, oc, oh, ow = out._strides
+    dst = out._view((N, Cc, H, 2, W, 2), (on, oc, 2 * oh, oh, 2 * ow, ow))
+    _copy_into(dst, src)
+    return out
