@@ -1,0 +1,284 @@
+"""Device parity: every hot-path op on cuda vs the CPU oracle (the restated reference arithmetic,
+pinned to the reference in test_oracle_pins.py) on the same seeded inputs.
+
+Tolerances: fp32 paths rtol 1e-4 (3xTF32 / fp32 SIMT), bf16 paths
+rtol 2e-2 against the fp32 oracle evaluated on the same bf16-rounded inputs.  Because relative
+error is meaningless for outputs that cancel to ~0, each check also allows an absolute error of
+rtol * max|reference|.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import mtorch_b200 as mt
+
+pytestmark = pytest.mark.gpu
+
+FP32_RTOL = 1e-4
+BF16_RTOL = 2e-2
+
+
+def check(got, ref, rtol):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    np.testing.assert_allclose(got, ref, rtol=rtol, atol=rtol * max(np.abs(ref).max(), 1e-30))
+
+
+def cu(a, dtype=None):
+    t = mt.tensor(np.asarray(a, np.float32))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def bf16_round(a):
+    return mt.tensor(np.asarray(a, np.float32)).to("bfloat16").numpy()
+
+
+def rnd(*shape, seed=0, scale=1.0):
+    return (np.random.default_rng(seed).standard_normal(shape) * scale).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------------------------
+# elementwise / norms
+
+
+def test_binary_broadcast_exact():
+    a, b = rnd(2, 3, 5, 7), rnd(3, 1, 7, seed=1)
+    for op, f in (("add", np.add), ("sub", np.subtract), ("mul", np.multiply), ("div", np.divide)):
+        got = getattr(mt, op)(cu(a), cu(b)).numpy()
+        np.testing.assert_array_equal(got, f(a, b).astype(np.float32))
+    np.testing.assert_array_equal((cu(a) * 2.5).numpy(), a * np.float32(2.5))
+    x = cu(a, "bfloat16")
+    np.testing.assert_array_equal((x + x).numpy(), bf16_round(bf16_round(a) * 2))
+
+
+def test_strided_copy_and_cast():
+    a = rnd(4, 6, 8)
+    t = cu(a)
+    np.testing.assert_array_equal(t.permute(2, 0, 1).contiguous().numpy(), a.transpose(2, 0, 1))
+    np.testing.assert_array_equal(t.to("bfloat16").float().numpy(), bf16_round(a))
+    np.testing.assert_array_equal(mt.cat([t, t[:, :2]], dim=1).numpy(), np.concatenate([a, a[:, :2]], 1))
+    x = cu(rnd(2, 3, 4, 5)).contiguous(memory_format=mt.channels_last)
+    up = mt.nn.functional.interpolate(x, scale_factor=2).numpy()
+    np.testing.assert_array_equal(up, x.numpy().repeat(2, 2).repeat(2, 3))
+
+
+def test_device_uniform_matches_host_generator():
+    mt.manual_seed(7)
+    host = mt.rand(1001).numpy()
+    mt.manual_seed(7)
+    dev = mt.empty(1001, device="cuda").uniform_(0.0, 1.0).numpy()
+    np.testing.assert_array_equal(dev, host)
+    after_dev = mt.rand(3).numpy()
+    mt.manual_seed(7)
+    mt.rand(1001)
+    np.testing.assert_array_equal(after_dev, mt.rand(3).numpy())
+
+
+def test_activations(golden):
+    x = golden["silu.x"]
+    check(mt.silu(cu(x)).numpy(), golden["silu.y"], 1e-5)
+    check(mt.gelu(cu(x)).numpy(), golden["gelu.y"], 1e-5)
+    check(mt.gelu(cu(x), approximate="tanh").numpy(), golden["gelu_tanh.y"], 1e-5)
+    xb = bf16_round(x)
+    check(mt.silu(cu(x, "bfloat16")).numpy(), oracle.silu_f32(xb), BF16_RTOL)
+
+
+def test_softmax_layer_norm_group_norm(golden):
+    check(mt.softmax(cu(golden["softmax.x"]), -1).numpy(), golden["softmax.y"], FP32_RTOL)
+    x = rnd(6, 5000, seed=3)
+    check(mt.softmax(cu(x), -1).numpy(), oracle.softmax_f32(x), FP32_RTOL)
+    check(mt.softmax(cu(x.T.copy()), 0).numpy(), oracle.softmax_f32(x).T, FP32_RTOL)
+    check(mt.layer_norm(cu(golden["layer_norm.x"]), [32], cu(golden["layer_norm.w"]), cu(golden["layer_norm.b"]))
+          .numpy(), golden["layer_norm.y"], FP32_RTOL)
+    x, w, b = rnd(300, 1280, seed=4), rnd(1280, seed=5), rnd(1280, seed=6)
+    check(mt.layer_norm(cu(x), [1280], cu(w), cu(b)).numpy(), oracle.layer_norm_f32(x, w, b), FP32_RTOL)
+    check(mt.group_norm(cu(golden["group_norm.x"]), 4, cu(golden["group_norm.w"]), cu(golden["group_norm.b"]))
+          .numpy(), golden["group_norm.y"], FP32_RTOL)
+
+
+@pytest.mark.parametrize("shape,G", [((2, 320, 16, 16), 32), ((3, 64, 9, 7), 8), ((1, 960, 8, 8), 32)])
+@pytest.mark.parametrize("layout", ["nchw", "channels_last"])
+def test_group_norm_silu(shape, G, layout):
+    x, w, b = rnd(*shape, seed=7, scale=2.0) + 0.5, rnd(shape[1], seed=8), rnd(shape[1], seed=9)
+    ref = oracle.group_norm_f32(x, G, w, b)
+    xt = cu(x)
+    if layout == "channels_last":
+        xt = xt.contiguous(memory_format=mt.channels_last)
+    got = mt.group_norm(xt, G, cu(w), cu(b))
+    check(got.numpy(), ref, FP32_RTOL)
+    fused = mt.nn.GroupNorm(G, shape[1]).cuda()
+    fused.weight.copy_(cu(w))
+    fused.bias.copy_(cu(b))
+    check(fused(xt, fuse_silu=True).numpy(), oracle.silu_f32(ref), FP32_RTOL)
+    xb = bf16_round(x)
+    gb = mt.group_norm(cu(x, "bfloat16").contiguous(memory_format=mt.channels_last), G, cu(w), cu(b), fuse_silu=True)
+    check(gb.numpy(), oracle.silu_f32(oracle.group_norm_f32(xb, G, w, b)), BF16_RTOL)
+
+
+def test_group_norm_batch_independent():
+    """An image's result does not depend on batch size or position (the multi-GPU sharding
+    relies on it): bitwise equal."""
+    x = cu(rnd(4, 320, 16, 16, seed=10), "bfloat16").contiguous(memory_format=mt.channels_last)
+    full = mt.group_norm(x, 32, fuse_silu=True).numpy()
+    part = mt.group_norm(x[2:], 32, fuse_silu=True).numpy()
+    np.testing.assert_array_equal(full[2:], part)
+
+
+# ---------------------------------------------------------------------------------------------
+# GEMM family
+
+
+def test_matmul_fp32_golden(golden):
+    check(mt.matmul(cu(golden["matmul.a"]), cu(golden["matmul.b"])).numpy(), golden["matmul.y"], FP32_RTOL)
+    check(mt.bmm(cu(golden["bmm.a"]), cu(golden["bmm.b"])).numpy(), golden["bmm.y"], FP32_RTOL)
+    check(mt.addmm(cu(golden["addmm.i"]), cu(golden["addmm.a"]), cu(golden["addmm.b"]), beta=0.5, alpha=2.0).numpy(),
+          golden["addmm.y"], FP32_RTOL)
+    check(mt.linear(cu(golden["linear.x"]), cu(golden["linear.w"]), cu(golden["linear.b"])).numpy(),
+          golden["linear.y"], FP32_RTOL)
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 320, 200), (130, 1000, 520), (1, 64, 3), (515, 48, 1280)])
+def test_matmul_fp32_3xtf32(M, K, N):
+    a, b = rnd(M, K, seed=M), rnd(K, N, seed=N)
+    check(mt.matmul(cu(a), cu(b)).numpy(), oracle.matmul_f32(a, b), FP32_RTOL)
+    # transposed views go through the operand packer
+    check(mt.matmul(cu(a.T.copy()).t(), cu(b.T.copy()).t()).numpy(), oracle.matmul_f32(a, b), FP32_RTOL)
+
+
+def test_batched_broadcast_matmul_fp32():
+    a, b = rnd(2, 3, 33, 40), rnd(3, 40, 17, seed=1)
+    ref = np.stack([[oracle.matmul_f32(a[i, j], b[j]) for j in range(3)] for i in range(2)])
+    check(mt.matmul(cu(a), cu(b)).numpy(), ref, FP32_RTOL)
+    check(mt.matmul(cu(a), cu(b[0])).numpy(), np.stack([[oracle.matmul_f32(a[i, j], b[0]) for j in range(3)]
+                                                          for i in range(2)]), FP32_RTOL)
+    v = rnd(40, seed=2)
+    check(mt.matmul(cu(a[0, 0]), cu(v)).numpy(), oracle.matmul_f32(a[0, 0], v[:, None])[:, 0], FP32_RTOL)
+
+
+@pytest.mark.parametrize("M,K,N", [(300, 320, 320), (1000, 320, 640), (257, 640, 1280), (128, 768, 320),
+                                   (64, 320, 4), (4096, 320, 2560)])
+def test_linear_bf16(M, K, N):
+    x, w, b = rnd(M, K, seed=1), rnd(N, K, seed=2, scale=0.05), rnd(N, seed=3)
+    ref = oracle.linear_f32(bf16_round(x), bf16_round(w), bf16_round(b))
+    got = mt.linear(cu(x, "bfloat16"), cu(w, "bfloat16"), cu(b, "bfloat16")).numpy()
+    check(got, ref, BF16_RTOL)
+
+
+def test_linear_bf16_fused_epilogues():
+    from mtorch_b200 import _lib
+    from mtorch_b200.ops import linear
+
+    M, K, F = 500, 320, 1280
+    x, w, b, r = rnd(M, K), rnd(2 * F, K, seed=1, scale=0.05), rnd(2 * F, seed=2), rnd(M, F, seed=3)
+    xb, wb, bb, rb = map(bf16_round, (x, w, b, r))
+    # GEGLU: module order is [value rows; gate rows]; the kernel wants (64 value, 64 gate) groups
+    h = oracle.linear_f32(xb, wb, bb)
+    val, gate = h[:, :F], h[:, F:]
+    ref = val * oracle.gelu_f32(gate) + rb
+    perm = np.concatenate([np.concatenate([np.arange(g, g + 64), F + np.arange(g, g + 64)]) for g in range(0, F, 64)])
+    got = linear(cu(x, "bfloat16"), cu(w[perm], "bfloat16"), cu(b[perm], "bfloat16"), epilogue=_lib.EPI_GEGLU,
+                 residual=cu(r, "bfloat16")).numpy()
+    check(got, ref, BF16_RTOL)
+    got = linear(cu(x, "bfloat16"), cu(w[:F], "bfloat16"), None, epilogue=_lib.EPI_SILU).numpy()
+    check(got, oracle.silu_f32(oracle.linear_f32(xb, wb[:F])), BF16_RTOL)
+
+
+def test_bmm_bf16_attention_shapes():
+    a, b = rnd(16, 256, 40), rnd(16, 40, 256, seed=1)
+    ref = np.stack([oracle.matmul_f32(bf16_round(a[i]), bf16_round(b[i])) for i in range(16)])
+    check(mt.bmm(cu(a, "bfloat16"), cu(b, "bfloat16")).numpy(), ref, BF16_RTOL)
+
+
+def test_linear_batch_independent():
+    x = cu(rnd(3000, 320), "bfloat16")
+    w = cu(rnd(640, 320, seed=1, scale=0.05), "bfloat16")
+    full = mt.linear(x, w).numpy()
+    np.testing.assert_array_equal(full[1500:], mt.linear(x[1500:], w).numpy())
+
+
+# ---------------------------------------------------------------------------------------------
+# conv2d
+
+
+@pytest.mark.parametrize("name", ["conv_p1", "conv_s2", "conv_d2", "conv_1x1"])
+def test_conv2d_fp32_golden(golden, name):
+    s, p, d, g = (int(v) for v in golden[f"{name}.params"])
+    got = mt.conv2d(cu(golden[f"{name}.x"]), cu(golden[f"{name}.w"]), cu(golden[f"{name}.b"]), s, p, d, g).numpy()
+    check(got, golden[f"{name}.y"], FP32_RTOL)
+
+
+@pytest.mark.parametrize("shape,K,k,pad", [((2, 64, 16, 16), 64, 3, 1), ((1, 96, 9, 11), 40, 3, 1),
+                                           ((2, 32, 8, 8), 48, 1, 0)])
+def test_conv2d_fp32_implicit(shape, K, k, pad):
+    x, w, b = rnd(*shape), rnd(K, shape[1], k, k, seed=1, scale=0.1), rnd(K, seed=2)
+    ref = oracle.conv2d_f32(x, w, b, 1, pad)
+    check(mt.conv2d(cu(x), cu(w), cu(b), 1, pad).numpy(), ref, FP32_RTOL)
+    xl = cu(x).contiguous(memory_format=mt.channels_last)
+    y = mt.conv2d(xl, cu(w), cu(b), 1, pad)
+    assert y.is_contiguous(mt.channels_last)
+    check(y.numpy(), ref, FP32_RTOL)
+
+
+@pytest.mark.parametrize("shape,K,k,stride,pad", [((2, 320, 32, 32), 320, 3, 1, 1), ((2, 128, 8, 8), 256, 3, 1, 1),
+                                                  ((1, 640, 16, 16), 1280, 1, 1, 0), ((2, 4, 32, 32), 320, 3, 1, 1),
+                                                  ((2, 320, 16, 16), 320, 3, 2, 1), ((1, 320, 64, 64), 4, 3, 1, 1)])
+def test_conv2d_bf16(shape, K, k, stride, pad):
+    x, w, b = rnd(*shape), rnd(K, shape[1], k, k, seed=1, scale=0.05), rnd(K, seed=2)
+    ref = oracle.conv2d_f32(bf16_round(x), bf16_round(w), bf16_round(b), stride, pad)
+    conv = mt.nn.Conv2d(shape[1], K, k, stride=stride, padding=pad).cuda().to("bfloat16")
+    conv.weight.copy_(cu(w, "bfloat16"))
+    conv.bias.copy_(cu(b, "bfloat16"))
+    xl = cu(x, "bfloat16").contiguous(memory_format=mt.channels_last)
+    check(conv(xl).numpy(), ref, BF16_RTOL)
+
+
+def test_conv2d_bf16_resnet_epilogue():
+    """Per-image bias (conv bias + time embedding) and the residual add fused in the epilogue."""
+    N, C, H = 2, 320, 16
+    x, w, r = rnd(N, C, H, H), rnd(C, C, 3, 3, seed=1, scale=0.05), rnd(N, C, H, H, seed=2)
+    pb = rnd(N, C, seed=3)
+    ref = oracle.conv2d_f32(bf16_round(x), bf16_round(w), None, 1, 1) + pb[:, :, None, None] + bf16_round(r)
+    xl = cu(x, "bfloat16").contiguous(memory_format=mt.channels_last)
+    rl = cu(r, "bfloat16").contiguous(memory_format=mt.channels_last)
+    got = mt.conv2d(xl, cu(w, "bfloat16"), cu(pb), 1, 1, residual=rl, bias_batch_stride=C)
+    check(got.numpy(), ref, BF16_RTOL)
+
+
+# ---------------------------------------------------------------------------------------------
+# attention
+
+
+def test_sdpa_fp32_golden(golden):
+    F = mt.nn.functional
+    q, k, v = (cu(golden[f"sdpa_self.{n}"]) for n in "qkv")
+    check(F.scaled_dot_product_attention(q, k, v).numpy(), golden["sdpa_self.y"], FP32_RTOL)
+    check(F.scaled_dot_product_attention(q, k, v, is_causal=True).numpy(), golden["sdpa_causal.y"], FP32_RTOL)
+    q, k, v = (cu(golden[f"sdpa_cross.{n}"]) for n in "qkv")
+    check(F.scaled_dot_product_attention(q, k, v, scale=0.3).numpy(), golden["sdpa_cross.y"], FP32_RTOL)
+    check(F.scaled_dot_product_attention(q, k, v, attn_mask=cu(golden["sdpa_fmask.m"])).numpy(),
+          golden["sdpa_fmask.y"], FP32_RTOL)
+    bm = mt.tensor(golden["sdpa_bmask.m"].astype(bool)).cuda()
+    check(F.scaled_dot_product_attention(q, k, v, attn_mask=bm).numpy(), golden["sdpa_bmask.y"], FP32_RTOL)
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk,D", [(2, 8, 300, 300, 40), (2, 8, 256, 77, 40), (1, 8, 200, 200, 80),
+                                         (1, 8, 64, 77, 160), (2, 8, 1024, 1024, 40)])
+def test_sdpa_bf16(B, H, Sq, Sk, D):
+    q, k, v = rnd(B, H, Sq, D), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
+    ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
+    got = mt.scaled_dot_product_attention(cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")).numpy()
+    check(got, ref, BF16_RTOL)
+
+
+def test_sdpa_fp32_strided_heads():
+    """Q/K/V as head-split views of [B, S, H*D] projections (no copies)."""
+    B, S, H, D = 2, 100, 8, 40
+    x = rnd(B, S, 3 * H * D)
+    t = cu(x)
+    q, k, v = (t[..., i * H * D:(i + 1) * H * D].reshape(B, S, H, D).transpose(1, 2) for i in range(3))
+    xs = x.reshape(B, S, 3, H, D).transpose(2, 0, 3, 1, 4)
+    ref = oracle.sdpa_f32(xs[0], xs[1], xs[2])
+    check(mt.scaled_dot_product_attention(q, k, v).numpy(), ref, FP32_RTOL)
