@@ -12,9 +12,14 @@ from __future__ import annotations
 import contextlib
 
 from . import _lib
-from .tensor import (Size, Tensor, add, bfloat16, bool_, device, div, double, dtype, empty, empty_like, float,
-                     float16, float32, float64, from_numpy, full, half, int32, int64, long, mul, ones, sub, tensor,
-                     zeros, zeros_like)
+from .tensor import (Size, Tensor, add, bfloat16, bool_, device, div, dtype, empty, empty_like, float16, float32,
+                     float64, from_numpy, full, int32, int64, mul, ones, sub, tensor, zeros, zeros_like)
+
+float = float32  # noqa: A001  (torch-style aliases)
+half = float16
+double = float64
+long = int64
+bool = bool_  # noqa: A001
 from .random import Generator, default_generator, initial_seed, manual_seed, rand, randn, randn_like
 from .ops import (addmm, baddbmm, bmm, cat, conv2d, gelu, group_norm, layer_norm, linear, log_softmax, matmul, mm,
                   scaled_dot_product_attention, silu, softmax)

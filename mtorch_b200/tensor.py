@@ -48,10 +48,6 @@ float64 = dtype("float64", 8, L.MT_F64, np.float64, True)
 int32 = dtype("int32", 4, L.MT_I32, np.int32, False)
 int64 = dtype("int64", 8, L.MT_I64, np.int64, False)
 bool_ = dtype("bool", 1, L.MT_BOOL, np.bool_, False)
-float = float32  # noqa: A001  (torch-style aliases)
-half = float16
-double = float64
-long = int64
 
 _BY_NAME = {d.name: d for d in (float32, bfloat16, float16, float64, int32, int64, bool_)}
 _BY_NAME.update({"float": float32, "half": float16, "double": float64, "long": int64, "int": int32})
