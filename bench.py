@@ -1,0 +1,356 @@
+"""Benchmark: SD-1.5-shaped UNet denoise steps/s.
+
+Workload: bf16 UNet (random init, seed 0) on latents [64, 4, 64, 64] ~ N(0,1) with context
+[64, 77, 768] ~ N(0,1); one "step" = one UNet evaluation of the whole batch + the fused DDIM
+update.  Under torchrun with N ranks the batch is sharded (64/N samples per GPU, strong scaling),
+weights are replicated, and the output latents are all-gathered once over NCCL at the end of the
+timed region.  `value` = steps/s of the whole 64-sample job.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the reference mtorch's own CPU implementation (built from its sources
+into oracle/_ref; the restated C oracle when that is absent) on the host cores, on a bounded
+sample of the same workload, and reports the extrapolated steps/s.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BATCH = 64
+H = W = 64
+CTX = 77
+METRIC = "UNet denoise steps/s (SD-1.5 shape, bf16, batch 64 latents 64x64, context 77x768)"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+
+
+class ClockSampler:
+    def __init__(self, path: Path):
+        self.path = path
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self, gpu_index=None):
+        if not self.path.exists():
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            if gpu_index is not None and f[0] != str(gpu_index):
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline (reference mtorch on the host cores)
+
+
+def _ref_sample_worker(seconds_hint: float = 0.0):
+    """One bounded sample of the workload on the reference CPU implementation: the UNet's level-0
+    3x3 conv 320->320 on a 16x16 patch of one sample, a 320-wide linear over 512 tokens and a
+    self-attention of 8 heads x 256 tokens x 40 (the three op classes that carry 99% of the UNet's
+    FLOPs).  Returns (seconds per class, flops per class, kind)."""
+    import oracle
+
+    m = oracle.ref()
+    kind = "reference" if m is not None else "port"
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((1, 320, 16, 16)).astype(np.float32)
+    w = (rng.standard_normal((320, 320, 3, 3)) * 0.02).astype(np.float32)
+    t = rng.standard_normal((512, 320)).astype(np.float32)
+    lw = (rng.standard_normal((320, 320)) * 0.05).astype(np.float32)
+    q = rng.standard_normal((1, 8, 256, 40)).astype(np.float32)
+    flops = {"conv": 2.0 * 320 * 320 * 9 * 256, "linear": 2.0 * 512 * 320 * 320, "attn": 4.0 * 8 * 256 * 256 * 40}
+    secs = {}
+    if m is not None:
+        F = m.nn.functional
+        mx, mw = m.tensor(x.tolist()), m.tensor(w.tolist())
+        mt_, ml = m.tensor(t.tolist()), m.tensor(lw.tolist())
+        mq = m.tensor(q.tolist())
+        t0 = time.perf_counter(); F.conv2d(mx, mw, None, padding=1); secs["conv"] = time.perf_counter() - t0
+        t0 = time.perf_counter(); F.linear(mt_, ml); secs["linear"] = time.perf_counter() - t0
+        t0 = time.perf_counter(); F.scaled_dot_product_attention(mq, mq, mq); secs["attn"] = time.perf_counter() - t0
+    else:
+        t0 = time.perf_counter(); oracle.conv2d_f32(x, w, None, 1, 1); secs["conv"] = time.perf_counter() - t0
+        t0 = time.perf_counter(); oracle.linear_f32(t, lw); secs["linear"] = time.perf_counter() - t0
+        t0 = time.perf_counter(); oracle.sdpa_f32(q, q, q); secs["attn"] = time.perf_counter() - t0
+    return secs, flops, kind
+
+
+def _step_flop_split():
+    """FLOPs of one C5 step (64 samples) split into conv / linear / attention classes."""
+    from mtorch_b200.unet import unet_flops_per_sample
+
+    cls: dict = {}
+    total = unet_flops_per_sample(classes=cls) * BATCH
+    return {k: v * BATCH for k, v in cls.items()}, total
+
+
+def cpu_baseline(processes: int = 1):
+    """Extrapolated reference-CPU steps/s from one bounded sample per process."""
+    if processes <= 1:
+        secs, flops, kind = _ref_sample_worker()
+        rates = [{k: flops[k] / secs[k] for k in secs}]
+    else:
+        import multiprocessing as mp
+
+        with mp.get_context("spawn").Pool(processes) as pool:
+            res = pool.map(_ref_sample_worker, [0.0] * processes)
+        kind = res[0][2]
+        rates = [{k: r[1][k] / r[0][k] for k in r[0]} for r in res]
+    split, total = _step_flop_split()
+    # aggregate rate of P independent single-threaded processes
+    agg = {k: sum(r[k] for r in rates) for k in rates[0]}
+    sec_per_step = sum(split[k] / agg[k] for k in split)
+    sample = ("reference mtorch portable CPU path: conv2d 1x320x16x16 3x3 (0.47 GFLOP), linear 512x320x320 "
+              "(0.10 GFLOP), sdpa 1x8x256x40 (0.08 GFLOP) per process; UNet step time extrapolated by FLOP class "
+              "(conv / linear / attention FLOP classes of the 51.4 TFLOP step)")
+    return {"value": 1.0 / sec_per_step, "unit": "steps/s", "cores": processes, "kind": kind, "sample": sample,
+            "gflops_per_s": {k: v / 1e9 for k, v in agg.items()}}
+
+
+# ---------------------------------------------------------------------------------------------
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    procs = os.cpu_count() or 1
+    cfg = {"workload": "C5: SD-1.5 UNet, batch 64 latents [64,4,64,64], context [64,77,768], DDIM step",
+           "global_batch": BATCH, "seq_len": H * W, "parallelism": "host cores (independent processes)",
+           "l2": "n/a (CPU)"}
+    for _ in range(args.warmup if args.warmup < 1 else 1):
+        pass
+    times, vals = [], []
+    base = None
+    for _ in range(max(args.steps, 1)):
+        t0 = time.perf_counter()
+        base = cpu_baseline(processes=procs)
+        times.append(time.perf_counter() - t0)
+        vals.append(base["value"])
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {**base, "value": value},
+            "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_ours(args):
+    import torch
+
+    import mtorch_b200 as mt
+    from mtorch_b200 import _lib, ops
+    from mtorch_b200.unet import DDIM, UNet, timestep_embedding, unet_flops_per_sample
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
+    if BATCH % world:
+        raise SystemExit(f"batch {BATCH} does not shard over {world} GPUs")
+    nb = BATCH // world
+    dev = f"cuda:{local}"
+    out_dir = ROOT / "gpurun_out"
+    out_dir.mkdir(exist_ok=True)
+
+    # ---- model and inputs (seeded; every rank builds the same weights) ----
+    mt.manual_seed(0)
+    unet = UNet(device=dev, dtype="bfloat16")
+    mt.manual_seed(1)
+    lat_all = mt.randn(BATCH, 4, H, W)
+    ctx_all = mt.randn(BATCH, CTX, 768)
+    lat_h = lat_all[rank * nb:(rank + 1) * nb].to("bfloat16")
+    ctx_h = ctx_all[rank * nb:(rank + 1) * nb].to("bfloat16")
+    sched = DDIM(steps=50)
+    temb_all = [mt.tensor(timestep_embedding(np.full(nb, float(t))), dtype="bfloat16", device=dev)
+                for t in sched.timesteps]
+    x = lat_h.to(dev)
+    ctx = ctx_h.to(dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i, x):
+        t = sched.timesteps[i % len(sched.timesteps)]
+        eps = unet(x, temb_all[i % len(temb_all)], ctx)
+        return sched.step(x, eps, t)
+
+    for i in range(args.warmup):
+        x = step(i, x)
+    torch.cuda.synchronize()
+    gathered = torch.empty(BATCH * 4 * H * W * 2, dtype=torch.uint8, device=dev)
+
+    # ---- device-timed region ----
+    lib = _lib.lib()
+    clocks = ClockSampler(out_dir / f"clocks_rank{rank}.csv")
+    with clocks:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        n0 = lib.mt_cuda_launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            x = step(args.warmup + i, x)
+        if dist:
+            dist.all_gather_into_tensor(gathered, x.contiguous()._buf[:x.numel() * 2])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        launches = lib.mt_cuda_launch_count() - n0
+    ms = e0.elapsed_time(e1)
+    if dist:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_per_step = ms / args.steps
+    value = 1000.0 / ms_per_step
+
+    # ---- end to end through the public API with host buffers (pinned), every step ----
+    lat_pin = torch.from_numpy(lat_h._buf[:lat_h.numel()].copy()).pin_memory()
+    ctx_pin = torch.from_numpy(ctx_h._buf[:ctx_h.numel()].copy()).pin_memory()
+    out_pin = torch.empty(lat_h.numel(), dtype=torch.int16).pin_memory()
+    xd = mt.empty(nb, 4, H, W, dtype="bfloat16", device=dev)
+    cd = mt.empty(nb, CTX, 768, dtype="bfloat16", device=dev)
+    h2d = (lat_pin.numel() + ctx_pin.numel()) * 2
+    d2h = out_pin.numel() * 2
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for i in range(args.steps):
+        lib.mt_cuda_memcpy(xd.data_ptr(), lat_pin.data_ptr(), h2d - ctx_pin.numel() * 2, 0, stream.cuda_stream)
+        lib.mt_cuda_memcpy(cd.data_ptr(), ctx_pin.data_ptr(), ctx_pin.numel() * 2, 0, stream.cuda_stream)
+        t = sched.timesteps[i % len(sched.timesteps)]
+        eps = unet(xd, temb_all[i % len(temb_all)], cd)
+        y = sched.step(xd, eps, t)
+        lib.mt_cuda_memcpy(out_pin.data_ptr(), y.data_ptr(), d2h, 1, stream.cuda_stream)
+        stream.synchronize()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e2.elapsed_time(e3)
+    if dist:
+        tt = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_e2e = float(tt.item())
+    e2e = {"value": 1000.0 * args.steps / ms_e2e, "unit": "steps/s", "h2d_bytes_per_step": h2d * world,
+           "d2h_bytes_per_step": d2h * world}
+
+    # ---- roofline of the dominant kernel: the implicit-GEMM 3x3 conv (tcgen05) ----
+    hbm, tf_burst, tf_sust, peak_kind = peaks()
+    conv = unet.down[0].conv2  # 320 -> 320, 3x3 at 64x64 (the UNet's most frequent conv shape)
+    xin = mt.empty(nb, 320, H, W, dtype="bfloat16", device=dev).uniform_(-1, 1).contiguous(
+        memory_format=mt.channels_last)
+    for _ in range(3):
+        conv(xin)
+    reps = 10
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    torch.cuda.synchronize()
+    ev[0].record(stream)
+    for _ in range(reps):
+        conv(xin)  # input 168 MB at nb=64 > L2 (126 MB); at small nb L2 may hold it
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    conv_ms = ev[0].elapsed_time(ev[1]) / reps
+    conv_flops = 2.0 * nb * H * W * 320 * 320 * 9
+    achieved = conv_flops / (conv_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": "gemm_sm100_kernel<160,false,true> (conv 3x3 320->320, 64x64, "
+                f"batch {nb})", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
+                "frac": achieved / tf_burst, "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
+                "step_tflops": unet_flops_per_sample() * nb / (ms_per_step * 1e-3) / 1e12}
+
+    if rank == 0:
+        clk = clocks.summary(gpu_index=None)
+        try:
+            base = cpu_baseline(processes=1)
+        except Exception as e:  # noqa: BLE001
+            base = {"value": None, "unit": "steps/s", "cores": 1, "kind": "unavailable", "sample": str(e)[:200]}
+        line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents/context, random-init "
+                "weights)", "config": {"workload": "C5: SD-1.5 UNet bf16, batch 64 latents [64,4,64,64], context "
+                "[64,77,768], 1 UNet eval + DDIM update per step", "model": "SD-1.5-shaped UNet (859.5M params)",
+                "global_batch": BATCH, "seq_len": H * W, "parallelism": f"batch-shard dp{world} + NCCL all-gather",
+                "l2": "activations > L2 (126 MB) at batch 64/GPU; no flush"},
+                "gpu_launches": int(launches), "e2e": e2e, "roofline": roofline, "cpu_baseline": base,
+                "clocks": clk}
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

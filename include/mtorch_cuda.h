@@ -52,6 +52,9 @@ int mt_cuda_synchronize(void* stream);
 /* Device-side error word written by bounded waits inside kernels (MT_ERR_TIMEOUT); `clear`
  * resets it.  Returns MT_OK when no kernel reported a problem. */
 int mt_cuda_device_status(int clear);
+/* Number of kernels this library has launched in the process (all devices); instrumentation for
+ * benchmarks (no counterpart in the reference, which has no device). */
+uint64_t mt_cuda_launch_count(void);
 
 /* ---- memory movement: replaces `to` (tensor.cpp:8479-8505) and `contiguous` (tensor.cpp:8210) */
 /* kind: 0 = host->device, 1 = device->host, 2 = device->device. */
@@ -87,6 +90,12 @@ int mt_cuda_binary(int op, void* y, int y_dtype, const int64_t* y_strides, const
  * update of the reference's scheduler scenario (tests/compat/benchmarking.py:6148-6168). */
 int mt_cuda_axpby(void* out, int out_dtype, const void* x, int x_dtype, double a, const void* y, int y_dtype,
                   double b, const void* z, int z_dtype, double c, int64_t n, void* stream);
+/* One DDIM update of n latents, fp32 math, as the reference's scheduler step
+ * (tests/compat/benchmarking.py:6148-6168): x0 = (x - sqrt(1-a_t) eps) / sqrt(a_t), clamped to
+ * [-1, 1] when clip != 0; eps' = (x - sqrt(a_t) x0) / sqrt(1-a_t);
+ * out = sqrt(a_prev) x0 + sqrt(1-a_prev) eps'.  out may alias x. */
+int mt_cuda_ddim_step(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n, double alpha_t,
+                      double alpha_prev, int clip, void* stream);
 
 /* ---- normalisation / softmax ------------------------------------------------------------- */
 /* Replaces `softmax` (tensor.cpp:15145-15213, fp32 kernel 7508-7742) along the innermost,

@@ -80,7 +80,8 @@ SIGNATURES = {
     "mt_cuda_set_device": (C.c_int, [C.c_int]),
     "mt_cuda_synchronize": (C.c_int, [VP]),
     "mt_cuda_device_status": (C.c_int, [C.c_int]),
-    "mt_cuda_memcpy": (C.c_int, [VP, VP, C.c_size_t, C.c_int, VP]),
+    "mt_cuda_launch_count": (C.c_uint64, []),
+    "mt_cuda_memcpy":(C.c_int, [VP, VP, C.c_size_t, C.c_int, VP]),
     "mt_cuda_memset": (C.c_int, [VP, C.c_int, C.c_size_t, VP]),
     "mt_cuda_copy_strided": (C.c_int, [VP, C.c_int, _P64, VP, C.c_int, _P64, _P64, C.c_int, VP]),
     "mt_cuda_fill_uniform": (C.c_int, [VP, C.c_int, I64, C.c_uint64, C.c_double, C.c_double, VP]),
@@ -90,7 +91,8 @@ SIGNATURES = {
                                  _P64, C.c_int, VP]),
     "mt_cuda_axpby": (C.c_int, [VP, C.c_int, VP, C.c_int, C.c_double, VP, C.c_int, C.c_double, VP, C.c_int,
                                 C.c_double, I64, VP]),
-    "mt_cuda_softmax": (C.c_int, [VP, C.c_int, VP, C.c_int, I64, I64, I64, C.c_int, VP]),
+    "mt_cuda_ddim_step": (C.c_int, [VP, VP, VP, C.c_int, C.c_int, I64, C.c_double, C.c_double, C.c_int, VP]),
+    "mt_cuda_softmax":(C.c_int, [VP, C.c_int, VP, C.c_int, I64, I64, I64, C.c_int, VP]),
     "mt_cuda_layer_norm": (C.c_int, [VP, C.c_int, VP, C.c_int, VP, VP, C.c_int, I64, I64, C.c_double, VP]),
     "mt_cuda_group_norm_workspace_size": (C.c_size_t, [I64, I64, I64, I64]),
     "mt_cuda_group_norm": (C.c_int, [VP, C.c_int, _P64, VP, C.c_int, _P64, VP, VP, C.c_int, I64, I64, I64, I64,

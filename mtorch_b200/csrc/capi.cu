@@ -1,5 +1,6 @@
 // The extern "C" boundary (include/mtorch_cuda.h): argument checks, error strings, device
 // management, TMA tensor-map encoding, and the host random generator.
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -30,7 +31,12 @@ int cuda_check(cudaError_t e, const char* what) {
   return fail(MT_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
 }
 
-int check_launch(const char* what) { return cuda_check(cudaGetLastError(), what); }
+static std::atomic<uint64_t> g_launches{0};
+
+int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cuda_check(cudaGetLastError(), what);
+}
 
 struct DevProps {
   int sms = 0;
@@ -133,6 +139,8 @@ int mt_cuda_device_status(int clear) {
   return MT_OK;
 }
 
+uint64_t mt_cuda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
 int mt_cuda_memcpy(void* dst, const void* src, size_t bytes, int kind, void* stream) {
   if (bytes == 0) return MT_OK;
   if (!dst || !src) return fail(MT_ERR_INVALID, "memcpy: null pointer");
@@ -174,6 +182,13 @@ int mt_cuda_binary(int op, void* y, int y_dtype, const int64_t* y_strides, const
 int mt_cuda_axpby(void* out, int out_dtype, const void* x, int x_dtype, double a, const void* y, int y_dtype, double b,
                   const void* z, int z_dtype, double c, int64_t n, void* stream) {
   return launch_axpby(out, out_dtype, x, x_dtype, a, y, y_dtype, b, z, z_dtype, c, n, S(stream));
+}
+
+int mt_cuda_ddim_step(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n, double alpha_t,
+                      double alpha_prev, int clip, void* stream) {
+  if (!(alpha_t > 0.0 && alpha_t < 1.0) || !(alpha_prev > 0.0 && alpha_prev <= 1.0))
+    return fail(MT_ERR_INVALID, "ddim_step: alphas must lie in (0, 1)");
+  return launch_ddim_step(out, x, eps, dtype, eps_dtype, n, alpha_t, alpha_prev, clip, S(stream));
 }
 
 int mt_cuda_softmax(void* y, int y_dtype, const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ld,

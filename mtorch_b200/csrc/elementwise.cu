@@ -389,6 +389,26 @@ int launch_axpby(void* out, int od, const void* x, int xd, double a, const void*
   return check_launch("axpby");
 }
 
+__global__ void ddim_step_kernel(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n,
+                                 float sa, float sb, float sap, float sbp, int clip) {
+  MT_GRID_STRIDE(i, n) {
+    const float xv = load_as_f32(x, i, dtype), ev = load_as_f32(eps, i, eps_dtype);
+    float x0 = (xv - sb * ev) / sa;
+    if (clip) x0 = fminf(fmaxf(x0, -1.0f), 1.0f);
+    const float e2 = (xv - sa * x0) / sb;
+    store_from_f32(out, i, dtype, sap * x0 + sbp * e2);
+  }
+}
+
+int launch_ddim_step(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n, double a_t,
+                     double a_prev, int clip, cudaStream_t st) {
+  if (n <= 0) return MT_OK;
+  ddim_step_kernel<<<grid_for(n, 256), 256, 0, st>>>(out, x, eps, dtype, eps_dtype, n, (float)sqrt(a_t),
+                                                     (float)sqrt(1.0 - a_t), (float)sqrt(a_prev),
+                                                     (float)sqrt(1.0 - a_prev), clip);
+  return check_launch("ddim_step");
+}
+
 int launch_pack2d(void* out, float* lo, const void* in, int dtype, int64_t batch, int64_t rows, int64_t cols,
                   int64_t sr, int64_t sc, int64_t sb, int64_t out_pitch, cudaStream_t st) {
   if (rows == 0 || cols == 0 || batch == 0) return MT_OK;

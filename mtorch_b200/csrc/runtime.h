@@ -49,6 +49,8 @@ int launch_binary(int op, void* y, int yd, const int64_t* ys, const void* a, int
                   cudaStream_t st);
 int launch_axpby(void* out, int od, const void* x, int xd, double a, const void* y, int yd, double b, const void* z,
                  int zd, double c, int64_t n, cudaStream_t st);
+int launch_ddim_step(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n, double a_t,
+                     double a_prev, int clip, cudaStream_t st);
 int launch_pack2d(void* out, float* lo, const void* in, int dtype, int64_t batch, int64_t rows, int64_t cols,
                   int64_t sr, int64_t sc, int64_t sb, int64_t out_pitch, cudaStream_t st);
 int launch_conv_pack_weight(void* out, float* lo, const void* w, int dtype, int64_t K, int64_t C, int64_t R,

@@ -288,7 +288,10 @@ def pack_conv_weight(w: Tensor):
 
 
 def scaled_dot_product_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None = None, dropout_p=0.0,
-                                 is_causal=False, scale=None, enable_gqa=False) -> Tensor:
+                                 is_causal=False, scale=None, enable_gqa=False, *, out: Tensor | None = None) -> Tensor:
+    """`scaled_dot_product_attention` (tensor.cpp:30930-31324).  `out` (optional) may be any
+    strided view of the right shape, e.g. a heads-merged [B, S, H, D] buffer seen as
+    [B, H, S, D], so the next projection reads it without a copy."""
     _require_cuda(q, k, v, attn_mask)
     if q.dtype is not k.dtype or q.dtype is not v.dtype:
         raise ValueError("scaled_dot_product_attention query, key, and value must have the same dtype")
@@ -301,7 +304,10 @@ def scaled_dot_product_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Ten
     lead = q._shape[:-2]
     Lq, E = q._shape[-2], q._shape[-1]
     Sk, Ev = k._shape[-2], v._shape[-1]
-    out = _new(lead + (Lq, Ev), q.dtype, q.device)
+    if out is None:
+        out = _new(lead + (Lq, Ev), q.dtype, q.device)
+    elif tuple(out.shape) != lead + (Lq, Ev):
+        raise RuntimeError(f"sdpa: out has shape {tuple(out.shape)}, expected {lead + (Lq, Ev)}")
     if dropout_p == 1.0:
         return out.zero_()
 
@@ -519,4 +525,17 @@ def interpolate_nearest2x(x: Tensor) -> Tensor:
     on, oc, oh, ow = out._strides
     dst = out._view((N, Cc, H, 2, W, 2), (on, oc, 2 * oh, oh, 2 * ow, ow))
     _copy_into(dst, src)
+    return out
+
+
+def ddim_step(x: Tensor, eps: Tensor, alpha_t: float, alpha_prev: float, clip=True, out: Tensor | None = None):
+    """One DDIM latent update (the reference's scheduler scenario, tests/compat/benchmarking.py:
+    6148-6168) as a single fused kernel."""
+    _require_cuda(x, eps)
+    xc, ec = x.contiguous(), eps.contiguous()
+    if out is None:
+        out = _new(x._shape, x.dtype, x.device)
+    L.check(_lib().mt_cuda_ddim_step(out.data_ptr(), xc.data_ptr(), ec.data_ptr(), x.dtype.code, ec.dtype.code,
+                                     x.numel(), float(alpha_t), float(alpha_prev), 1 if clip else 0, x._stream()),
+            "ddim_step")
     return out

@@ -1,0 +1,361 @@
+"""SD-1.5-shaped UNet denoiser and DDIM loop on the device path.
+
+The reference has no UNet model: its Stable-Diffusion workload is a set of scenario functions
+composed from public ops (tests/compat/benchmarking.py, e.g. the MiniUNet pipeline at 6879-6920
+and 7245-7263, the ResNet / attention / GEGLU / DDIM scenarios).  This module composes the same
+ops at SD-1.5 shapes: channel multipliers 320/640/1280/1280, 2 ResNet blocks per level, spatial
+transformers (self-attention, cross-attention to a 768-d context, GEGLU FFN) at the first three
+levels, 8 heads, timestep embedding 320 -> 1280.
+
+Layout: activations stay channels-last ([N, C, H, W] with C innermost), so the token view of a
+feature map ([N*H*W, C]) is free and convolutions run as implicit GEMM.  Fusions (each one
+kernel): GroupNorm+SiLU; conv1 + (conv bias + time-embedding projection) as a per-image bias;
+conv2 + shortcut residual; attention-out / FF-out / proj-out projections + residual; GEGLU
+(value * gelu(gate)) in the FF-in GEMM epilogue; QKV as one GEMM with attention reading strided
+head views; attention writing heads-merged output; DDIM update as one kernel.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from . import _lib as L
+from . import ops
+from .nn import Conv2d, GroupNorm, LayerNorm, Linear, Module, ModuleList
+from .tensor import Tensor, _new, float32, tensor
+
+
+def _tokens(x: Tensor) -> Tensor:
+    """[N, C, H, W] channels-last -> [N*H*W, C] view (no copy)."""
+    n, c, h, w = x.shape
+    assert x.is_contiguous("channels_last"), "UNet activations are kept channels-last"
+    return x.permute(0, 2, 3, 1).reshape(n * h * w, c)
+
+
+def _image(t: Tensor, n, h, w) -> Tensor:
+    c = t.shape[-1]
+    return t.reshape(n, h, w, c).permute(0, 3, 1, 2)
+
+
+class ResnetBlock(Module):
+    def __init__(self, cin, cout, temb=1280, device=None, dtype=None):
+        super().__init__()
+        self.norm1 = GroupNorm(32, cin, device=device, dtype=dtype)
+        self.conv1 = Conv2d(cin, cout, 3, padding=1, device=device, dtype=dtype)
+        self.time_emb_proj = Linear(temb, cout, device=device, dtype=dtype)
+        self.norm2 = GroupNorm(32, cout, device=device, dtype=dtype)
+        self.conv2 = Conv2d(cout, cout, 3, padding=1, device=device, dtype=dtype)
+        self.conv_shortcut = Conv2d(cin, cout, 1, device=device, dtype=dtype) if cin != cout else None
+        self.cout = cout
+
+    def forward(self, x, temb_silu):
+        n = x.shape[0]
+        h = self.norm1(x, fuse_silu=True)
+        # per-image bias = time_emb_proj(silu(temb)) + time_emb_proj.bias + conv1.bias  (fp32 [N, C])
+        b = ops.add(self.time_emb_proj.bias, self.conv1.bias).float()
+        tb = ops.gemm(temb_silu, self.time_emb_proj.weight.transpose(0, 1), bias=b, out_dtype=float32)
+        h = self.conv1(h, bias=tb, bias_batch_stride=self.cout)
+        h = self.norm2(h, fuse_silu=True)
+        res = x if self.conv_shortcut is None else self.conv_shortcut(x)
+        return self.conv2(h, residual=res)
+
+
+class GEGLUFeedForward(Module):
+    """Linear(C, 8C) -> (value, gate) halves -> value * gelu(gate) -> Linear(4C, C).  The first
+    weight is kept in the module's canonical [value rows; gate rows] order; the kernel consumes a
+    cached copy interleaved in (64 value, 64 gate) row groups."""
+
+    def __init__(self, c, mult=4, device=None, dtype=None):
+        super().__init__()
+        self.inner = c * mult
+        self.proj = Linear(c, 2 * self.inner, device=device, dtype=dtype)
+        self.out = Linear(self.inner, c, device=device, dtype=dtype)
+        self._il = None
+
+    def _interleaved(self):
+        w, b = self.proj.weight, self.proj.bias
+        key = (id(w), w._version, id(b), b._version)
+        if self._il is None or self._il[0] != key:
+            F, K = self.inner, w.shape[1]
+            wi = w.reshape(2, F // 64, 64, K).permute(1, 0, 2, 3).contiguous().reshape(2 * F, K)
+            bi = b.reshape(2, F // 64, 64).permute(1, 0, 2).contiguous().reshape(2 * F)
+            self._il = (key, wi, bi)
+        return self._il[1], self._il[2]
+
+    def forward(self, h, residual):
+        wi, bi = self._interleaved()
+        g = ops.linear(h, wi, bi, epilogue=L.EPI_GEGLU)
+        return ops.linear(g, self.out.weight, self.out.bias, residual=residual)
+
+
+class BasicTransformerBlock(Module):
+    def __init__(self, c, heads, ctx_dim=768, device=None, dtype=None):
+        super().__init__()
+        self.heads, self.c = heads, c
+        kw = dict(device=device, dtype=dtype)
+        self.norm1 = LayerNorm(c, **kw)
+        self.to_qkv = Linear(c, 3 * c, bias=False, **kw)
+        self.to_out1 = Linear(c, c, **kw)
+        self.norm2 = LayerNorm(c, **kw)
+        self.to_q2 = Linear(c, c, bias=False, **kw)
+        self.to_kv2 = Linear(ctx_dim, 2 * c, bias=False, **kw)
+        self.to_out2 = Linear(c, c, **kw)
+        self.norm3 = LayerNorm(c, **kw)
+        self.ff = GEGLUFeedForward(c, **kw)
+
+    def _attend(self, q, k, v, n, s_q, s_k):
+        """q: [n*s_q, C] view with row pitch, k/v: [n*s_k, C] views -> [n*s_q, C] heads-merged."""
+        H, D = self.heads, self.c // self.heads
+
+        def heads(t, s):
+            # [n*s, C] (row pitch p) -> [n, H, s, D] strided view
+            p = t.stride(0)
+            return t._view((n, H, s, D), (s * p, D, p, 1))
+
+        o = _new((n * s_q, self.c), q.dtype, q.device)
+        ov = o._view((n, H, s_q, D), (s_q * self.c, D, self.c, 1))
+        ops.scaled_dot_product_attention(heads(q, s_q), heads(k, s_k), heads(v, s_k), out=ov)
+        return o
+
+    def forward(self, h, ctx, n, s):
+        c = self.c
+        x = self.norm1(h)
+        qkv = ops.linear(x, self.to_qkv.weight)
+        a = self._attend(qkv[:, 0:c], qkv[:, c:2 * c], qkv[:, 2 * c:3 * c], n, s, s)
+        h = ops.linear(a, self.to_out1.weight, self.to_out1.bias, residual=h)
+        x = self.norm2(h)
+        q = ops.linear(x, self.to_q2.weight)
+        s_ctx = ctx.shape[1]
+        kv = ops.linear(ctx.reshape(-1, ctx.shape[-1]), self.to_kv2.weight)
+        a = self._attend(q, kv[:, 0:c], kv[:, c:2 * c], n, s, s_ctx)
+        h = ops.linear(a, self.to_out2.weight, self.to_out2.bias, residual=h)
+        x = self.norm3(h)
+        return self.ff(x, residual=h)
+
+
+class SpatialTransformer(Module):
+    def __init__(self, c, heads=8, ctx_dim=768, device=None, dtype=None):
+        super().__init__()
+        kw = dict(device=device, dtype=dtype)
+        self.norm = GroupNorm(32, c, eps=1e-6, **kw)
+        self.proj_in = Linear(c, c, **kw)
+        self.block = BasicTransformerBlock(c, heads, ctx_dim, **kw)
+        self.proj_out = Linear(c, c, **kw)
+
+    def forward(self, x, ctx):
+        n, c, hh, ww = x.shape
+        t = _tokens(self.norm(x))
+        t = ops.linear(t, self.proj_in.weight, self.proj_in.bias)
+        t = self.block(t, ctx, n, hh * ww)
+        t = ops.linear(t, self.proj_out.weight, self.proj_out.bias, residual=_tokens(x))
+        return _image(t, n, hh, ww)
+
+
+class Downsample(Module):
+    def __init__(self, c, device=None, dtype=None):
+        super().__init__()
+        self.conv = Conv2d(c, c, 3, stride=2, padding=1, device=device, dtype=dtype)
+
+    def forward(self, x):
+        return self.conv(x)
+
+
+class Upsample(Module):
+    def __init__(self, c, device=None, dtype=None):
+        super().__init__()
+        self.conv = Conv2d(c, c, 3, padding=1, device=device, dtype=dtype)
+
+    def forward(self, x):
+        return self.conv(ops.interpolate_nearest2x(x))
+
+
+def timestep_embedding(t: np.ndarray, dim=320) -> np.ndarray:
+    """Sinusoidal embedding, cos first (SD's flip_sin_to_cos=True, shift 0)."""
+    half = dim // 2
+    freqs = np.exp(-math.log(10000.0) * np.arange(half, dtype=np.float64) / half)
+    args = np.asarray(t, np.float64)[:, None] * freqs[None]
+    return np.concatenate([np.cos(args), np.sin(args)], axis=1).astype(np.float32)
+
+
+class UNet(Module):
+    def __init__(self, in_ch=4, out_ch=4, chans=(320, 640, 1280, 1280), attn=(True, True, True, False), layers=2,
+                 heads=8, ctx_dim=768, device=None, dtype=None):
+        super().__init__()
+        kw = dict(device=device, dtype=dtype)
+        self.chans = chans
+        tdim = chans[0] * 4
+        self.time_lin1 = Linear(chans[0], tdim, **kw)
+        self.time_lin2 = Linear(tdim, tdim, **kw)
+        self.conv_in = Conv2d(in_ch, chans[0], 3, padding=1, **kw)
+        self.down = ModuleList()
+        skip_ch = [chans[0]]
+        c = chans[0]
+        for lvl, co in enumerate(chans):
+            for _ in range(layers):
+                self.down.append(ResnetBlock(c, co, tdim, **kw))
+                c = co
+                self.down.append(SpatialTransformer(c, heads, ctx_dim, **kw) if attn[lvl] else None_())
+                skip_ch.append(c)
+            if lvl != len(chans) - 1:
+                self.down.append(Downsample(c, **kw))
+                skip_ch.append(c)
+        self.mid1 = ResnetBlock(c, c, tdim, **kw)
+        self.mid_attn = SpatialTransformer(c, heads, ctx_dim, **kw)
+        self.mid2 = ResnetBlock(c, c, tdim, **kw)
+        self.up = ModuleList()
+        for lvl, co in reversed(list(enumerate(chans))):
+            for _ in range(layers + 1):
+                self.up.append(ResnetBlock(c + skip_ch.pop(), co, tdim, **kw))
+                c = co
+                self.up.append(SpatialTransformer(c, heads, ctx_dim, **kw) if attn[lvl] else None_())
+            if lvl != 0:
+                self.up.append(Upsample(c, **kw))
+        self.norm_out = GroupNorm(32, c, **kw)
+        self.conv_out = Conv2d(c, out_ch, 3, padding=1, **kw)
+
+    def time_embed(self, t: Tensor) -> Tensor:
+        """silu(time_embedding(t)) — consumed by every ResNet block's projection."""
+        h = ops.linear(t, self.time_lin1.weight, self.time_lin1.bias, epilogue=L.EPI_SILU)
+        return ops.linear(h, self.time_lin2.weight, self.time_lin2.bias, epilogue=L.EPI_SILU)
+
+    def forward(self, x: Tensor, t_emb: Tensor, ctx: Tensor) -> Tensor:
+        """x [N, 4, H, W] (any layout), t_emb [N, 320] (sinusoidal, model dtype), ctx [N, 77, 768]."""
+        temb = self.time_embed(t_emb)
+        h = ops.conv2d(x, self.conv_in.weight, self.conv_in.bias, 1, 1, packed=self.conv_in.packed_weight(),
+                       out_channels_last=True)
+        skips = [h]
+        mods = list(self.down)
+        i = 0
+        while i < len(mods):
+            m = mods[i]
+            if isinstance(m, ResnetBlock):
+                h = m(h, temb)
+                a = mods[i + 1]
+                if not isinstance(a, None_):
+                    h = a(h, ctx)
+                skips.append(h)
+                i += 2
+            else:
+                h = m(h)
+                skips.append(h)
+                i += 1
+        h = self.mid1(h, temb)
+        h = self.mid_attn(h, ctx)
+        h = self.mid2(h, temb)
+        mods = list(self.up)
+        i = 0
+        while i < len(mods):
+            m = mods[i]
+            if isinstance(m, ResnetBlock):
+                h = m(ops.cat([h, skips.pop()], dim=1), temb)
+                a = mods[i + 1]
+                if not isinstance(a, None_):
+                    h = a(h, ctx)
+                i += 2
+            else:
+                h = m(h)
+                i += 1
+        h = self.norm_out(h, fuse_silu=True)
+        out = ops.conv2d(h, self.conv_out.weight, self.conv_out.bias, 1, 1, packed=self.conv_out.packed_weight(),
+                         out_channels_last=False)
+        return out
+
+
+class None_(Module):
+    """Placeholder for a level without attention (keeps the module list regular)."""
+
+    def forward(self, x, *a):
+        return x
+
+
+def unet_flops_per_sample(H=64, W=64, ctx_len=77, classes: dict | None = None) -> float:
+    """Algorithmic FLOPs of one UNet forward for one sample (2 per MAC).  If `classes` is given it
+    receives the split into "conv", "attn" (QK^T and PV) and "linear" (everything else)."""
+    chans, layers = (320, 640, 1280, 1280), 2
+    fl = 0.0
+    acc = {"conv": 0.0, "attn": 0.0}
+
+    def conv(cin, cout, k, h, w):
+        f = 2.0 * cin * cout * k * k * h * w
+        acc["conv"] += f
+        return f
+
+    def resnet(cin, cout, h, w):
+        f = conv(cin, cout, 3, h, w) + conv(cout, cout, 3, h, w) + 2.0 * 1280 * cout
+        if cin != cout:
+            f += conv(cin, cout, 1, h, w)
+        return f
+
+    def transformer(c, h, w):
+        s = h * w
+        f = 2 * 2.0 * s * c * c  # proj in / out
+        f += 2.0 * s * c * 3 * c + 2 * 2.0 * s * s * c + 2.0 * s * c * c  # self attn
+        f += 2.0 * s * c * c + 2.0 * ctx_len * 768 * 2 * c + 2 * 2.0 * s * ctx_len * c + 2.0 * s * c * c  # cross
+        f += 2.0 * s * c * 8 * c + 2.0 * s * 4 * c * c  # GEGLU FF
+        acc["attn"] += 2 * 2.0 * s * s * c + 2 * 2.0 * s * ctx_len * c
+        return f
+
+    h = H
+    fl += conv(4, 320, 3, H, W) + 2.0 * 320 * 1280 + 2.0 * 1280 * 1280
+    c = 320
+    skip = [320]
+    for lvl, co in enumerate(chans):
+        for _ in range(layers):
+            fl += resnet(c, co, h, h)
+            c = co
+            if lvl < 3:
+                fl += transformer(c, h, h)
+            skip.append(c)
+        if lvl != 3:
+            fl += conv(c, c, 3, h // 2, h // 2)
+            h //= 2
+            skip.append(c)
+    fl += 2 * resnet(c, c, h, h) + transformer(c, h, h)
+    for lvl, co in reversed(list(enumerate(chans))):
+        for _ in range(layers + 1):
+            fl += resnet(c + skip.pop(), co, h, h)
+            c = co
+            if lvl < 3:
+                fl += transformer(c, h, h)
+        if lvl != 0:
+            h *= 2
+            fl += conv(c, c, 3, h, h)
+    fl += conv(320, 4, 3, H, W)
+    if classes is not None:
+        classes.update(conv=acc["conv"], attn=acc["attn"], linear=fl - acc["conv"] - acc["attn"])
+    return fl
+
+
+class DDIM:
+    """DDIM sampling schedule: SD's scaled-linear betas (sqrt-linspace(0.00085, 0.012)^2 over
+    1000 training steps, as the reference's scheduler scenario builds them,
+    tests/compat/benchmarking.py:6138-6141), evenly spaced inference timesteps, and the
+    reference's step formula with the x0 clamp (6148-6168)."""
+
+    def __init__(self, steps=50, train_steps=1000, beta_start=0.00085, beta_end=0.012, clip=True):
+        betas = np.linspace(beta_start ** 0.5, beta_end ** 0.5, train_steps, dtype=np.float64) ** 2
+        self.alphas_cumprod = np.cumprod(1.0 - betas)
+        self.interval = train_steps // steps
+        self.timesteps = (np.arange(steps) * self.interval)[::-1].copy()
+        self.clip = clip
+
+    def alphas(self, t):
+        prev = max(int(t) - self.interval, 0)
+        return float(self.alphas_cumprod[int(t)]), float(self.alphas_cumprod[prev])
+
+    def step(self, x: Tensor, eps: Tensor, t, out: Tensor | None = None) -> Tensor:
+        a_t, a_prev = self.alphas(t)
+        return ops.ddim_step(x, eps, a_t, a_prev, clip=self.clip, out=out)
+
+
+def denoise(unet: UNet, latents: Tensor, ctx: Tensor, sched: DDIM, steps: int | None = None) -> Tensor:
+    """The DDIM loop: `steps` (default: all) UNet evaluations + fused updates, on device."""
+    n = latents.shape[0]
+    x = latents.contiguous()
+    ts = sched.timesteps if steps is None else sched.timesteps[:steps]
+    for t in ts:
+        temb = tensor(timestep_embedding(np.full(n, float(t))), dtype=latents.dtype, device=latents.device)
+        eps = unet(x, temb, ctx)
+        x = sched.step(x, eps, t)
+    return x
