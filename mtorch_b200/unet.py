@@ -23,7 +23,7 @@ import numpy as np
 from . import _lib as L
 from . import ops
 from .nn import Conv2d, GroupNorm, LayerNorm, Linear, Module, ModuleList
-from .tensor import Tensor, _new, float32, tensor
+from .tensor import Tensor, _new, add, float32, tensor
 
 
 def _tokens(x: Tensor) -> Tensor:
@@ -53,7 +53,7 @@ class ResnetBlock(Module):
         n = x.shape[0]
         h = self.norm1(x, fuse_silu=True)
         # per-image bias = time_emb_proj(silu(temb)) + time_emb_proj.bias + conv1.bias  (fp32 [N, C])
-        b = ops.add(self.time_emb_proj.bias, self.conv1.bias).float()
+        b = add(self.time_emb_proj.bias, self.conv1.bias).float()
         tb = ops.gemm(temb_silu, self.time_emb_proj.weight.transpose(0, 1), bias=b, out_dtype=float32)
         h = self.conv1(h, bias=tb, bias_batch_stride=self.cout)
         h = self.norm2(h, fuse_silu=True)
