@@ -1,16 +1,399 @@
-// bf16 / f16 flash attention on tcgen05.  Until the tensor-core kernel is in place this unit
-// reports every request as "not handled", so the SIMT flash kernel runs.
+// Flash attention on the 5th-generation tensor cores (tcgen05 + TMEM), bf16 / f16, sm_100a.
+//
+// One CTA = 128 query rows of one (batch, head); KV tiles of 128 keys stream through a
+// TMA ring.  Roles (192 threads):
+//   warp 0      TMA producer: Q once, then (K_j, V_j) per stage.  Operands are read straight
+//               from the caller's strided [B, H, S, D] views (e.g. head slices of a fused QKV
+//               projection) with 5-D tensor maps {8, S, D/8, H, B}: the box lands in shared
+//               memory as [D/8 chunk][row][8 elems] — the UMMA no-swizzle core-matrix layout —
+//               and the head-dim padding to a multiple of 16 comes from TMA's zero fill.
+//   warp 1      MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers (fp32), then
+//               O_j = P_j V_j (P from shared memory, V as an MN-major operand) into TMEM.
+//   warps 2..5  softmax (one query row per thread, its TMEM lane): online softmax in base 2 on
+//               S_j (pass 1: row max, pass 2: p = 2^(s - m), row sum, bf16 P to shared memory),
+//               then O += O_j * 1 and the running rescale in registers; finally O / l to global.
+// No masks / causal on this path (the UNet does not use them): those requests run the SIMT
+// kernel.  All waits are bounded (timeout -> device error word, kernel returns).
 #include "runtime.h"
 
 namespace mt {
 
 MT_STATUS_READER(read_status_attention)
 
+constexpr int kFaBM = 128;       // query rows per CTA
+constexpr int kFaBN = 128;       // keys per tile
+constexpr int kFaThreads = 192;
+constexpr int kFaMaxStages = 4;
+
+struct FaParams {
+  int Sq, Sk, H, Hkv, B;
+  float scale_log2;  // softmax scale * log2(e)
+  void* o;
+  int64_t os[4];
+  int Dv;
+  int out_dtype;
+  int stages;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Shared-memory descriptor, no swizzle: lbo / sbo in bytes (see the layout notes above).
+__device__ __forceinline__ uint64_t sdesc_none(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFF) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;  // layout type 0 = SWIZZLE_NONE
+}
+
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16_row(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int DP, int DVP, bool F16>
+__global__ void __launch_bounds__(kFaThreads, 1)
+    fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+  constexpr int Q_BYTES = kFaBM * DP * 2;
+  constexpr int K_BYTES = kFaBN * DP * 2;
+  constexpr int V_BYTES = kFaBN * DVP * 2;
+  constexpr int P_BYTES = kFaBM * kFaBN * 2;
+  constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+  constexpr uint32_t kLboQK = kFaBM * 16;  // next 8-element K chunk (rows * 16 B); BM == BN
+  constexpr uint32_t kSbo = 128;          // next 8 rows
+  constexpr int FMT = F16 ? 0 : 1;
+  constexpr uint32_t idesc_s = make_idesc(FMT, kFaBM, kFaBN);
+  constexpr uint32_t idesc_o = make_idesc(FMT, kFaBM, DVP) | (1u << 16);  // B (V) MN-major
+
+  extern __shared__ uint8_t fa_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sP = sQ + Q_BYTES;
+  uint8_t* sKV = sP + P_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + p.stages * STAGE_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kFaMaxStages;
+  uint64_t* s_full = kv_empty + kFaMaxStages;  // [2]
+  uint64_t* s_empty = s_full + 2;              // [2]
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* o_full = p_full + 1;
+  uint64_t* o_empty = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int stages = p.stages;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / (p.H / p.Hkv);
+  const int q0 = blockIdx.x * kFaBM;
+  const int n_tiles = (p.Sk + kFaBN - 1) / kFaBN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, 128);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s[2] = {tmem, tmem + 128};
+  const uint32_t t_o = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, Q_BYTES);
+      tma_load_5d(sQ, &tmQ, q_full, 0, q0, 0, h, b);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1, 11, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[stage], STAGE_BYTES);
+        uint8_t* sk = sKV + stage * STAGE_BYTES;
+        tma_load_5d(sk, &tmK, &kv_full[stage], 0, j * kFaBN, 0, hk, b);
+        tma_load_5d(sk + K_BYTES, &tmV, &kv_full[stage], 0, j * kFaBN, 0, hk, b);
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, 12, abort_flag);
+      int stage = 0, prev_stage = 0;
+      uint32_t phase = 0;
+      // O_{jj} = P_{jj} V_{jj}; releases the KV stage of tile jj.
+      auto issue_pv = [&](int jj) -> bool {
+        if (!mbar_wait(p_full, jj & 1, 15, abort_flag)) return false;
+        if (!mbar_wait(o_empty, (jj & 1) ^ 1, 16, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sKV + prev_stage * STAGE_BYTES + K_BYTES);
+        // V (MN-major): next 8 keys = 128 B (LBO), next 8 value dims = BN * 16 B (SBO)
+#pragma unroll
+        for (int kk = 0; kk < kFaBN / 16; ++kk)
+          umma_f16(t_o, sdesc_none(p_addr + kk * 2 * (kFaBM * 16), kFaBM * 16, kSbo),
+                   sdesc_none(v_addr + kk * 256, 128, kFaBN * 16), idesc_o, kk > 0 ? 1u : 0u);
+        umma_commit(o_full);
+        umma_commit(&kv_empty[prev_stage]);
+        return true;
+      };
+      for (int j = 0; ok && j <= n_tiles; ++j) {
+        // With a single KV stage the next tile's K/V can only arrive after PV of this one.
+        if (j > 0 && stages == 1 && !issue_pv(j - 1)) break;
+        if (j < n_tiles) {
+          if (!mbar_wait(&kv_full[stage], phase, 13, abort_flag)) break;
+          if (!mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, 14, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sKV + stage * STAGE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < DP / 16; ++kk)
+            umma_f16(t_s[j & 1], sdesc_none(q_addr + kk * 2 * kLboQK, kLboQK, kSbo),
+                     sdesc_none(k_addr + kk * 2 * kLboQK, kLboQK, kSbo), idesc_s, kk > 0 ? 1u : 0u);
+          umma_commit(&s_full[j & 1]);
+        }
+        if (j > 0 && stages > 1 && !issue_pv(j - 1)) break;
+        if (j < n_tiles) {
+          prev_stage = stage;
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- softmax / output warpgroup ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float o_acc[DVP];
+#pragma unroll
+    for (int i = 0; i < DVP; ++i) o_acc[i] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    const float sl = p.scale_log2;
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, 17, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t ts = t_s[j & 1] + lane_off;
+      const int kvalid = min(kFaBN, p.Sk - j * kFaBN);
+      // pass 1: row max of the scaled scores
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kFaBN; c0 += 16) {
+        float v[16];
+        tmem_ld16_row(ts + c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (c0 + i < kvalid) mx = fmaxf(mx, v[i] * sl);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float corr = ex2(m_run - m_new);  // 0 on the first tile (m_run = -inf)
+      // pass 2: p = 2^(s*scale*log2e - m), row sum, P (bf16/f16) to shared memory
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kFaBN; c0 += 16) {
+        float v[16];
+        tmem_ld16_row(ts + c0, v);
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float a = (c0 + i < kvalid) ? ex2(v[i] * sl - m_new) : 0.f;
+          const float bq = (c0 + i + 1 < kvalid) ? ex2(v[i + 1] * sl - m_new) : 0.f;
+          sum += a + bq;
+          pk[i / 2] = F16 ? pack_f16x2(a, bq) : pack_bf16x2(a, bq);
+        }
+        // keys c0..c0+7 -> chunk c0/8, keys c0+8..c0+15 -> chunk c0/8+1; this row at +row*16
+        uint4* d0 = reinterpret_cast<uint4*>(sP + (c0 / 8) * (kFaBM * 16) + row * 16);
+        uint4* d1 = reinterpret_cast<uint4*>(sP + (c0 / 8 + 1) * (kFaBM * 16) + row * 16);
+        *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[j & 1]);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+      l_run = l_run * corr + sum;
+      m_run = m_new;
+      // accumulate O_j (scaled by the same running max) once the PV MMA is done
+      if (!mbar_wait(o_full, j & 1, 18, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < DVP; c0 += 16) {
+        float v[16];
+        tmem_ld16_row(t_o + lane_off + c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o_acc[c0 + i] = o_acc[c0 + i] * corr + v[i];
+      }
+      tc_fence_before();
+      mbar_arrive(o_empty);
+    }
+    const int qi = q0 + row;
+    if (ok && qi < p.Sq) {
+      const float inv = 1.0f / l_run;
+      char* base = static_cast<char*>(p.o);
+      const int64_t off = (int64_t)b * p.os[0] + (int64_t)h * p.os[1] + (int64_t)qi * p.os[2];
+      if (p.os[3] == 1 && (p.Dv % 8) == 0 && ((reinterpret_cast<uintptr_t>(base) + off * 2) % 16) == 0) {
+        uint4* dst = reinterpret_cast<uint4*>(base + off * 2);
+#pragma unroll
+        for (int c = 0; c < DVP; c += 8) {
+          if (c < p.Dv) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = F16 ? pack_f16x2(o_acc[c + 2 * i] * inv, o_acc[c + 2 * i + 1] * inv)
+                         : pack_bf16x2(o_acc[c + 2 * i] * inv, o_acc[c + 2 * i + 1] * inv);
+            dst[c / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < DVP; ++c)
+          if (c < p.Dv) store_from_f32(p.o, off + (int64_t)c * p.os[3], p.out_dtype, o_acc[c] * inv);
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host side.
+
+template <int DP, int DVP>
+struct FaCfg {
+  static constexpr int FIXED = kFaBM * DP * 2 + kFaBM * kFaBN * 2;
+  static constexpr int STAGE = kFaBN * (DP + DVP) * 2;
+  static constexpr int SMEM_MAX = 225 * 1024;
+  static constexpr int STAGES_RAW = (SMEM_MAX - 2048 - FIXED) / STAGE;
+  static constexpr int STAGES = STAGES_RAW > kFaMaxStages ? kFaMaxStages : STAGES_RAW;
+  static constexpr int smem_bytes(int stages) { return FIXED + stages * STAGE + 2048; }
+};
+
+// 5-D map {8, S, D/8, heads, batch} over a strided [B, Hx, S, D] view (element strides st).
+static int fa_map(CUtensorMap* m, int dtype, const void* base, int64_t B, int64_t Hx, int64_t S, int64_t D,
+                  const int64_t* st, int box_chunks) {
+  if (st[3] != 1) return fail(MT_ERR_UNSUPPORTED, "flash attention: head dim must be unit-stride");
+  uint64_t dims[5] = {8, (uint64_t)S, (uint64_t)(D / 8), (uint64_t)Hx, (uint64_t)B};
+  uint64_t strides[4] = {(uint64_t)st[2] * 2, 16, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  uint32_t box[5] = {8, 128, (uint32_t)box_chunks, 1, 1};
+  if (B == 1) strides[3] = strides[2] * (uint64_t)Hx + 16;  // unused dim: any legal stride
+  if (Hx == 1) strides[2] = 16;
+  return make_tensor_map(m, dtype, 5, base, dims, strides, box, 0);
+}
+
+template <int DP, int DVP, bool F16>
+static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
+  using Cfg = FaCfg<DP, DVP>;
+  const int stages = Cfg::STAGES;
+  if (stages < 1) return fail(MT_ERR_UNSUPPORTED, "flash attention: head dim too large for shared memory");
+  const int smem = Cfg::smem_bytes(stages) + 1024;
+  auto kern = fa_sm100_kernel<DP, DVP, F16>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                        "flash attention smem attribute");
+    if (rc) return rc;
+    attr[dev & 63] = true;
+  }
+  CUtensorMap mq, mk, mv;
+  int rc = fa_map(&mq, d.dtype, d.q, d.B, d.H, d.Sq, d.D, d.q_strides, DP / 8);
+  if (!rc) rc = fa_map(&mk, d.dtype, d.k, d.B, d.Hkv, d.Sk, d.D, d.k_strides, DP / 8);
+  if (!rc) rc = fa_map(&mv, d.dtype, d.v, d.B, d.Hkv, d.Sk, d.Dv, d.v_strides, DVP / 8);
+  if (rc) return rc;
+  FaParams p{};
+  p.Sq = (int)d.Sq; p.Sk = (int)d.Sk; p.H = (int)d.H; p.Hkv = (int)d.Hkv; p.B = (int)d.B;
+  p.scale_log2 = (float)(d.scale * 1.4426950408889634);
+  p.o = d.o;
+  for (int i = 0; i < 4; ++i) p.os[i] = d.o_strides[i];
+  p.Dv = (int)d.Dv;
+  p.out_dtype = d.dtype;
+  p.stages = stages;
+  dim3 grid((unsigned)((d.Sq + kFaBM - 1) / kFaBM), (unsigned)(d.B * d.H));
+  kern<<<grid, kFaThreads, smem, st>>>(mq, mk, mv, p);
+  return check_launch("flash_attention_sm100");
+}
+
 size_t sdpa_tc_workspace(const mt_sdpa_desc&) { return 0; }
 
-int run_sdpa_tc(const mt_sdpa_desc&, void*, size_t, cudaStream_t, bool* handled) {
+static bool aligned16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int run_sdpa_tc(const mt_sdpa_desc& d, void*, size_t, cudaStream_t st, bool* handled) {
   *handled = false;
-  return MT_OK;
+  if (d.dtype != MT_BF16 && d.dtype != MT_F16) return MT_OK;
+  if (d.mask_kind != 0 || d.causal) return MT_OK;
+  if (d.D != d.Dv || d.D % 8 != 0) return MT_OK;
+  if (d.Sq > INT32_MAX || d.Sk > INT32_MAX || d.B * d.H > 65535) return MT_OK;
+  if (!aligned16p(d.q) || !aligned16p(d.k) || !aligned16p(d.v)) return MT_OK;
+  for (int i = 0; i < 3; ++i)
+    if ((d.q_strides[i] * 2) % 16 || (d.k_strides[i] * 2) % 16 || (d.v_strides[i] * 2) % 16) return MT_OK;
+  if (d.q_strides[3] != 1 || d.k_strides[3] != 1 || d.v_strides[3] != 1) return MT_OK;
+  const bool f16 = d.dtype == MT_F16;
+  int rc;
+  const int64_t Dp = (d.D + 15) / 16 * 16;
+  switch (Dp) {
+    case 48: rc = f16 ? fa_launch<48, 48, true>(d, st) : fa_launch<48, 48, false>(d, st); break;
+    case 64: rc = f16 ? fa_launch<64, 64, true>(d, st) : fa_launch<64, 64, false>(d, st); break;
+    case 80: rc = f16 ? fa_launch<80, 80, true>(d, st) : fa_launch<80, 80, false>(d, st); break;
+    case 128: rc = f16 ? fa_launch<128, 128, true>(d, st) : fa_launch<128, 128, false>(d, st); break;
+    case 160: rc = f16 ? fa_launch<160, 160, true>(d, st) : fa_launch<160, 160, false>(d, st); break;
+    default: return MT_OK;
+  }
+  *handled = true;
+  return rc;
 }
 
 }  // namespace mt
