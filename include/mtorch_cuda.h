@@ -116,6 +116,21 @@ int mt_cuda_group_norm(void* y, int y_dtype, const int64_t* y_strides, const voi
                        int64_t C, int64_t HW, int64_t groups, double eps, int fuse_silu, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* Group norm for callers that cannot hand the library a workspace — for example code running
+ * inside a host callback, a custom allocator hook, or an embedding runtime that owns every
+ * device allocation and forbids cudaMalloc / cudaFree on its threads.  Same arguments and result
+ * as mt_cuda_group_norm minus the workspace; the statistics scratch lives in a fixed array
+ * inside this library (MT_GROUP_NORM_STATIC_SCRATCH_BYTES per GPU, held until process exit).
+ * Requests needing more scratch than that (about N * ceil(HW/64) * groups > 500000 for
+ * channels-last input, 16 bytes each) are rejected with MT_ERR_INVALID.  The first call on each device looks up
+ * the array's device address and should therefore come before any stream capture.  All calls
+ * share the one array: calls that may overlap on the GPU (different streams, or different host
+ * threads) race and must be serialised by the caller.  No counterpart in the reference. */
+#define MT_GROUP_NORM_STATIC_SCRATCH_BYTES (8u << 20)
+int mt_cuda_group_norm_noalloc(void* y, int y_dtype, const int64_t* y_strides, const void* x, int x_dtype,
+                               const int64_t* x_strides, const void* weight, const void* bias, int wb_dtype, int64_t N,
+                               int64_t C, int64_t HW, int64_t groups, double eps, int fuse_silu, void* stream);
+
 /* ---- dense contractions on tcgen05 / TMEM ---------------------------------------------- */
 typedef enum {
   MT_EPI_NONE = 0,

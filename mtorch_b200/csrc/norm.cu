@@ -1,5 +1,7 @@
 // Row softmax, layer norm and group norm (+ fused SiLU).  HBM-bound; fp32 arithmetic with
 // fp64 combination of group-norm partial sums.
+#include <mutex>
+
 #include "runtime.h"
 
 namespace mt {
@@ -374,4 +376,98 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
   return check_launch("group_norm apply");
 }
 
+// ---------------------------------------------------------------------------------------------
+// Group norm without a caller workspace: the partial sums and per-group statistics live in a
+// fixed array of this translation unit, so the call performs no device allocation at all.
+// Every byte of the scratch that is read is first written in the same call (partial kernel ->
+// finalize -> apply), so nothing has to be cleared between calls.
+
+static __device__ __align__(256) unsigned char g_gn_static_scratch[MT_GROUP_NORM_STATIC_SCRATCH_BYTES];
+
+static void* g_gn_scratch_addr[64];
+static cudaError_t g_gn_scratch_err[64];
+static std::once_flag g_gn_scratch_once[64];
+
+// Device address of the scratch array on the current device.  In host code the array's name is
+// only a host-side stand-in; the address must come from cudaGetSymbolAddress, once per device,
+// with that device current.
+static int gn_static_scratch(void** out) {
+  int dev = 0;
+  int rc = cuda_check(cudaGetDevice(&dev), "group_norm_noalloc: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return fail(MT_ERR_UNSUPPORTED, "group_norm_noalloc: device index %d", dev);
+  std::call_once(g_gn_scratch_once[dev], [dev] {
+    void* p = nullptr;
+    g_gn_scratch_err[dev] = cudaGetSymbolAddress(&p, g_gn_static_scratch);
+    g_gn_scratch_addr[dev] = p;
+  });
+  if (g_gn_scratch_err[dev] != cudaSuccess)
+    return fail(MT_ERR_LAUNCH, "group_norm_noalloc: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(g_gn_scratch_err[dev]));
+  *out = g_gn_scratch_addr[dev];
+  return MT_OK;
+}
+
+static int launch_group_norm_noalloc(void* y, int yd, const int64_t* ys, const void* x, int xd, const int64_t* xs,
+                                     const void* w, const void* b, int wbd, int64_t N, int64_t C, int64_t HW,
+                                     int64_t G, double eps, int silu, cudaStream_t st) {
+  if (!ys || !xs) return fail(MT_ERR_INVALID, "group_norm_noalloc: null strides");
+  if (G <= 0 || C % G != 0)
+    return fail(MT_ERR_INVALID, "group_norm: channels %lld not divisible by groups %lld", (long long)C, (long long)G);
+  if (N == 0 || C == 0 || HW == 0) return MT_OK;
+  const bool cl = (xs[1] == 1 && xs[2] == C) && HW > 1;
+  const bool nchw = (xs[2] == 1 && xs[1] == HW) || (HW == 1 && xs[1] == 1);
+  if (!cl && !nchw) return fail(MT_ERR_UNSUPPORTED, "group_norm: input must be NCHW-contiguous or channels-last");
+  if (N > 65535 || (!cl && N * G > 65535)) return fail(MT_ERR_UNSUPPORTED, "group_norm: batch too large");
+  const int chunks = gn_chunks(C, HW, G, cl);
+  const size_t part_bytes = align_up((size_t)N * chunks * G * 2 * sizeof(double), 256);
+  const size_t need = part_bytes + (size_t)N * G * 2 * sizeof(float);
+  if (need > MT_GROUP_NORM_STATIC_SCRATCH_BYTES)
+    return fail(MT_ERR_INVALID,
+                "group_norm_noalloc: this shape needs %zu bytes of scratch, more than the fixed %u bytes; "
+                "use mt_cuda_group_norm with a workspace",
+                need, (unsigned)MT_GROUP_NORM_STATIC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  int rc = gn_static_scratch(&scratch);
+  if (rc) return rc;
+  double* part = static_cast<double*>(scratch);
+  float* stats = reinterpret_cast<float*>(static_cast<char*>(scratch) + part_bytes);
+  if (cl) {
+    const int64_t slots = C >= kGnThreads ? C : (kGnThreads / C) * C;
+    if (2 * slots * sizeof(float) > 48 * 1024) return fail(MT_ERR_UNSUPPORTED, "group_norm: too many channels");
+    gn_partial_cl_kernel<<<dim3(chunks, (unsigned)N), kGnThreads, 2 * slots * sizeof(float), st>>>(
+        x, xd, xs[0], xs[2], C, HW, G, chunks, part);
+  } else {
+    gn_partial_nchw_kernel<<<dim3(chunks, (unsigned)(N * G)), kGnThreads, 0, st>>>(x, xd, xs[0], xs[1], C, HW, G,
+                                                                                  chunks, part);
+  }
+  rc = check_launch("group_norm_noalloc partial");
+  if (rc) return rc;
+  gn_finalize_kernel<<<(unsigned)((N * G + 127) / 128), 128, 0, st>>>(part, stats, N, G, chunks,
+                                                                      (double)(C / G) * (double)HW, eps);
+  rc = check_launch("group_norm_noalloc finalize");
+  if (rc) return rc;
+  const bool ycl = (ys[1] == 1 && ys[2] == C && ys[0] == HW * C);
+  const int64_t total = N * C * HW;
+  if (cl && ycl && xs[0] == HW * C && xd == MT_BF16 && yd == MT_BF16 && C % 8 == 0 && (uintptr_t)x % 16 == 0 &&
+      (uintptr_t)y % 16 == 0) {
+    const int64_t blocks = std::min<int64_t>((total / 8 + 255) / 256, (int64_t)num_sms() * 16);
+    gn_apply_cl_bf16x8_kernel<<<(unsigned)blocks, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, stats, w,
+                                                                b, wbd, N, HW, C, G, silu);
+  } else {
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
+    gn_apply_generic_kernel<<<(unsigned)blocks, 256, 0, st>>>(y, yd, ys[0], ys[1], ys[2], x, xd, xs[0], xs[1], xs[2],
+                                                             stats, w, b, wbd, N, C, HW, G, silu, cl ? 1 : 0);
+  }
+  return check_launch("group_norm_noalloc apply");
+}
+
 }  // namespace mt
+
+extern "C" int mt_cuda_group_norm_noalloc(void* y, int y_dtype, const int64_t* y_strides, const void* x, int x_dtype,
+                                          const int64_t* x_strides, const void* weight, const void* bias, int wb_dtype,
+                                          int64_t N, int64_t C, int64_t HW, int64_t groups, double eps, int fuse_silu,
+                                          void* stream) {
+  return mt::launch_group_norm_noalloc(y, y_dtype, y_strides, x, x_dtype, x_strides, weight, bias, wb_dtype, N, C, HW,
+                                       groups, eps, fuse_silu, reinterpret_cast<cudaStream_t>(stream));
+}
