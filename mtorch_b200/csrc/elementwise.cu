@@ -49,6 +49,22 @@ __global__ void copy_strided_kernel(void* dst, int dd, const void* src, int sd, 
   }
 }
 
+// Same-dtype strided copy in 16-byte units (offsets of `nd` are in 16-byte units).
+__global__ void copy_rows16_kernel(uint4* dst, const uint4* src, StridedND nd, int64_t n16) {
+  const int64_t inner = nd.sizes[nd.ndim - 1];
+  MT_GRID_STRIDE(i, n16) {
+    const int64_t row = i / inner, v = i - row * inner;
+    int64_t od = 0, os = 0, r = row;
+    for (int d = nd.ndim - 2; d >= 0; --d) {
+      const int64_t c = r % nd.sizes[d];
+      r /= nd.sizes[d];
+      od += c * nd.s0[d];
+      os += c * nd.s1[d];
+    }
+    dst[od + v] = src[os + v];
+  }
+}
+
 // Contiguous same-dtype 16-byte copies.
 __global__ void copy_vec16_kernel(uint4* dst, const uint4* src, int64_t n16) {
   MT_GRID_STRIDE(i, n16) dst[i] = src[i];
@@ -302,12 +318,64 @@ int launch_copy_strided(void* dst, int dd, const int64_t* dst_st, const void* sr
       return check_launch("cast");
     }
   }
+  // Normalise: drop size-1 dims, order by destination stride (largest first) and merge dims
+  // that are contiguous in both operands.  A channel-concat into a channels-last tensor, or a
+  // nearest-upsample view, becomes [rows, inner] with a unit-stride inner run on both sides.
   StridedND nd{};
-  nd.ndim = ndim;
+  int m = 0;
   for (int d = 0; d < ndim; ++d) {
-    nd.sizes[d] = sizes[d];
-    nd.s0[d] = dst_st[d];
-    nd.s1[d] = src_st[d];
+    if (sizes[d] == 1) continue;
+    nd.sizes[m] = sizes[d];
+    nd.s0[m] = dst_st[d];
+    nd.s1[m] = src_st[d];
+    ++m;
+  }
+  for (int i = 1; i < m; ++i)  // insertion sort, descending |dst stride|
+    for (int j = i; j > 0 && llabs(nd.s0[j]) > llabs(nd.s0[j - 1]); --j) {
+      std::swap(nd.sizes[j], nd.sizes[j - 1]);
+      std::swap(nd.s0[j], nd.s0[j - 1]);
+      std::swap(nd.s1[j], nd.s1[j - 1]);
+    }
+  int k = 0;
+  for (int i = 1; i < m; ++i) {
+    if (nd.s0[k] == nd.s0[i] * nd.sizes[i] && nd.s1[k] == nd.s1[i] * nd.sizes[i]) {
+      nd.sizes[k] *= nd.sizes[i];
+      nd.s0[k] = nd.s0[i];
+      nd.s1[k] = nd.s1[i];
+    } else {
+      ++k;
+      nd.sizes[k] = nd.sizes[i];
+      nd.s0[k] = nd.s0[i];
+      nd.s1[k] = nd.s1[i];
+    }
+  }
+  nd.ndim = m ? k + 1 : 0;
+  if (nd.ndim == 0) {  // a single element
+    nd.ndim = 1;
+    nd.sizes[0] = 1;
+    nd.s0[0] = nd.s1[0] = 1;
+  }
+  const int es = dtype_size(dd);
+  const int last = nd.ndim - 1;
+  if (dd == sd && nd.s0[last] == 1 && nd.s1[last] == 1 && (nd.sizes[last] * es) % 16 == 0 &&
+      (uintptr_t)dst % 16 == 0 && (uintptr_t)src % 16 == 0) {
+    bool ok = true;
+    for (int d = 0; d < last; ++d) ok = ok && (nd.s0[d] * es) % 16 == 0 && (nd.s1[d] * es) % 16 == 0;
+    if (ok) {
+      // rows of 16-byte vectors: the outer dims are addressed in units of 16 bytes
+      StridedND rows{};
+      rows.ndim = nd.ndim;
+      for (int d = 0; d < last; ++d) {
+        rows.sizes[d] = nd.sizes[d];
+        rows.s0[d] = nd.s0[d] * es / 16;
+        rows.s1[d] = nd.s1[d] * es / 16;
+      }
+      rows.sizes[last] = nd.sizes[last] * es / 16;
+      rows.s0[last] = rows.s1[last] = 1;
+      const int64_t n16 = n * es / 16;
+      copy_rows16_kernel<<<grid_for(n16, 256), 256, 0, st>>>((uint4*)dst, (const uint4*)src, rows, n16);
+      return check_launch("copy_rows16");
+    }
   }
   copy_strided_kernel<<<grid_for(n, 256), 256, 0, st>>>(dst, dd, src, sd, nd, n);
   return check_launch("copy_strided");

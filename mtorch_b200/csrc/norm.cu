@@ -147,10 +147,85 @@ __global__ void __launch_bounds__(NT) layer_norm_kernel(void* y, int yd, const v
   }
 }
 
+// bf16 rows of cols = 8*k <= 8*32*VPL elements: one warp per row, 16-byte loads, the row held in
+// registers (VPL vectors per lane), two-pass mean / variance, 16-byte stores.
+template <int VPL>
+__global__ void __launch_bounds__(256) layer_norm_bf16_warp_kernel(__nv_bfloat16* y, const __nv_bfloat16* x,
+                                                                   const void* w, const void* b, int wbd,
+                                                                   int64_t rows, int cols, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nv = cols / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(x + row * cols);
+  float v[VPL][8];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int vi = lane + 32 * k;
+    if (vi < nv) {
+      uint4 u = src[vi];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        v[k][2 * j] = f.x;
+        v[k][2 * j + 1] = f.y;
+        s += f.x + f.y;
+      }
+    }
+  }
+  const float mean = warp_sum(s) / (float)cols;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k)
+    if (lane + 32 * k < nv)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q += (v[k][j] - mean) * (v[k][j] - mean);
+  const float inv = rsqrtf(warp_sum(q) / (float)cols + eps);
+  uint4* dst = reinterpret_cast<uint4*>(y + row * cols);
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int vi = lane + 32 * k;
+    if (vi < nv) {
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float r[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int c = vi * 8 + 2 * j + e;
+          float t = (v[k][2 * j + e] - mean) * inv;
+          if (w) t *= load_as_f32(w, c, wbd);
+          if (b) t += load_as_f32(b, c, wbd);
+          r[e] = t;
+        }
+        o[j] = pack_bf16x2(r[0], r[1]);
+      }
+      dst[vi] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 int launch_layer_norm(void* y, int yd, const void* x, int xd, const void* w, const void* b, int wbd, int64_t rows,
                       int64_t cols, double eps, cudaStream_t st) {
   if (rows == 0 || cols == 0) return MT_OK;
   if (rows > 0x7fffffffLL) return fail(MT_ERR_UNSUPPORTED, "layer_norm: too many rows");
+  if (xd == MT_BF16 && yd == MT_BF16 && cols % 8 == 0 && cols <= 8 * 32 * 8 && (uintptr_t)x % 16 == 0 &&
+      (uintptr_t)y % 16 == 0 && rows / 8 < 0x7fffffffLL) {
+    const unsigned grid = (unsigned)((rows + 7) / 8);
+    const int vpl = (int)((cols / 8 + 31) / 32);
+    if (vpl <= 2)
+      layer_norm_bf16_warp_kernel<2><<<grid, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd, rows,
+                                                           (int)cols, (float)eps);
+    else if (vpl <= 4)
+      layer_norm_bf16_warp_kernel<4><<<grid, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd, rows,
+                                                           (int)cols, (float)eps);
+    else
+      layer_norm_bf16_warp_kernel<8><<<grid, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd, rows,
+                                                           (int)cols, (float)eps);
+    return check_launch("layer_norm_bf16_warp");
+  }
   if (cols <= 512)
     layer_norm_kernel<64, 8><<<(unsigned)rows, 64, 0, st>>>(y, yd, x, xd, w, b, wbd, cols, (float)eps);
   else
@@ -211,6 +286,109 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_cl_kernel(const void* x
     double* o = part + (((int64_t)n * chunks + chunk) * G + g) * 2;
     o[0] = s;
     o[1] = q;
+  }
+}
+
+// Channels-last bf16 partial sums, 8 channels (16 bytes) per load: V = C/8 vectors per pixel,
+// thread t owns vector t % V of pixel lane t / V; one (lane, channel) slot per thread and
+// channel in shared memory keeps the reduction order fixed.
+__global__ void __launch_bounds__(kGnThreads) gn_partial_cl_bf16x8_kernel(const __nv_bfloat16* x, int64_t sn,
+                                                                          int64_t C, int64_t HW, int64_t G,
+                                                                          int chunks, double* part) {
+  extern __shared__ float gn_sh[];  // [2][lanes * C]
+  const int n = blockIdx.y, chunk = blockIdx.x;
+  const int64_t per = (HW + chunks - 1) / chunks;
+  const int64_t p0 = chunk * per, p1 = min(HW, p0 + per);
+  const int64_t V = C / 8;
+  const int64_t lanes = V >= kGnThreads ? 1 : kGnThreads / V;
+  const int64_t slots = lanes * C;
+  const __nv_bfloat16* xb = x + (int64_t)n * sn;
+  for (int64_t t = threadIdx.x; t < lanes * V; t += kGnThreads) {
+    const int64_t lane = t / V, v = t % V;
+    float s[8], q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = q[j] = 0.f;
+    for (int64_t p = p0 + lane; p < p1; p += lanes) {
+      uint4 u = *reinterpret_cast<const uint4*>(xb + p * C + v * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        s[2 * j] += f.x;
+        q[2 * j] += f.x * f.x;
+        s[2 * j + 1] += f.y;
+        q[2 * j + 1] += f.y * f.y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      gn_sh[lane * C + v * 8 + j] = s[j];
+      gn_sh[slots + lane * C + v * 8 + j] = q[j];
+    }
+  }
+  __syncthreads();
+  for (int64_t c = threadIdx.x; c < C; c += kGnThreads) {
+    float s = 0.f, q = 0.f;
+    for (int64_t l = 0; l < lanes; ++l) {
+      s += gn_sh[l * C + c];
+      q += gn_sh[slots + l * C + c];
+    }
+    gn_sh[c] = s;
+    gn_sh[slots + c] = q;
+  }
+  __syncthreads();
+  const int64_t Cg = C / G;
+  for (int64_t g = threadIdx.x; g < G; g += kGnThreads) {
+    double s = 0.0, q = 0.0;
+    for (int64_t c = g * Cg; c < (g + 1) * Cg; ++c) {
+      s += gn_sh[c];
+      q += gn_sh[slots + c];
+    }
+    double* o = part + (((int64_t)n * chunks + chunk) * G + g) * 2;
+    o[0] = s;
+    o[1] = q;
+  }
+}
+
+// Per-(image, channel) affine of the normalisation: y = x * a + b with a = rstd * gamma and
+// b = beta - mean * a, so the apply pass needs no division or group lookup.
+__global__ void gn_table_kernel(const float* stats, const void* w, const void* b, int wbd, int64_t N, int64_t C,
+                                int64_t G, float2* tab) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= N * C) return;
+  const int64_t n = i / C, c = i % C;
+  const float* st = stats + (n * G + c / (C / G)) * 2;
+  float a = st[1], sh = -st[0] * st[1];
+  if (w) {
+    const float gm = load_as_f32(w, c, wbd);
+    a *= gm;
+    sh *= gm;
+  }
+  if (b) sh += load_as_f32(b, c, wbd);
+  tab[i] = make_float2(a, sh);
+}
+
+__global__ void gn_apply_cl_bf16x8_tab_kernel(__nv_bfloat16* y, const __nv_bfloat16* x, const float2* tab, int64_t HW,
+                                              int64_t C, int64_t total8, int silu) {
+  const int64_t C8 = C / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c8 = i % C8;
+    const int64_t n = i / (HW * C8);
+    uint4 v = reinterpret_cast<const uint4*>(x)[i];
+    const float4* t = reinterpret_cast<const float4*>(tab + n * C + c8 * 8);
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 ab = t[j];  // (a0, b0, a1, b1)
+      float2 f = __bfloat1622float2(h[j]);
+      float r0 = f.x * ab.x + ab.y, r1 = f.y * ab.z + ab.w;
+      if (silu) {
+        r0 = silu_f(r0);
+        r1 = silu_f(r1);
+      }
+      h[j] = __floats2bfloat162_rn(r0, r1);
+    }
+    reinterpret_cast<uint4*>(y)[i] = v;
   }
 }
 
@@ -328,8 +506,13 @@ static int gn_chunks(int64_t C, int64_t HW, int64_t G, bool cl) {
   return (int)chunks;
 }
 
+static size_t gn_part_bytes(int64_t N, int64_t G) {
+  return align_up((size_t)N * kGnMaxChunks * G * 2 * sizeof(double), 256);
+}
+static size_t gn_stats_bytes(int64_t N, int64_t G) { return align_up((size_t)N * G * 2 * sizeof(float), 256); }
+
 size_t group_norm_workspace(int64_t N, int64_t C, int64_t HW, int64_t G) {
-  return align_up((size_t)N * kGnMaxChunks * G * 2 * sizeof(double), 256) + (size_t)N * G * 2 * sizeof(float);
+  return gn_part_bytes(N, G) + gn_stats_bytes(N, G) + (size_t)N * C * sizeof(float2);
 }
 
 int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd, const int64_t* xs, const void* w,
@@ -344,9 +527,17 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
   if (!cl && !nchw) return fail(MT_ERR_UNSUPPORTED, "group_norm: input must be NCHW-contiguous or channels-last");
   if (N > 65535 || (!cl && N * G > 65535)) return fail(MT_ERR_UNSUPPORTED, "group_norm: batch too large");
   double* part = (double*)ws;
-  float* stats = (float*)((char*)ws + align_up((size_t)N * kGnMaxChunks * G * 2 * sizeof(double), 256));
+  float* stats = (float*)((char*)ws + gn_part_bytes(N, G));
+  float2* tab = (float2*)((char*)ws + gn_part_bytes(N, G) + gn_stats_bytes(N, G));
   const int chunks = gn_chunks(C, HW, G, cl);
-  if (cl) {
+  const bool vec_in = cl && xd == MT_BF16 && C % 8 == 0 && (uintptr_t)x % 16 == 0 && (xs[0] * 2) % 16 == 0;
+  if (vec_in) {
+    const int64_t V = C / 8;
+    const int64_t slots = (V >= kGnThreads ? 1 : kGnThreads / V) * C;
+    if (2 * slots * sizeof(float) > 48 * 1024) return fail(MT_ERR_UNSUPPORTED, "group_norm: too many channels");
+    gn_partial_cl_bf16x8_kernel<<<dim3(chunks, (unsigned)N), kGnThreads, 2 * slots * sizeof(float), st>>>(
+        (const __nv_bfloat16*)x, xs[0], C, HW, G, chunks, part);
+  } else if (cl) {
     const int64_t slots = C >= kGnThreads ? C : (kGnThreads / C) * C;
     if (2 * slots * sizeof(float) > 48 * 1024) return fail(MT_ERR_UNSUPPORTED, "group_norm: too many channels");
     gn_partial_cl_kernel<<<dim3(chunks, (unsigned)N), kGnThreads, 2 * slots * sizeof(float), st>>>(
@@ -363,11 +554,13 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
   if (rc) return rc;
   const bool ycl = (ys[1] == 1 && ys[2] == C && ys[0] == HW * C);
   const int64_t total = N * C * HW;
-  if (cl && ycl && xs[0] == HW * C && xd == MT_BF16 && yd == MT_BF16 && C % 8 == 0 && (uintptr_t)x % 16 == 0 &&
-      (uintptr_t)y % 16 == 0) {
-    const int64_t blocks = std::min<int64_t>((total / 8 + 255) / 256, (int64_t)num_sms() * 16);
-    gn_apply_cl_bf16x8_kernel<<<(unsigned)blocks, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, stats, w,
-                                                                b, wbd, N, HW, C, G, silu);
+  if (vec_in && ycl && xs[0] == HW * C && yd == MT_BF16 && (uintptr_t)y % 16 == 0) {
+    gn_table_kernel<<<(unsigned)((N * C + 255) / 256), 256, 0, st>>>(stats, w, b, wbd, N, C, G, tab);
+    rc = check_launch("group_norm table");
+    if (rc) return rc;
+    const int64_t blocks = std::min<int64_t>((total / 8 + 255) / 256, (int64_t)num_sms() * 32);
+    gn_apply_cl_bf16x8_tab_kernel<<<(unsigned)blocks, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, tab,
+                                                                    HW, C, total / 8, silu);
   } else {
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
     gn_apply_generic_kernel<<<(unsigned)blocks, 256, 0, st>>>(y, yd, ys[0], ys[1], ys[2], x, xd, xs[0], xs[1], xs[2],

@@ -65,6 +65,26 @@ def test_strided_copy_and_cast():
     np.testing.assert_array_equal(up, x.numpy().repeat(2, 2).repeat(2, 3))
 
 
+def test_channels_last_cat_and_upsample_bf16_exact():
+    """The UNet's skip concat and nearest-2x upsample on channels-last bf16 (16-byte row path)."""
+    a = cu(rnd(2, 320, 8, 8), "bfloat16").contiguous(memory_format=mt.channels_last)
+    b = cu(rnd(2, 640, 8, 8, seed=1), "bfloat16").contiguous(memory_format=mt.channels_last)
+    c = mt.cat([a, b], dim=1)
+    assert c.is_contiguous(mt.channels_last)
+    np.testing.assert_array_equal(c.numpy(), np.concatenate([a.numpy(), b.numpy()], 1))
+    up = mt.nn.functional.interpolate(b, scale_factor=2)
+    assert up.is_contiguous(mt.channels_last)
+    np.testing.assert_array_equal(up.numpy(), b.numpy().repeat(2, 2).repeat(2, 3))
+
+
+@pytest.mark.parametrize("cols", [320, 640, 1280, 200])
+def test_layer_norm_bf16(cols):
+    x, w, b = rnd(333, cols, seed=4, scale=3.0) + 1.0, rnd(cols, seed=5), rnd(cols, seed=6)
+    ref = oracle.layer_norm_f32(bf16_round(x), bf16_round(w), bf16_round(b))
+    got = mt.layer_norm(cu(x, "bfloat16"), [cols], cu(w, "bfloat16"), cu(b, "bfloat16")).numpy()
+    check(got, ref, BF16_RTOL)
+
+
 def test_device_uniform_matches_host_generator():
     mt.manual_seed(7)
     host = mt.rand(1001).numpy()
