@@ -20,7 +20,9 @@ from mtorch_b200.tensor import workspace
 
 pytestmark = pytest.mark.gpu
 
-RTOL = 1e-4
+# the tolerances the other GPU tests use: fp32 1e-4; bf16 2e-2 (one bf16 rounding step, since the
+# two entry points may order the fp32 affine arithmetic differently before rounding to bf16)
+RTOL = {"float32": 1e-4, "bfloat16": 2e-2}
 
 
 def _reference(x, G, w, b, silu):
@@ -62,7 +64,7 @@ def test_no_alloc_group_norm_matches_workspace_version_twice(dtype):
         silu = call % 2
         want = _reference(x, G, w, b, silu).numpy()
         got = _no_alloc(x, G, w, b, silu).numpy()
-        np.testing.assert_allclose(got, want, rtol=RTOL, atol=RTOL * np.abs(want).max())
+        np.testing.assert_allclose(got, want, rtol=RTOL[dtype], atol=RTOL[dtype] * np.abs(want).max())
 
 
 def test_no_alloc_group_norm_rejects_oversized_request():
