@@ -6,7 +6,7 @@
 //               (BN rows x 128 B) into a STAGES-deep shared-memory ring (mbarrier full/empty);
 //   warp 1      MMA issuer: one thread issues tcgen05.mma (kind::f16 for bf16/f16, three
 //               kind::tf32 products for fp32) into one of two TMEM accumulators (2 x BN columns);
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane TMEM quarter),
+//   warps 2..9  epilogue: tcgen05.ld the accumulator (two warps per 32-lane TMEM quarter),
 //               apply alpha / beta*C / bias / activation / residual and store; the TMEM buffer
 //               is then released, so the next tile's MMAs overlap this tile's stores.
 // Convolution: the A tile of output pixels (tn x th x tw = 128) at filter tap (r, s) and channel
@@ -22,7 +22,7 @@ namespace mt {
 MT_STATUS_READER(read_status_gemm)
 
 constexpr int kBM = 128;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;  // 2 producer/MMA warps + 8 epilogue warps
 
 struct TileParams {
   int num_m_tiles, num_n_tiles, batch;
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 256);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -273,8 +273,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..9) ----------------
+    // Two warps per TMEM lane quarter: warps 2..5 take the even 32-column chunks of the tile,
+    // warps 6..9 the odd ones.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const bool geglu = ep.act == MT_EPI_GEGLU;
     const int64_t n_out = geglu ? ep.N / 2 : ep.N;
@@ -317,7 +320,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool vec = ep.vec_ok != 0;
       if (!geglu) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = half * 32; c0 < BN; c0 += 64) {
           uint32_t r[32];
           tmem_ld32(taddr + c0, r);
           tmem_ld_wait();
@@ -346,8 +349,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // 64 their gates; output column = nt*BN/2 + g*64 + j.
 #pragma unroll 1
         for (int g = 0; g < BN / 128; ++g) {
-#pragma unroll 1
-          for (int h = 0; h < 64; h += 32) {
+          {
+            const int h = half * 32;
             uint32_t rv[32], rg[32];
             tmem_ld32(taddr + g * 128 + h, rv);
             tmem_ld32(taddr + g * 128 + 64 + h, rg);
