@@ -1,28 +1,30 @@
 // Flash attention on the 5th-generation tensor cores (tcgen05 + TMEM), bf16 / f16, sm_100a.
 //
-// One CTA = 128 query rows of one (batch, head); KV tiles of 128 keys stream through a
-// TMA ring.  Roles (192 threads):
-//   warp 0      TMA producer: Q once, then (K_j, V_j) per stage.  Operands are read straight
-//               from the caller's strided [B, H, S, D] views (e.g. head slices of a fused QKV
-//               projection) with 5-D tensor maps {8, S, D/8, H, B}: the box lands in shared
-//               memory as [D/8 chunk][row][8 elems] — the UMMA no-swizzle core-matrix layout —
-//               and the head-dim padding to a multiple of 16 comes from TMA's zero fill.
-//   warp 1      MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers (fp32), then
-//               O_j = P_j V_j (P from shared memory, V as an MN-major operand) into TMEM.
-//   warps 2..5  softmax (one query row per thread, its TMEM lane): online softmax in base 2 on
-//               S_j (pass 1: row max, pass 2: p = 2^(s - m), row sum, bf16 P to shared memory),
-//               then O += O_j * 1 and the running rescale in registers; finally O / l to global.
-// No masks / causal on this path (the UNet does not use them): those requests run the SIMT
-// kernel.  All waits are bounded (timeout -> device error word, kernel returns).
+// One CTA = NQ tiles of 128 query rows (NQ = 2 for head dims <= 128) of one (batch, head); KV
+// tiles of 128 keys stream through a TMA ring and are shared by the NQ query tiles.
+// Roles (64 + 128*NQ threads):
+//   warp 0      TMA producer: the Q tiles once, then (K_j, V_j) per stage.  Operands are read
+//               straight from the caller's strided [B, H, S, D] views (e.g. head slices of a
+//               fused QKV projection) with 5-D tensor maps {8, S, D/8, H, B}: a box lands in
+//               shared memory as [D/8 chunk][row][8 elems] — the UMMA no-swizzle core-matrix
+//               layout — and the head-dim padding to a multiple of 16 is TMA's zero fill.
+//   warp 1      MMA issuer: S_x = Q_x K_j^T into TMEM (fp32) for each query tile x, then
+//               O_x = P_x V_j (P from shared memory, V as an MN-major operand) into TMEM.
+//   warps 2..   one softmax warpgroup per query tile (one query row per thread = its TMEM lane):
+//               online softmax in base 2 on S (pass 1: row max of the raw scores; pass 2:
+//               p = 2^(s*scale*log2e - m) with packed f32x2 FMAs, row sums, bf16/f16 P to shared
+//               memory), then O += O_j with the running rescale in registers; finally O / l.
+// While one warpgroup exponentiates its scores the tensor core computes the other tile's
+// scores, so the two query tiles interleave.  Masks / causal requests run the SIMT kernel (the
+// UNet does not use them).  All waits are bounded (timeout -> device error word, return).
 #include "runtime.h"
 
 namespace mt {
 
 MT_STATUS_READER(read_status_attention)
 
-constexpr int kFaBM = 128;       // query rows per CTA
-constexpr int kFaBN = 128;       // keys per tile
-constexpr int kFaThreads = 192;
+constexpr int kFaBM = 128;  // query rows per tile
+constexpr int kFaBN = 128;  // keys per KV tile
 constexpr int kFaMaxStages = 4;
 
 struct FaParams {
@@ -45,7 +47,27 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Shared-memory descriptor, no swizzle: lbo / sbo in bytes (see the layout notes above).
+__device__ __forceinline__ uint64_t f2_bits(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+// (a0, a1) * (b0, b1) + (c0, c1) in one instruction
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// Shared-memory descriptor, no swizzle: lbo / sbo in bytes.
 __device__ __forceinline__ uint64_t sdesc_none(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
   d |= (uint64_t)((addr & 0x3FFFF) >> 4);
@@ -64,20 +86,16 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16_row(uint32_t taddr, float* v) {
-  uint32_t r[16];
+__device__ __forceinline__ void tmem_ld16_raw(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  tmem_ld_wait();
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int DP, int DVP, bool F16>
-__global__ void __launch_bounds__(kFaThreads, 1)
+template <int DP, int DVP, int NQ, bool F16>
+__global__ void __launch_bounds__(64 + 128 * NQ, 1)
     fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FaParams p) {
   constexpr int Q_BYTES = kFaBM * DP * 2;
@@ -85,27 +103,28 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   constexpr int V_BYTES = kFaBN * DVP * 2;
   constexpr int P_BYTES = kFaBM * kFaBN * 2;
   constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
-  constexpr uint32_t kLboQK = kFaBM * 16;  // next 8-element K chunk (rows * 16 B); BM == BN
-  constexpr uint32_t kSbo = 128;          // next 8 rows
+  constexpr uint32_t kLbo = kFaBM * 16;  // next 8-element K chunk (128 rows * 16 B); BM == BN
+  constexpr uint32_t kSbo = 128;        // next 8 rows
   constexpr int FMT = F16 ? 0 : 1;
   constexpr uint32_t idesc_s = make_idesc(FMT, kFaBM, kFaBN);
   constexpr uint32_t idesc_o = make_idesc(FMT, kFaBM, DVP) | (1u << 16);  // B (V) MN-major
+  static_assert(NQ == 1 || 2 * 128 + 2 * DVP <= 512, "TMEM budget");
 
   extern __shared__ uint8_t fa_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sP = sQ + Q_BYTES;
-  uint8_t* sKV = sP + P_BYTES;
+  uint8_t* sQ = smem;                   // [NQ][Q]
+  uint8_t* sP = sQ + NQ * Q_BYTES;      // [NQ][P]
+  uint8_t* sKV = sP + NQ * P_BYTES;     // [stages][K, V]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + p.stages * STAGE_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + kFaMaxStages;
-  uint64_t* s_full = kv_empty + kFaMaxStages;  // [2]
+  uint64_t* s_full = kv_empty + kFaMaxStages;  // [2] score slots
   uint64_t* s_empty = s_full + 2;              // [2]
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* o_full = p_full + 1;
-  uint64_t* o_empty = o_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 1);
+  uint64_t* p_full = s_empty + 2;              // [NQ]
+  uint64_t* o_full = p_full + 2;               // [NQ]
+  uint64_t* o_empty = o_full + 2;              // [NQ]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -113,7 +132,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int hk = h / (p.H / p.Hkv);
-  const int q0 = blockIdx.x * kFaBM;
+  const int qbase = blockIdx.x * (kFaBM * NQ);
   const int n_tiles = (p.Sk + kFaBN - 1) / kFaBN;
 
   if (threadIdx.x == 0) {
@@ -125,10 +144,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_full, 1);
-    mbar_init(o_empty, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -140,16 +159,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s[2] = {tmem, tmem + 128};
-  const uint32_t t_o = tmem + 256;
+  // score slot i at columns [128 i, 128 i + 128); O of query tile x after the score slots
+  const uint32_t t_o0 = tmem + 256;
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, Q_BYTES);
-      tma_load_5d(sQ, &tmQ, q_full, 0, q0, 0, h, b);
+      mbar_arrive_expect_tx(q_full, NQ * Q_BYTES);
+      for (int x = 0; x < NQ; ++x) tma_load_5d(sQ + x * Q_BYTES, &tmQ, q_full, 0, qbase + x * kFaBM, 0, h, b);
       int stage = 0;
       uint32_t phase = 0;
       for (int j = 0; j < n_tiles; ++j) {
@@ -170,18 +189,21 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       bool ok = mbar_wait(q_full, 0, 12, abort_flag);
       int stage = 0, prev_stage = 0;
       uint32_t phase = 0;
-      // O_{jj} = P_{jj} V_{jj}; releases the KV stage of tile jj.
+      // O_x = P_x V_{jj} for every query tile; releases the KV stage of tile jj.
       auto issue_pv = [&](int jj) -> bool {
-        if (!mbar_wait(p_full, jj & 1, 15, abort_flag)) return false;
-        if (!mbar_wait(o_empty, (jj & 1) ^ 1, 16, abort_flag)) return false;
-        tc_fence_after();
         const uint32_t v_addr = smem_u32(sKV + prev_stage * STAGE_BYTES + K_BYTES);
-        // V (MN-major): next 8 keys = 128 B (LBO), next 8 value dims = BN * 16 B (SBO)
+        for (int x = 0; x < NQ; ++x) {
+          if (!mbar_wait(&p_full[x], jj & 1, 15, abort_flag)) return false;
+          if (!mbar_wait(&o_empty[x], (jj & 1) ^ 1, 16, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t pa = p_addr + x * P_BYTES;
+          // V (MN-major): next 8 keys = 128 B (LBO), next 8 value dims = BN * 16 B (SBO)
 #pragma unroll
-        for (int kk = 0; kk < kFaBN / 16; ++kk)
-          umma_f16(t_o, sdesc_none(p_addr + kk * 2 * (kFaBM * 16), kFaBM * 16, kSbo),
-                   sdesc_none(v_addr + kk * 256, 128, kFaBN * 16), idesc_o, kk > 0 ? 1u : 0u);
-        umma_commit(o_full);
+          for (int kk = 0; kk < kFaBN / 16; ++kk)
+            umma_f16(t_o0 + x * DVP, sdesc_none(pa + kk * 2 * kLbo, kLbo, kSbo),
+                     sdesc_none(v_addr + kk * 256, 128, kFaBN * 16), idesc_o, kk > 0 ? 1u : 0u);
+          umma_commit(&o_full[x]);
+        }
         umma_commit(&kv_empty[prev_stage]);
         return true;
       };
@@ -190,14 +212,25 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (j > 0 && stages == 1 && !issue_pv(j - 1)) break;
         if (j < n_tiles) {
           if (!mbar_wait(&kv_full[stage], phase, 13, abort_flag)) break;
-          if (!mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, 14, abort_flag)) break;
-          tc_fence_after();
           const uint32_t k_addr = smem_u32(sKV + stage * STAGE_BYTES);
+          bool sok = true;
+          for (int x = 0; x < NQ; ++x) {
+            // NQ == 2: slot x is reused every KV tile; NQ == 1: the two slots alternate
+            const int slot = NQ == 2 ? x : (j & 1);
+            const uint32_t par = NQ == 2 ? ((j & 1) ^ 1) : (((j >> 1) & 1) ^ 1);
+            if (!mbar_wait(&s_empty[slot], par, 14, abort_flag)) {
+              sok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t qa = q_addr + x * Q_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < DP / 16; ++kk)
-            umma_f16(t_s[j & 1], sdesc_none(q_addr + kk * 2 * kLboQK, kLboQK, kSbo),
-                     sdesc_none(k_addr + kk * 2 * kLboQK, kLboQK, kSbo), idesc_s, kk > 0 ? 1u : 0u);
-          umma_commit(&s_full[j & 1]);
+            for (int kk = 0; kk < DP / 16; ++kk)
+              umma_f16(tmem + slot * 128, sdesc_none(qa + kk * 2 * kLbo, kLbo, kSbo),
+                       sdesc_none(k_addr + kk * 2 * kLbo, kLbo, kSbo), idesc_s, kk > 0 ? 1u : 0u);
+            umma_commit(&s_full[slot]);
+          }
+          if (!sok) break;
         }
         if (j > 0 && stages > 1 && !issue_pv(j - 1)) break;
         if (j < n_tiles) {
@@ -210,73 +243,103 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax / output warpgroup ----------------
+    // ---------------- softmax / output warpgroups ----------------
+    const int x = (warp - 2) >> 2;  // query tile of this warpgroup
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint8_t* sPx = sP + x * P_BYTES;
+    const uint32_t t_o = t_o0 + x * DVP + lane_off;
     float o_acc[DVP];
 #pragma unroll
     for (int i = 0; i < DVP; ++i) o_acc[i] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
     const float sl = p.scale_log2;
+    const uint64_t sl2 = f2_bits(sl, sl);
     bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, 17, abort_flag)) { ok = false; break; }
+      const int slot = NQ == 2 ? x : (j & 1);
+      const uint32_t par = NQ == 2 ? (j & 1) : ((j >> 1) & 1);
+      if (!mbar_wait(&s_full[slot], par, 17, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const uint32_t ts = t_s[j & 1] + lane_off;
+      const uint32_t ts = tmem + slot * 128 + lane_off;
       const int kvalid = min(kFaBN, p.Sk - j * kFaBN);
-      // pass 1: row max of the scaled scores
+      const bool full = kvalid == kFaBN;
+      // pass 1: row max of the raw scores (the scale is positive)
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c0 = 0; c0 < kFaBN; c0 += 16) {
-        float v[16];
-        tmem_ld16_row(ts + c0, v);
+        uint32_t r[16];
+        tmem_ld16_raw(ts + c0, r);
+        tmem_ld_wait();
+        if (full) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (c0 + i < kvalid) mx = fmaxf(mx, v[i] * sl);
+          for (int i = 0; i < 16; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
       }
-      const float m_new = fmaxf(m_run, mx);
+      const float m_new = fmaxf(m_run, mx * sl);
       const float corr = ex2(m_run - m_new);  // 0 on the first tile (m_run = -inf)
-      // pass 2: p = 2^(s*scale*log2e - m), row sum, P (bf16/f16) to shared memory
-      float sum = 0.f;
+      const uint64_t negm2 = f2_bits(-m_new, -m_new);
+      // pass 2: p = 2^(s * sl - m), packed row sums, P (bf16/f16) to shared memory
+      uint64_t sum2 = f2_bits(0.f, 0.f);
 #pragma unroll 1
       for (int c0 = 0; c0 < kFaBN; c0 += 16) {
-        float v[16];
-        tmem_ld16_row(ts + c0, v);
+        uint32_t r[16];
+        tmem_ld16_raw(ts + c0, r);
+        tmem_ld_wait();
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
-          const float a = (c0 + i < kvalid) ? ex2(v[i] * sl - m_new) : 0.f;
-          const float bq = (c0 + i + 1 < kvalid) ? ex2(v[i + 1] * sl - m_new) : 0.f;
-          sum += a + bq;
-          pk[i / 2] = F16 ? pack_f16x2(a, bq) : pack_bf16x2(a, bq);
+          const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2, negm2);
+          float a0, a1;
+          f2_unpack(arg, a0, a1);
+          float e0 = ex2(a0), e1 = ex2(a1);
+          if (!full) {
+            if (c0 + i >= kvalid) e0 = 0.f;
+            if (c0 + i + 1 >= kvalid) e1 = 0.f;
+          }
+          sum2 = fadd2(sum2, f2_bits(e0, e1));
+          pk[i / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
         }
         // keys c0..c0+7 -> chunk c0/8, keys c0+8..c0+15 -> chunk c0/8+1; this row at +row*16
-        uint4* d0 = reinterpret_cast<uint4*>(sP + (c0 / 8) * (kFaBM * 16) + row * 16);
-        uint4* d1 = reinterpret_cast<uint4*>(sP + (c0 / 8 + 1) * (kFaBM * 16) + row * 16);
+        uint4* d0 = reinterpret_cast<uint4*>(sPx + (c0 / 8) * (kFaBM * 16) + row * 16);
+        uint4* d1 = reinterpret_cast<uint4*>(sPx + (c0 / 8 + 1) * (kFaBM * 16) + row * 16);
         *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
       tc_fence_before();
-      mbar_arrive(&s_empty[j & 1]);
+      mbar_arrive(&s_empty[slot]);
       fence_proxy_async_smem();
-      mbar_arrive(p_full);
-      l_run = l_run * corr + sum;
+      mbar_arrive(&p_full[x]);
+      float s0, s1;
+      f2_unpack(sum2, s0, s1);
+      l_run = l_run * corr + (s0 + s1);
       m_run = m_new;
       // accumulate O_j (scaled by the same running max) once the PV MMA is done
-      if (!mbar_wait(o_full, j & 1, 18, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&o_full[x], j & 1, 18, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
 #pragma unroll
       for (int c0 = 0; c0 < DVP; c0 += 16) {
-        float v[16];
-        tmem_ld16_row(t_o + lane_off + c0, v);
+        uint32_t r[16];
+        tmem_ld16_raw(t_o + c0, r);
+        tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o_acc[c0 + i] = o_acc[c0 + i] * corr + v[i];
+        for (int i = 0; i < 16; ++i) o_acc[c0 + i] = fmaf(o_acc[c0 + i], corr, __uint_as_float(r[i]));
       }
       tc_fence_before();
-      mbar_arrive(o_empty);
+      mbar_arrive(&o_empty[x]);
     }
-    const int qi = q0 + row;
+    const int qi = qbase + x * kFaBM + row;
     if (ok && qi < p.Sq) {
       const float inv = 1.0f / l_run;
       char* base = static_cast<char*>(p.o);
@@ -311,11 +374,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 // ---------------------------------------------------------------------------------------------
 // Host side.
 
-template <int DP, int DVP>
+template <int DP, int DVP, int NQ>
 struct FaCfg {
-  static constexpr int FIXED = kFaBM * DP * 2 + kFaBM * kFaBN * 2;
+  static constexpr int FIXED = NQ * (kFaBM * DP * 2 + kFaBM * kFaBN * 2);
   static constexpr int STAGE = kFaBN * (DP + DVP) * 2;
-  static constexpr int SMEM_MAX = 225 * 1024;
+  static constexpr int SMEM_MAX = 224 * 1024;
   static constexpr int STAGES_RAW = (SMEM_MAX - 2048 - FIXED) / STAGE;
   static constexpr int STAGES = STAGES_RAW > kFaMaxStages ? kFaMaxStages : STAGES_RAW;
   static constexpr int smem_bytes(int stages) { return FIXED + stages * STAGE + 2048; }
@@ -327,19 +390,19 @@ static int fa_map(CUtensorMap* m, int dtype, const void* base, int64_t B, int64_
   if (st[3] != 1) return fail(MT_ERR_UNSUPPORTED, "flash attention: head dim must be unit-stride");
   uint64_t dims[5] = {8, (uint64_t)S, (uint64_t)(D / 8), (uint64_t)Hx, (uint64_t)B};
   uint64_t strides[4] = {(uint64_t)st[2] * 2, 16, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  if (Hx == 1) strides[2] = 16;  // single head: any legal stride
+  if (B == 1) strides[3] = 16;   // single batch entry: any legal stride
   uint32_t box[5] = {8, 128, (uint32_t)box_chunks, 1, 1};
-  if (B == 1) strides[3] = strides[2] * (uint64_t)Hx + 16;  // unused dim: any legal stride
-  if (Hx == 1) strides[2] = 16;
   return make_tensor_map(m, dtype, 5, base, dims, strides, box, 0);
 }
 
-template <int DP, int DVP, bool F16>
+template <int DP, int DVP, int NQ, bool F16>
 static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
-  using Cfg = FaCfg<DP, DVP>;
+  using Cfg = FaCfg<DP, DVP, NQ>;
   const int stages = Cfg::STAGES;
   if (stages < 1) return fail(MT_ERR_UNSUPPORTED, "flash attention: head dim too large for shared memory");
   const int smem = Cfg::smem_bytes(stages) + 1024;
-  auto kern = fa_sm100_kernel<DP, DVP, F16>;
+  auto kern = fa_sm100_kernel<DP, DVP, NQ, F16>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -362,14 +425,29 @@ static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
   p.Dv = (int)d.Dv;
   p.out_dtype = d.dtype;
   p.stages = stages;
-  dim3 grid((unsigned)((d.Sq + kFaBM - 1) / kFaBM), (unsigned)(d.B * d.H));
-  kern<<<grid, kFaThreads, smem, st>>>(mq, mk, mv, p);
+  dim3 grid((unsigned)((d.Sq + kFaBM * NQ - 1) / (kFaBM * NQ)), (unsigned)(d.B * d.H));
+  kern<<<grid, 64 + 128 * NQ, smem, st>>>(mq, mk, mv, p);
   return check_launch("flash_attention_sm100");
 }
 
 size_t sdpa_tc_workspace(const mt_sdpa_desc&) { return 0; }
 
 static bool aligned16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <bool F16>
+static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, cudaStream_t st, bool* handled) {
+  // two query tiles per CTA when there are enough queries to fill them
+  const bool two = d.Sq > kFaBM;
+  *handled = true;
+  switch (Dp) {
+    case 48: return two ? fa_launch<48, 48, 2, F16>(d, st) : fa_launch<48, 48, 1, F16>(d, st);
+    case 64: return two ? fa_launch<64, 64, 2, F16>(d, st) : fa_launch<64, 64, 1, F16>(d, st);
+    case 80: return two ? fa_launch<80, 80, 2, F16>(d, st) : fa_launch<80, 80, 1, F16>(d, st);
+    case 128: return two ? fa_launch<128, 128, 2, F16>(d, st) : fa_launch<128, 128, 1, F16>(d, st);
+    case 160: return fa_launch<160, 160, 1, F16>(d, st);
+    default: *handled = false; return MT_OK;
+  }
+}
 
 int run_sdpa_tc(const mt_sdpa_desc& d, void*, size_t, cudaStream_t st, bool* handled) {
   *handled = false;
@@ -381,19 +459,8 @@ int run_sdpa_tc(const mt_sdpa_desc& d, void*, size_t, cudaStream_t st, bool* han
   for (int i = 0; i < 3; ++i)
     if ((d.q_strides[i] * 2) % 16 || (d.k_strides[i] * 2) % 16 || (d.v_strides[i] * 2) % 16) return MT_OK;
   if (d.q_strides[3] != 1 || d.k_strides[3] != 1 || d.v_strides[3] != 1) return MT_OK;
-  const bool f16 = d.dtype == MT_F16;
-  int rc;
   const int64_t Dp = (d.D + 15) / 16 * 16;
-  switch (Dp) {
-    case 48: rc = f16 ? fa_launch<48, 48, true>(d, st) : fa_launch<48, 48, false>(d, st); break;
-    case 64: rc = f16 ? fa_launch<64, 64, true>(d, st) : fa_launch<64, 64, false>(d, st); break;
-    case 80: rc = f16 ? fa_launch<80, 80, true>(d, st) : fa_launch<80, 80, false>(d, st); break;
-    case 128: rc = f16 ? fa_launch<128, 128, true>(d, st) : fa_launch<128, 128, false>(d, st); break;
-    case 160: rc = f16 ? fa_launch<160, 160, true>(d, st) : fa_launch<160, 160, false>(d, st); break;
-    default: return MT_OK;
-  }
-  *handled = true;
-  return rc;
+  return d.dtype == MT_F16 ? fa_dispatch<true>(d, Dp, st, handled) : fa_dispatch<false>(d, Dp, st, handled);
 }
 
 }  // namespace mt

@@ -285,7 +285,8 @@ def test_sdpa_fp32_golden(golden):
 
 
 @pytest.mark.parametrize("B,H,Sq,Sk,D", [(2, 8, 300, 300, 40), (2, 8, 256, 77, 40), (1, 8, 200, 200, 80),
-                                         (1, 8, 64, 77, 160), (2, 8, 1024, 1024, 40)])
+                                         (1, 8, 64, 77, 160), (2, 8, 1024, 1024, 40), (2, 8, 100, 100, 40),
+                                         (1, 4, 129, 130, 64), (1, 2, 256, 200, 128), (1, 2, 300, 257, 160)])
 def test_sdpa_bf16(B, H, Sq, Sk, D):
     q, k, v = rnd(B, H, Sq, D), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
     ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
