@@ -195,6 +195,7 @@ def run_ours(args):
 
     import mtorch_b200 as mt
     from mtorch_b200 import _lib, ops
+    from mtorch_b200.graphs import Graphed
     from mtorch_b200.unet import DDIM, UNet, timestep_embedding, unet_flops_per_sample
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -228,9 +229,15 @@ def run_ours(args):
     ctx = ctx_h.to(dev)
     stream = torch.cuda.current_stream()
 
+    # The UNet forward is captured once as a CUDA graph (static latent / time-embedding / context
+    # buffers); each step copies its inputs in, replays it and applies the fused DDIM update.
+    use_graph = not args.eager
+    graphed = Graphed(unet, x, temb_all[0], ctx) if use_graph else None
+
     def step(i, x):
         t = sched.timesteps[i % len(sched.timesteps)]
-        eps = unet(x, temb_all[i % len(temb_all)], ctx)
+        te = temb_all[i % len(temb_all)]
+        eps = graphed(x, te, ctx) if use_graph else unet(x, te, ctx)
         return sched.step(x, eps, t)
 
     for i in range(args.warmup):
@@ -246,6 +253,7 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
         n0 = lib.mt_cuda_launch_count()
+        r0 = graphed.replays if use_graph else 0
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(args.steps):
@@ -256,7 +264,10 @@ def run_ours(args):
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
+        # kernels launched directly + this library's kernels replayed inside the CUDA graph
         launches = lib.mt_cuda_launch_count() - n0
+        if use_graph:
+            launches += (graphed.replays - r0) * graphed.kernels_per_replay
     ms = e0.elapsed_time(e1)
     if dist:
         tt = torch.tensor([ms], device=dev)
@@ -278,11 +289,14 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
+    if use_graph:  # copy straight into the graph's static input buffers
+        xd, cd = graphed.static_in[0], graphed.static_in[2]
     for i in range(args.steps):
         lib.mt_cuda_memcpy(xd.data_ptr(), lat_pin.data_ptr(), h2d - ctx_pin.numel() * 2, 0, stream.cuda_stream)
         lib.mt_cuda_memcpy(cd.data_ptr(), ctx_pin.data_ptr(), ctx_pin.numel() * 2, 0, stream.cuda_stream)
         t = sched.timesteps[i % len(sched.timesteps)]
-        eps = unet(xd, temb_all[i % len(temb_all)], cd)
+        te = temb_all[i % len(temb_all)]
+        eps = graphed(xd, te, cd) if use_graph else unet(xd, te, cd)
         y = sched.step(xd, eps, t)
         lib.mt_cuda_memcpy(out_pin.data_ptr(), y.data_ptr(), d2h, 1, stream.cuda_stream)
         stream.synchronize()
@@ -345,6 +359,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--eager", action="store_true", help="launch the UNet op by op instead of replaying a CUDA graph")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -89,6 +89,23 @@ def test_ddim_step_matches_reference_formula():
     check(got, np.sqrt(a_p) * x0 + np.sqrt(1 - a_p) * e2, 1e-5)
 
 
+def test_cuda_graph_replay_matches_eager():
+    from mtorch_b200.graphs import Graphed
+
+    mt.manual_seed(0)
+    net = U.UNet(chans=(64, 128), attn=(True, False), layers=1, heads=2, ctx_dim=64, device="cuda", dtype="bfloat16")
+    rng = np.random.default_rng(5)
+    x = mt.tensor(rng.standard_normal((2, 4, 16, 16)).astype(np.float32), dtype="bfloat16").cuda()
+    ctx = mt.tensor(rng.standard_normal((2, 5, 64)).astype(np.float32), dtype="bfloat16").cuda()
+    te = mt.tensor(U.timestep_embedding(np.full(2, 300.0), 64), dtype="bfloat16").cuda()
+    g = Graphed(net, x, te, ctx)
+    assert g.kernels_per_replay > 50
+    eager = net(x, te, ctx).numpy()
+    np.testing.assert_array_equal(g(x, te, ctx).numpy(), eager)
+    x2 = mt.tensor(rng.standard_normal((2, 4, 16, 16)).astype(np.float32), dtype="bfloat16").cuda()
+    np.testing.assert_array_equal(g(x2, te, ctx).numpy(), net(x2, te, ctx).numpy())
+
+
 def test_tiny_unet_bf16_runs_and_is_batch_independent():
     mt.manual_seed(0)
     net = U.UNet(chans=(64, 128), attn=(True, False), layers=1, heads=2, ctx_dim=64, device="cuda", dtype="bfloat16")
