@@ -467,6 +467,21 @@ static int pick_bn(int64_t N, int kind, bool geglu, bool conv) {
   return best;
 }
 
+// Small problems (fewer tiles than SMs — the deep UNet levels at a few samples per GPU) use a
+// narrower column tile to spread over more SMs.  Each output element is still accumulated over
+// K in the same order, so results do not depend on the choice (batch invariance is kept).
+static int narrow_bn(int bn, int64_t N, int64_t m_tiles, bool geglu) {
+  const int64_t sms = num_sms();
+  auto tiles = [&](int c) { return m_tiles * ((N + c - 1) / c); };
+  const int cands[2] = {128, 64};
+  for (int c : cands) {
+    if (tiles(bn) >= sms) break;
+    if (c >= bn || (geglu && c % 128 != 0)) continue;
+    if (tiles(c) > tiles(bn)) bn = c;
+  }
+  return bn;
+}
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // 3-D K-major map: dims {K, rows, batch}, 128-byte-wide box of `box_rows` rows.
@@ -603,6 +618,7 @@ int run_gemm(const mt_gemm_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st)
   L.conv = false;
   const bool geglu = d.epilogue == MT_EPI_GEGLU;
   L.bn = pick_bn(d.N, d.dtype, geglu, false);
+  if (d.dtype != MT_F32) L.bn = narrow_bn(L.bn, d.N, (int64_t)((d.M + kBM - 1) / kBM) * d.batch, geglu);
   const int64_t a_b = p.a_batched ? d.batch : 1, b_b = p.b_batched ? d.batch : 1;
   rc = map_kmajor(&L.a, d.dtype, p.A, d.K, d.M, a_b, p.lda, p.sa, kBM);
   if (!rc) rc = map_kmajor(&L.b, d.dtype, p.B, d.K, d.N, b_b, p.ldb, p.sb, L.bn);
@@ -751,7 +767,6 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   tp.bk = 128 / es;
   tp.batch = 1;
   tp.a_batched = tp.b_batched = 0;
-  tp.num_n_tiles = (int)((d.K + L->bn - 1) / L->bn);
   int rc;
   if (implicit) {
     auto pow2_ge = [](int64_t v) {
@@ -782,6 +797,8 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
     rc = map_kmajor(&L->a, d.dtype, a, Kg, M, 1, Kg, 0, kBM);
     if (!rc && tf32) rc = map_kmajor(&L->alo, MT_F32, alo, Kg, M, 1, Kg, 0, kBM);
   }
+  if (!tf32) L->bn = narrow_bn(L->bn, d.K, tp.num_m_tiles, false);
+  tp.num_n_tiles = (int)((d.K + L->bn - 1) / L->bn);
   if (!rc) rc = map_kmajor(&L->b, d.dtype, wp, Kg, d.K, 1, Kg, 0, L->bn);
   if (!rc && tf32) rc = map_kmajor(&L->blo, MT_F32, wlo, Kg, d.K, 1, Kg, 0, L->bn);
   if (rc) return rc;

@@ -212,6 +212,17 @@ def test_bmm_bf16_attention_shapes():
     check(mt.bmm(cu(a, "bfloat16"), cu(b, "bfloat16")).numpy(), ref, BF16_RTOL)
 
 
+def test_small_problem_tiling_is_batch_invariant():
+    """Few-tile problems use narrower column tiles; results must not change with the batch."""
+    x = cu(rnd(16384, 1280), "bfloat16")
+    w = cu(rnd(1280, 1280, seed=1, scale=0.03), "bfloat16")
+    np.testing.assert_array_equal(mt.linear(x, w).numpy()[:256], mt.linear(x[:256], w).numpy())
+    xi = cu(rnd(32, 1280, 8, 8, seed=2), "bfloat16").contiguous(memory_format=mt.channels_last)
+    wc = cu(rnd(1280, 1280, 3, 3, seed=3, scale=0.01), "bfloat16")
+    full = mt.conv2d(xi, wc, None, 1, 1).numpy()
+    np.testing.assert_array_equal(full[:2], mt.conv2d(xi[:2], wc, None, 1, 1).numpy())
+
+
 def test_linear_batch_independent():
     x = cu(rnd(3000, 320), "bfloat16")
     w = cu(rnd(640, 320, seed=1, scale=0.05), "bfloat16")
