@@ -195,6 +195,7 @@ def run_ours(args):
 
     import mtorch_b200 as mt
     from mtorch_b200 import _lib, ops
+    from mtorch_b200 import parallel
     from mtorch_b200.graphs import Graphed
     from mtorch_b200.unet import DDIM, UNet, timestep_embedding, unet_flops_per_sample
 
@@ -204,12 +205,9 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
-    if BATCH % world:
-        raise SystemExit(f"batch {BATCH} does not shard over {world} GPUs")
-    nb = BATCH // world
+        dist = parallel.init("nccl", device_id=torch.device(f"cuda:{local}"))
+    lo, hi = parallel.shard(BATCH, world, rank)
+    nb = hi - lo
     dev = f"cuda:{local}"
     out_dir = ROOT / "gpurun_out"
     out_dir.mkdir(exist_ok=True)
@@ -220,8 +218,8 @@ def run_ours(args):
     mt.manual_seed(1)
     lat_all = mt.randn(BATCH, 4, H, W)
     ctx_all = mt.randn(BATCH, CTX, 768)
-    lat_h = lat_all[rank * nb:(rank + 1) * nb].to("bfloat16")
-    ctx_h = ctx_all[rank * nb:(rank + 1) * nb].to("bfloat16")
+    lat_h = lat_all[lo:hi].to("bfloat16")
+    ctx_h = ctx_all[lo:hi].to("bfloat16")
     sched = DDIM(steps=50)
     temb_all = [mt.tensor(timestep_embedding(np.full(nb, float(t))), dtype="bfloat16", device=dev)
                 for t in sched.timesteps]
@@ -243,7 +241,6 @@ def run_ours(args):
     for i in range(args.warmup):
         x = step(i, x)
     torch.cuda.synchronize()
-    gathered = torch.empty(BATCH * 4 * H * W * 2, dtype=torch.uint8, device=dev)
 
     # ---- device-timed region ----
     lib = _lib.lib()
@@ -259,7 +256,7 @@ def run_ours(args):
         for i in range(args.steps):
             x = step(args.warmup + i, x)
         if dist:
-            dist.all_gather_into_tensor(gathered, x.contiguous()._buf[:x.numel() * 2])
+            parallel.gather_shards(x.contiguous()._buf[:x.numel() * 2])  # output latents, all ranks
         e1.record(stream)
         torch.cuda.synchronize()
         if dist:
@@ -353,6 +350,51 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_kernel(args):
+    """One hot kernel alone at its level-0 UNet shape: `steps` timed launches after `warmup`,
+    CUDA events on torch's current stream.  Used for ncu captures of a single kernel."""
+    import torch
+
+    import mtorch_b200 as mt
+    from mtorch_b200 import _lib, ops
+
+    nb = args.batch
+    stream = torch.cuda.current_stream()
+    mt.manual_seed(0)
+    if args.kernel == "conv":
+        conv = mt.nn.Conv2d(320, 320, 3, padding=1, device="cuda", dtype="bfloat16")
+        x = mt.empty(nb, 320, H, W, dtype="bfloat16", device="cuda").uniform_(-1, 1).contiguous(
+            memory_format=mt.channels_last)
+        fn = lambda: conv(x)  # noqa: E731
+        flops = 2.0 * nb * H * W * 320 * 320 * 9
+        name = "implicit-GEMM conv 3x3 320->320 at 64x64"
+    elif args.kernel == "geglu":
+        x = mt.empty(nb * H * W, 320, dtype="bfloat16", device="cuda").uniform_(-1, 1)
+        w = mt.empty(2560, 320, dtype="bfloat16", device="cuda").uniform_(-0.05, 0.05)
+        fn = lambda: ops.linear(x, w, None, epilogue=_lib.EPI_GEGLU)  # noqa: E731
+        flops = 2.0 * nb * H * W * 320 * 2560
+        name = "GEGLU linear 320->2x1280 over 64x64 tokens"
+    else:
+        q, k, v = (mt.empty(nb, 8, H * W, 40, dtype="bfloat16", device="cuda").uniform_(-1, 1) for _ in range(3))
+        fn = lambda: mt.scaled_dot_product_attention(q, k, v)  # noqa: E731
+        flops = 4.0 * nb * 8 * (H * W) ** 2 * 40
+        name = "flash attention, 8 heads x 4096 tokens x 40"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    _, tf_burst, _, kind = peaks()
+    tflops = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({"kernel": name, "batch": nb, "ms_per_launch": ms, "tflops": tflops,
+                      "frac_of_bf16_peak": tflops / tf_burst, "peak_kind": kind}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -360,8 +402,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--eager", action="store_true", help="launch the UNet op by op instead of replaying a CUDA graph")
+    ap.add_argument("--kernel", choices=["conv", "attn", "geglu"], default=None,
+                    help="time one hot kernel alone at its UNet shape (for profiling), not the UNet")
+    ap.add_argument("--batch", type=int, default=BATCH, help="samples for --kernel runs")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
