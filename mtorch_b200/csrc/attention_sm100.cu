@@ -268,19 +268,22 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
       const uint32_t ts = tmem + slot * 128 + lane_off;
       const int kvalid = min(kFaBN, p.Sk - j * kFaBN);
       const bool full = kvalid == kFaBN;
+      // TMEM reads are issued 64 columns at a time before one tcgen05.wait::ld, so the load
+      // latency is paid twice per pass rather than once per 16 columns.
       // pass 1: row max of the raw scores (the scale is positive)
       float mx = -INFINITY;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kFaBN; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16_raw(ts + c0, r);
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
+        uint32_t r[64];
+        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
         if (full) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
+          for (int i = 0; i < 64; ++i)
             if (c0 + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
         }
       }
@@ -290,29 +293,35 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
       // pass 2: p = 2^(s * sl - m), packed row sums, P (bf16/f16) to shared memory
       uint64_t sum2 = f2_bits(0.f, 0.f);
 #pragma unroll 1
-      for (int c0 = 0; c0 < kFaBN; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16_raw(ts + c0, r);
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
+        uint32_t r[64];
+        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
-        uint32_t pk[8];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2, negm2);
-          float a0, a1;
-          f2_unpack(arg, a0, a1);
-          float e0 = ex2(a0), e1 = ex2(a1);
-          if (!full) {
-            if (c0 + i >= kvalid) e0 = 0.f;
-            if (c0 + i + 1 >= kvalid) e1 = 0.f;
+        for (int q = 0; q < 4; ++q) {  // 16 keys -> two 16-byte P chunks
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const int k = q * 16 + i;
+            const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[k]), __uint_as_float(r[k + 1])), sl2, negm2);
+            float a0, a1;
+            f2_unpack(arg, a0, a1);
+            float e0 = ex2(a0), e1 = ex2(a1);
+            if (!full) {
+              if (c0 + k >= kvalid) e0 = 0.f;
+              if (c0 + k + 1 >= kvalid) e1 = 0.f;
+            }
+            sum2 = fadd2(sum2, f2_bits(e0, e1));
+            pk[i / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
           }
-          sum2 = fadd2(sum2, f2_bits(e0, e1));
-          pk[i / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+          // keys c..c+7 -> chunk c/8, keys c+8..c+15 -> chunk c/8+1; this row at +row*16
+          const int c = c0 + q * 16;
+          uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
+          uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
+          *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
-        // keys c0..c0+7 -> chunk c0/8, keys c0+8..c0+15 -> chunk c0/8+1; this row at +row*16
-        uint4* d0 = reinterpret_cast<uint4*>(sPx + (c0 / 8) * (kFaBM * 16) + row * 16);
-        uint4* d1 = reinterpret_cast<uint4*>(sPx + (c0 / 8 + 1) * (kFaBM * 16) + row * 16);
-        *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[slot]);
@@ -329,12 +338,20 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
       }
       tc_fence_after();
 #pragma unroll
-      for (int c0 = 0; c0 < DVP; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16_raw(t_o + c0, r);
-        tmem_ld_wait();
+      for (int c0 = 0; c0 < DVP; c0 += 32) {
+        if (c0 + 32 <= DVP) {
+          uint32_t r[32];
+          tmem_ld32(t_o + c0, r);
+          tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o_acc[c0 + i] = fmaf(o_acc[c0 + i], corr, __uint_as_float(r[i]));
+          for (int i = 0; i < 32; ++i) o_acc[c0 + i] = fmaf(o_acc[c0 + i], corr, __uint_as_float(r[i]));
+        } else {
+          uint32_t r[16];
+          tmem_ld16_raw(t_o + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o_acc[c0 + i] = fmaf(o_acc[c0 + i], corr, __uint_as_float(r[i]));
+        }
       }
       tc_fence_before();
       mbar_arrive(&o_empty[x]);
