@@ -450,6 +450,13 @@ static int dispatch(const GemmLaunch& L, cudaStream_t st) {
 // implicit conv with fp32 use 128.
 static int pick_bn(int64_t N, int kind, bool geglu, bool conv) {
   if (kind == MT_F32) return (N <= 64 && !geglu && !conv) ? 64 : 128;
+  // Tuning knob: MT_GEMM_BN=<64|128|160|256> forces the column tile of bf16/f16 GEMMs.
+  static const int forced = [] {
+    const char* e = getenv("MT_GEMM_BN");
+    const int v = e ? atoi(e) : 0;
+    return (v == 64 || v == 128 || v == 160 || v == 256) ? v : 0;
+  }();
+  if (forced && !(geglu && forced % 128)) return forced;
   if (geglu) return N % 256 == 0 ? 256 : 128;
   const int cands[4] = {256, 160, 128, 64};
   for (int c : cands)
