@@ -45,6 +45,7 @@ struct EpiParams {
   const void* bias; int bias_dtype; int64_t bias_bstride;
   float alpha; int act;
   int vec_ok;  // 16-byte aligned rows of D / C / residual
+  int bias_vec;  // bias rows 16-byte aligned and bf16 / fp32: vector loads
 };
 
 // 32 consecutive values of one row: load (accumulate scale*x into v) / store, runtime dtype.
@@ -331,7 +332,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
-            if (ep.bias) row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, false, 1.f, v);
+            if (ep.bias)
+              row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, ep.bias_vec != 0, 1.f, v);
             if (ep.C) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
             if (ep.act == MT_EPI_GELU) {
 #pragma unroll
@@ -367,8 +369,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 gt[j] = ep.alpha * __uint_as_float(rg[j]);
               }
               if (ep.bias) {
-                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v, nvalid, false, 1.f, v);
-                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v + 64, nvalid, false, 1.f, gt);
+                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v, nvalid, ep.bias_vec != 0, 1.f, v);
+                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v + 64, nvalid, ep.bias_vec != 0, 1.f,
+                             gt);
               }
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = v[j] * gelu_f(gt[j]);
@@ -490,6 +493,11 @@ static int narrow_bn(int bn, int64_t N, int64_t m_tiles, bool geglu) {
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int bias_vec_ok(const void* bias, int dtype, int64_t bstride) {
+  if (!bias || (dtype != MT_BF16 && dtype != MT_F32)) return 0;
+  return aligned16(bias) && (bstride * dtype_size(dtype)) % 16 == 0;
+}
 
 // 3-D K-major map: dims {K, rows, batch}, 128-byte-wide box of `box_rows` rows.
 static int map_kmajor(CUtensorMap* m, int dtype, const void* base, int64_t K, int64_t rows, int64_t batch,
@@ -660,6 +668,7 @@ int run_gemm(const mt_gemm_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st)
   if (ep.res)
     vec = vec && aligned16(d.residual) && (d.ldr * oes) % 16 == 0 && (d.batch == 1 || (d.stride_r * oes) % 16 == 0);
   ep.vec_ok = vec;
+  ep.bias_vec = bias_vec_ok(d.bias, d.bias_dtype, d.bias_batch_stride);
   return dispatch(L, st);
 }
 
@@ -826,6 +835,7 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   ep.alpha = 1.f; ep.act = d.epilogue;
   const int oes = dtype_size(d.out_dtype);
   ep.vec_ok = aligned16(yout) && (d.K * oes) % 16 == 0 && (!res || aligned16(res));
+  ep.bias_vec = bias_vec_ok(d.bias, d.bias_dtype, d.bias_batch_stride);
   return MT_OK;
 }
 
