@@ -115,68 +115,6 @@ __device__ __forceinline__ void row_store(void* p, int dtype, int64_t off, int n
     if (j < nvalid) store_from_f32(p, off + j, dtype, v[j]);
 }
 
-// Stores one warp's 32 rows x 32 columns (lane r holds row r in v) through shared memory so that
-// global accesses are row-contiguous: after the exchange, 8 lanes cover one row's 32 columns
-// (4 columns each), adding the residual on the way.  The staging tile is XOR-swizzled in 16-byte
-// units so both the row-per-lane writes and the 8-lanes-per-row reads are bank-conflict free.
-// Every lane of the warp must call it (shuffles); per-row validity is honoured inside.
-__device__ __forceinline__ void store_chunk_staged(float* stg, const float (&v)[32], int lane, bool valid,
-                                                   int64_t offD, int64_t offR, int nvalid, const EpiParams& ep) {
-  float4* s4 = reinterpret_cast<float4*>(stg);
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    s4[lane * 8 + (i ^ (lane & 7))] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-  __syncwarp();
-  const int sub = lane & 7;
-  const int c = sub * 4;
-#pragma unroll 1
-  for (int it = 0; it < 8; ++it) {
-    const int r = it * 4 + (lane >> 3);
-    const int rvalid = __shfl_sync(0xffffffffu, valid ? 1 : 0, r);
-    const int64_t od = __shfl_sync(0xffffffffu, offD, r) + c;   // this lane's 4 columns of row r
-    const int64_t orr = __shfl_sync(0xffffffffu, offR, r) + c;
-    float4 f = s4[r * 8 + (sub ^ (r & 7))];
-    if (!rvalid || c >= nvalid) continue;
-    float o[4] = {f.x, f.y, f.z, f.w};
-    const int n4 = nvalid - c < 4 ? nvalid - c : 4;
-    if (n4 == 4) {
-      if (ep.res) {
-        if (ep.out_dtype == MT_F32) {
-          const float4 q = *reinterpret_cast<const float4*>(static_cast<const float*>(ep.res) + orr);
-          o[0] += q.x; o[1] += q.y; o[2] += q.z; o[3] += q.w;
-        } else {
-          const uint2 q = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(ep.res) + orr);
-          const uint32_t w[2] = {q.x, q.y};
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            float2 t;
-            if (ep.out_dtype == MT_BF16) t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-            else t = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
-            o[2 * k] += t.x;
-            o[2 * k + 1] += t.y;
-          }
-        }
-      }
-      if (ep.out_dtype == MT_F32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(ep.D) + od) = make_float4(o[0], o[1], o[2], o[3]);
-      } else if (ep.out_dtype == MT_BF16) {
-        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ep.D) + od) =
-            make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
-      } else {
-        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ep.D) + od) =
-            make_uint2(pack_f16x2(o[0], o[1]), pack_f16x2(o[2], o[3]));
-      }
-    } else {
-      for (int k = 0; k < n4; ++k) {
-        float t = o[k];
-        if (ep.res) t += load_as_f32(ep.res, orr + k, ep.out_dtype);
-        store_from_f32(ep.D, od + k, ep.out_dtype, t);
-      }
-    }
-  }
-  __syncwarp();
-}
-
 __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b, int& mt, int& nt) {
   nt = t % tp.num_n_tiles;
   const int rest = t / tp.num_n_tiles;
@@ -197,8 +135,7 @@ struct GemmCfg {
                                    : (2 * BN <= 128) ? 128
                                    : (2 * BN <= 256) ? 256
                                                      : 512;
-  static constexpr int EPI_STAGE_BYTES = 8 * 32 * 32 * 4;  // one 32x32 fp32 chunk per epilogue warp
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 template <int BN, bool TF32, bool CONV>
@@ -216,7 +153,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* epi_stage = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -383,7 +319,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int64_t offR = i0 * ep.r_s0 + i1 * ep.r_s1 + i2 * ep.r_s2;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
       const bool vec = ep.vec_ok != 0;
-      float* stg = epi_stage + (warp - 2) * (32 * 32);
       if (!geglu) {
 #pragma unroll 1
         for (int c0 = half * 32; c0 < BN; c0 += 64) {
@@ -393,15 +328,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int64_t col0 = (int64_t)nt * BN + c0;
           const int64_t remain = n_out - col0;
           const int nvalid = remain < 32 ? (int)remain : 32;
-          if (nvalid > 0) {  // warp-uniform
+          if (valid && nvalid > 0) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
-            if (valid) {
-              if (ep.bias)
-                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, ep.bias_vec != 0, 1.f, v);
-              if (ep.C) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
-            }
+            if (ep.bias)
+              row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, ep.bias_vec != 0, 1.f, v);
+            if (ep.C) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
             if (ep.act == MT_EPI_GELU) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = gelu_f(v[j]);
@@ -409,12 +342,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
             }
-            if (vec) {
-              store_chunk_staged(stg, v, lane, valid, offD + col0, offR + col0, nvalid, ep);
-            } else if (valid) {
-              if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
-              row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
-            }
+            if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
+            row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
           }
         }
       } else {
@@ -422,32 +351,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // 64 their gates; output column = nt*BN/2 + g*64 + j.
 #pragma unroll 1
         for (int g = 0; g < BN / 128; ++g) {
-          const int h = half * 32;
-          uint32_t rv[32], rg[32];
-          tmem_ld32(taddr + g * 128 + h, rv);
-          tmem_ld32(taddr + g * 128 + 64 + h, rg);
-          tmem_ld_wait();
-          const int64_t gcol_v = (int64_t)nt * BN + g * 128 + h;
-          const int64_t col0 = (int64_t)nt * (BN / 2) + g * 64 + h;
-          const int64_t remain = n_out - col0;
-          const int nvalid = remain < 32 ? (int)remain : 32;
-          if (nvalid > 0) {  // warp-uniform
-            float v[32], gt[32];
+          {
+            const int h = half * 32;
+            uint32_t rv[32], rg[32];
+            tmem_ld32(taddr + g * 128 + h, rv);
+            tmem_ld32(taddr + g * 128 + 64 + h, rg);
+            tmem_ld_wait();
+            const int64_t gcol_v = (int64_t)nt * BN + g * 128 + h;
+            const int64_t col0 = (int64_t)nt * (BN / 2) + g * 64 + h;
+            const int64_t remain = n_out - col0;
+            const int nvalid = remain < 32 ? (int)remain : 32;
+            if (valid && nvalid > 0) {
+              float v[32], gt[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              v[j] = ep.alpha * __uint_as_float(rv[j]);
-              gt[j] = ep.alpha * __uint_as_float(rg[j]);
-            }
-            if (valid && ep.bias) {
-              row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v, nvalid, ep.bias_vec != 0, 1.f, v);
-              row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v + 64, nvalid, ep.bias_vec != 0, 1.f,
-                           gt);
-            }
+              for (int j = 0; j < 32; ++j) {
+                v[j] = ep.alpha * __uint_as_float(rv[j]);
+                gt[j] = ep.alpha * __uint_as_float(rg[j]);
+              }
+              if (ep.bias) {
+                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v, nvalid, ep.bias_vec != 0, 1.f, v);
+                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v + 64, nvalid, ep.bias_vec != 0, 1.f,
+                             gt);
+              }
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = v[j] * gelu_f(gt[j]);
-            if (vec) {
-              store_chunk_staged(stg, v, lane, valid, offD + col0, offR + col0, nvalid, ep);
-            } else if (valid) {
+              for (int j = 0; j < 32; ++j) v[j] = v[j] * gelu_f(gt[j]);
               if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
               row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
             }
