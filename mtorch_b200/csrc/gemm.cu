@@ -322,52 +322,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!geglu) {
 #pragma unroll 1
         for (int c0 = half * 32; c0 < BN; c0 += 64) {
-          const int64_t col0 = (int64_t)nt * BN + c0;
-          const int64_t remain = n_out - col0;
-          const int nvalid = remain < 32 ? (int)remain : 32;
-          // Issue this chunk's global reads (16-bit residual, bias) before waiting on TMEM so their
-          // latency overlaps the accumulator load.
-          uint4 resq[4], biasq[8];
-          const bool pre_res = ep.res && vec && valid && nvalid == 32 && ep.out_dtype != MT_F32;
-          const bool pre_bias = ep.bias && ep.bias_vec && valid && nvalid == 32;
-          if (pre_res) {
-            const uint4* q = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(ep.res) + offR + col0);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) resq[i] = q[i];
-          }
-          if (pre_bias) {
-            const char* bp = static_cast<const char*>(ep.bias) +
-                             (i0 * ep.bias_bstride + col0) * (ep.bias_dtype == MT_F32 ? 4 : 2);
-            const uint4* q = reinterpret_cast<const uint4*>(bp);
-            const int nq = ep.bias_dtype == MT_F32 ? 8 : 4;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (i < nq) biasq[i] = q[i];
-          }
           uint32_t r[32];
           tmem_ld32(taddr + c0, r);
           tmem_ld_wait();
+          const int64_t col0 = (int64_t)nt * BN + c0;
+          const int64_t remain = n_out - col0;
+          const int nvalid = remain < 32 ? (int)remain : 32;
           if (valid && nvalid > 0) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
-            if (pre_bias) {
-              if (ep.bias_dtype == MT_F32) {
-                const float* f = reinterpret_cast<const float*>(biasq);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] += f[j];
-              } else {
-                const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(biasq);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const float2 f = __bfloat1622float2(hb[j]);
-                  v[2 * j] += f.x;
-                  v[2 * j + 1] += f.y;
-                }
-              }
-            } else if (ep.bias) {
+            if (ep.bias)
               row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, ep.bias_vec != 0, 1.f, v);
-            }
             if (ep.C) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
             if (ep.act == MT_EPI_GELU) {
 #pragma unroll
@@ -376,18 +342,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
             }
-            if (pre_res) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const uint32_t w = reinterpret_cast<const uint32_t*>(resq)[j];
-                const float2 f = ep.out_dtype == MT_BF16 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w))
-                                                         : __half22float2(*reinterpret_cast<const __half2*>(&w));
-                v[2 * j] += f.x;
-                v[2 * j + 1] += f.y;
-              }
-            } else if (ep.res) {
-              row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
-            }
+            if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
             row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
           }
         }
