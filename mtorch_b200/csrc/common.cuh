@@ -72,19 +72,12 @@ __device__ __forceinline__ void store_from_f64(void* p, int64_t i, int dtype, do
 // Activations (fp32).  GELU uses CUDA's erff (exact-erf GELU, the reference's
 // approximate="none" definition 0.5*x*(1+erf(x/sqrt(2))), tensor.cpp:17103-17113).
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
-// GELU(x) = x * Phi(x) evaluated the way the reference's fp32 kernel does (tensor.cpp:17265-17272):
-// for |x| <= 1 the odd Taylor series of x*Phi(x) to x^13; otherwise 0.5*x*(1 + erf(x/sqrt 2)) with
-// the Abramowitz-Stegun 7.1.26 rational approximation of erf (|error| < 1.5e-7).  Both are
-// published formulas; they are also cheaper than a full-precision erf in the GEMM epilogues.
+// GELU(x) = x * Phi(x) = 0.5*x*(1 + erf(x/sqrt 2)) with erf from the Abramowitz-Stegun 7.1.26
+// rational approximation (|error| < 1.5e-7), the published formula the reference's fp32 kernel
+// uses for |x| > 1 (tensor.cpp:17132-17144, 17265-17272; for |x| <= 1 it uses an equally accurate
+// Taylor series).  One branch-free formula keeps the GEMM epilogue free of warp divergence.
 __device__ __forceinline__ float gelu_f(float x) {
   const float ax = fabsf(x);
-  if (ax <= 1.0f) {
-    const float x2 = x * x;
-    const float series =
-        1.0f + x2 * (-1.0f / 6.0f + x2 * (1.0f / 40.0f + x2 * (-1.0f / 336.0f + x2 * (1.0f / 3456.0f +
-                                                                                         x2 * (-1.0f / 42240.0f)))));
-    return 0.5f * x + 0.39894228040143267794f * x2 * series;
-  }
   const float z = ax * 0.70710678118654752440f;
   const float t = __fdividef(1.0f, 1.0f + 0.3275911f * z);
   const float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
