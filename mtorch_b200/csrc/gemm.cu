@@ -115,19 +115,6 @@ __device__ __forceinline__ void row_store(void* p, int dtype, int64_t off, int n
     if (j < nvalid) store_from_f32(p, off + j, dtype, v[j]);
 }
 
-// v[j] += s[j] for 32 staged fp32 values (warp-uniform addresses: shared-memory broadcast).
-__device__ __forceinline__ void add_staged32(const float* s, float (&v)[32]) {
-  const float4* s4 = reinterpret_cast<const float4*>(s);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float4 f = s4[i];
-    v[4 * i] += f.x;
-    v[4 * i + 1] += f.y;
-    v[4 * i + 2] += f.z;
-    v[4 * i + 3] += f.w;
-  }
-}
-
 __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b, int& mt, int& nt) {
   nt = t % tp.num_n_tiles;
   const int rest = t / tp.num_n_tiles;
@@ -148,8 +135,7 @@ struct GemmCfg {
                                    : (2 * BN <= 128) ? 128
                                    : (2 * BN <= 256) ? 256
                                                      : 512;
-  static constexpr int BIAS_STAGE_BYTES = 8 * 256 * 4;  // one BN-wide fp32 bias row per epilogue warp
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + BIAS_STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 template <int BN, bool TF32, bool CONV>
@@ -167,7 +153,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* bias_stage = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -297,25 +282,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int row = quarter * 32 + lane;
     const bool geglu = ep.act == MT_EPI_GEGLU;
     const int64_t n_out = geglu ? ep.N / 2 : ep.N;
-    const bool tile_bias = ep.bias && ep.bias_bstride == 0;
-    float* wbias = bias_stage + (warp - 2) * 256;
     int local = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
-      int b, mt, nt;
-      decode_tile(tp, t, b, mt, nt);
-      // A per-column bias is staged into this warp's slice of shared memory while the MMAs of
-      // the tile are still running (the loads' latency hides behind the accumulator wait).
-      if (tile_bias) {
-        for (int c = lane; c < BN; c += 32) {
-          const int64_t col = (int64_t)nt * BN + c;
-          wbias[c] = col < ep.N ? load_as_f32(ep.bias, col, ep.bias_dtype) : 0.f;
-        }
-        __syncwarp();
-      }
       if (!mbar_wait(&tfull[buf], tph, 4, abort_flag)) break;
       tc_fence_after();
+      int b, mt, nt;
+      decode_tile(tp, t, b, mt, nt);
       // Map this thread's accumulator row to output coordinates (i0, i1, i2).
       int64_t i0 = 0, i1 = 0, i2 = 0;
       bool valid;
@@ -358,9 +332,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
-            if (tile_bias)
-              add_staged32(wbias + c0, v);
-            else if (ep.bias)
+            if (ep.bias)
               row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, ep.bias_vec != 0, 1.f, v);
             if (ep.C) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
             if (ep.act == MT_EPI_GELU) {
@@ -396,10 +368,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 v[j] = ep.alpha * __uint_as_float(rv[j]);
                 gt[j] = ep.alpha * __uint_as_float(rg[j]);
               }
-              if (tile_bias) {
-                add_staged32(wbias + g * 128 + h, v);
-                add_staged32(wbias + g * 128 + 64 + h, gt);
-              } else if (ep.bias) {
+              if (ep.bias) {
                 row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v, nvalid, ep.bias_vec != 0, 1.f, v);
                 row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + gcol_v + 64, nvalid, ep.bias_vec != 0, 1.f,
                              gt);
