@@ -389,6 +389,316 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// Variant for small head dims (D <= 64) with the output kept in TMEM across KV tiles.
+//
+// Same roles and two query tiles per CTA, but the PV products accumulate into O in TMEM and the
+// running max is only raised when a row's new maximum exceeds the one in use by more than 2^8
+// ("lazy rescale"): p = 2^(s*scale*log2e - m_used) then stays <= 256, exact enough in bf16 / fp32.
+// A rescale (rare after the first tile) waits for the previous PV, multiplies the row of O in
+// TMEM and continues.  P is double-buffered in shared memory, so a softmax warpgroup never waits
+// for its previous PV product — only for the S tile it consumes.
+constexpr float kLazyThreshold = 8.0f;  // log2 of the largest p allowed before rescaling
+
+template <int DP, int DVP, bool F16>
+__global__ void __launch_bounds__(320, 1)
+    fa_lazy_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+  constexpr int NQ = 2;
+  constexpr int Q_BYTES = kFaBM * DP * 2;
+  constexpr int K_BYTES = kFaBN * DP * 2;
+  constexpr int V_BYTES = kFaBN * DVP * 2;
+  constexpr int P_BYTES = kFaBM * kFaBN * 2;
+  constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+  constexpr uint32_t kLbo = kFaBM * 16;
+  constexpr uint32_t kSbo = 128;
+  constexpr int FMT = F16 ? 0 : 1;
+  constexpr uint32_t idesc_s = make_idesc(FMT, kFaBM, kFaBN);
+  constexpr uint32_t idesc_o = make_idesc(FMT, kFaBM, DVP) | (1u << 16);
+  static_assert(2 * 128 + 2 * DVP <= 512, "TMEM budget");
+
+  extern __shared__ uint8_t fa_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                    // [2][Q]
+  uint8_t* sP = sQ + NQ * Q_BYTES;       // [2 tiles][2 buffers][P]
+  uint8_t* sKV = sP + NQ * 2 * P_BYTES;  // [stages][K, V]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + p.stages * STAGE_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kFaMaxStages;
+  uint64_t* s_full = kv_empty + kFaMaxStages;  // [2]
+  uint64_t* s_empty = s_full + 2;              // [2]
+  uint64_t* p_full = s_empty + 2;              // [2]
+  uint64_t* p_free = p_full + 2;               // [2 tiles][2 buffers]
+  uint64_t* o_done = p_free + 4;               // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int stages = p.stages;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / (p.H / p.Hkv);
+  const int qbase = blockIdx.x * (kFaBM * NQ);
+  const int n_tiles = (p.Sk + kFaBN - 1) / kFaBN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) mbar_init(&p_free[i], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_o0 = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, NQ * Q_BYTES);
+      for (int x = 0; x < NQ; ++x) tma_load_5d(sQ + x * Q_BYTES, &tmQ, q_full, 0, qbase + x * kFaBM, 0, h, b);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1, 21, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[stage], STAGE_BYTES);
+        uint8_t* sk = sKV + stage * STAGE_BYTES;
+        tma_load_5d(sk, &tmK, &kv_full[stage], 0, j * kFaBN, 0, hk, b);
+        tma_load_5d(sk + K_BYTES, &tmV, &kv_full[stage], 0, j * kFaBN, 0, hk, b);
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, 22, abort_flag);
+      int stage = 0, prev_stage = 0;
+      uint32_t phase = 0;
+      for (int j = 0; ok && j <= n_tiles; ++j) {
+        if (j < n_tiles) {
+          if (!mbar_wait(&kv_full[stage], phase, 23, abort_flag)) break;
+          const uint32_t k_addr = smem_u32(sKV + stage * STAGE_BYTES);
+          bool sok = true;
+          for (int x = 0; x < NQ && sok; ++x) {
+            if (!mbar_wait(&s_empty[x], (j & 1) ^ 1, 24, abort_flag)) {
+              sok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t qa = q_addr + x * Q_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < DP / 16; ++kk)
+              umma_f16(tmem + x * 128, sdesc_none(qa + kk * 2 * kLbo, kLbo, kSbo),
+                       sdesc_none(k_addr + kk * 2 * kLbo, kLbo, kSbo), idesc_s, kk > 0 ? 1u : 0u);
+            umma_commit(&s_full[x]);
+          }
+          if (!sok) break;
+        }
+        if (j > 0) {
+          const int jj = j - 1;
+          const uint32_t v_addr = smem_u32(sKV + prev_stage * STAGE_BYTES + K_BYTES);
+          bool pok = true;
+          for (int x = 0; x < NQ; ++x) {
+            if (!mbar_wait(&p_full[x], jj & 1, 25, abort_flag)) {
+              pok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t pa = p_addr + (x * 2 + (jj & 1)) * P_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < kFaBN / 16; ++kk)
+              umma_f16(t_o0 + x * DVP, sdesc_none(pa + kk * 2 * kLbo, kLbo, kSbo),
+                       sdesc_none(v_addr + kk * 256, 128, kFaBN * 16), idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&p_free[x * 2 + (jj & 1)]);
+            umma_commit(&o_done[x]);
+          }
+          if (!pok) break;
+          umma_commit(&kv_empty[prev_stage]);
+        }
+        if (j < n_tiles) {
+          prev_stage = stage;
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else {
+    const int x = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t t_o = t_o0 + x * DVP + lane_off;
+    const uint32_t ts = tmem + x * 128 + lane_off;
+    float m_used = -INFINITY, l_run = 0.f;
+    const float sl = p.scale_log2;
+    const uint64_t sl2 = f2_bits(sl, sl);
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (!mbar_wait(&s_full[x], j & 1, 26, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kvalid = min(kFaBN, p.Sk - j * kFaBN);
+      const bool full = kvalid == kFaBN;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
+        uint32_t r[64];
+        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld_wait();
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (c0 + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
+      }
+      const float mt = mx * sl;
+      if (j == 0) {
+        m_used = mt;
+      } else {
+        const bool need = mt > m_used + kLazyThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          // O holds the sum over the previous tiles: wait for the last PV, then rescale in TMEM
+          const float m_new = need ? mt : m_used;
+          const float corr = ex2(m_used - m_new);
+          if (!mbar_wait(&o_done[x], (j - 1) & 1, 27, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c0 = 0; c0 < DVP; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16_raw(t_o + c0, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+            tmem_st16(t_o + c0, r);
+          }
+          tmem_st_wait();
+          l_run *= corr;
+          m_used = m_new;
+        }
+      }
+      // the P buffer this tile writes was read by the PV two tiles back
+      if (!mbar_wait(&p_free[x * 2 + (j & 1)], ((j >> 1) & 1) ^ 1, 28, abort_flag)) {
+        ok = false;
+        break;
+      }
+      uint8_t* sPx = sP + (x * 2 + (j & 1)) * P_BYTES;
+      const uint64_t negm2 = f2_bits(-m_used, -m_used);
+      uint64_t sum2 = f2_bits(0.f, 0.f);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
+        uint32_t r[64];
+        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const int k = q * 16 + i;
+            const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[k]), __uint_as_float(r[k + 1])), sl2, negm2);
+            float a0, a1;
+            f2_unpack(arg, a0, a1);
+            float e0 = ex2(a0), e1 = ex2(a1);
+            if (!full) {
+              if (c0 + k >= kvalid) e0 = 0.f;
+              if (c0 + k + 1 >= kvalid) e1 = 0.f;
+            }
+            sum2 = fadd2(sum2, f2_bits(e0, e1));
+            pk[i / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+          }
+          const int c = c0 + q * 16;
+          uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
+          uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
+          *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[x]);
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[x]);
+      float s0, s1;
+      f2_unpack(sum2, s0, s1);
+      l_run += s0 + s1;
+    }
+    // final: O (all PV products accumulated) / l
+    if (ok && mbar_wait(&o_done[x], (n_tiles - 1) & 1, 29, abort_flag)) {
+      tc_fence_after();
+      float o[DVP];
+#pragma unroll
+      for (int c0 = 0; c0 < DVP; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16_raw(t_o + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[c0 + i] = __uint_as_float(r[i]);
+      }
+      const int qi = qbase + x * kFaBM + row;
+      if (qi < p.Sq) {
+        const float inv = 1.0f / l_run;
+        char* base = static_cast<char*>(p.o);
+        const int64_t off = (int64_t)b * p.os[0] + (int64_t)h * p.os[1] + (int64_t)qi * p.os[2];
+        if (p.os[3] == 1 && (p.Dv % 8) == 0 && ((reinterpret_cast<uintptr_t>(base) + off * 2) % 16) == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(base + off * 2);
+#pragma unroll
+          for (int c = 0; c < DVP; c += 8) {
+            if (c < p.Dv) {
+              uint32_t w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                w[i] = F16 ? pack_f16x2(o[c + 2 * i] * inv, o[c + 2 * i + 1] * inv)
+                           : pack_bf16x2(o[c + 2 * i] * inv, o[c + 2 * i + 1] * inv);
+              dst[c / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < DVP; ++c)
+            if (c < p.Dv) store_from_f32(p.o, off + (int64_t)c * p.os[3], p.out_dtype, o[c] * inv);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host side.
 
 template <int DP, int DVP, int NQ>
@@ -447,6 +757,46 @@ static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
   return check_launch("flash_attention_sm100");
 }
 
+// Launch of the lazy-rescale variant; returns false (not launched) when two KV stages do not fit.
+template <int DP, int DVP, bool F16>
+static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched) {
+  constexpr int FIXED = 2 * (kFaBM * DP * 2 + 2 * kFaBM * kFaBN * 2);
+  constexpr int STAGE = kFaBN * (DP + DVP) * 2;
+  constexpr int SMEM_MAX = 224 * 1024;
+  int stages = (SMEM_MAX - 2048 - FIXED) / STAGE;
+  if (stages > kFaMaxStages) stages = kFaMaxStages;
+  *launched = false;
+  if (stages < 2) return MT_OK;
+  const int smem = FIXED + stages * STAGE + 2048 + 1024;
+  auto kern = fa_lazy_sm100_kernel<DP, DVP, F16>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                        "flash attention smem attribute");
+    if (rc) return rc;
+    attr[dev & 63] = true;
+  }
+  CUtensorMap mq, mk, mv;
+  int rc = fa_map(&mq, d.dtype, d.q, d.B, d.H, d.Sq, d.D, d.q_strides, DP / 8);
+  if (!rc) rc = fa_map(&mk, d.dtype, d.k, d.B, d.Hkv, d.Sk, d.D, d.k_strides, DP / 8);
+  if (!rc) rc = fa_map(&mv, d.dtype, d.v, d.B, d.Hkv, d.Sk, d.Dv, d.v_strides, DVP / 8);
+  if (rc) return rc;
+  FaParams p{};
+  p.Sq = (int)d.Sq; p.Sk = (int)d.Sk; p.H = (int)d.H; p.Hkv = (int)d.Hkv; p.B = (int)d.B;
+  p.scale_log2 = (float)(d.scale * 1.4426950408889634);
+  p.o = d.o;
+  for (int i = 0; i < 4; ++i) p.os[i] = d.o_strides[i];
+  p.Dv = (int)d.Dv;
+  p.out_dtype = d.dtype;
+  p.stages = stages;
+  dim3 grid((unsigned)((d.Sq + 2 * kFaBM - 1) / (2 * kFaBM)), (unsigned)(d.B * d.H));
+  kern<<<grid, 320, smem, st>>>(mq, mk, mv, p);
+  *launched = true;
+  return check_launch("flash_attention_lazy_sm100");
+}
+
 size_t sdpa_tc_workspace(const mt_sdpa_desc&) { return 0; }
 
 static bool aligned16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -456,6 +806,11 @@ static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, cudaStream_t st, bool*
   // two query tiles per CTA when there are enough queries to fill them
   const bool two = d.Sq > kFaBM;
   *handled = true;
+  if (two && Dp == 48 && !getenv("MT_FA_NO_LAZY")) {
+    bool launched = false;
+    const int rc = fa_lazy_launch<48, 48, F16>(d, st, &launched);
+    if (rc || launched) return rc;
+  }
   switch (Dp) {
     case 48: return two ? fa_launch<48, 48, 2, F16>(d, st) : fa_launch<48, 48, 1, F16>(d, st);
     case 64: return two ? fa_launch<64, 64, 2, F16>(d, st) : fa_launch<64, 64, 1, F16>(d, st);

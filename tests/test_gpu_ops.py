@@ -305,6 +305,19 @@ def test_sdpa_bf16(B, H, Sq, Sk, D):
     check(got, ref, BF16_RTOL)
 
 
+def test_sdpa_bf16_growing_scores_rescale():
+    """Later key tiles score much higher than earlier ones, so the running maximum grows by far more
+    than the lazy-rescale threshold several times within a row."""
+    B, H, S, D = 2, 4, 640, 40
+    q = rnd(B, H, S, D, scale=2.0)
+    k = rnd(B, H, S, D, seed=1)
+    k *= (1.0 + np.repeat(np.arange(S // 128), 128) * 1.5)[None, None, :, None].astype(np.float32)
+    v = rnd(B, H, S, D, seed=2)
+    ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
+    got = mt.scaled_dot_product_attention(cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")).numpy()
+    check(got, ref, BF16_RTOL)
+
+
 def test_sdpa_fp32_strided_heads():
     """Q/K/V as head-split views of [B, S, H*D] projections (no copies)."""
     B, S, H, D = 2, 100, 8, 40
