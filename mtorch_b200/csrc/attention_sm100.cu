@@ -427,10 +427,11 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* kv_empty = kv_full + kFaMaxStages;
   uint64_t* s_full = kv_empty + kFaMaxStages;  // [2]
   uint64_t* s_empty = s_full + 2;              // [2]
-  uint64_t* p_full = s_empty + 2;              // [2]
-  uint64_t* p_free = p_full + 2;               // [2 tiles][2 buffers]
-  uint64_t* o_done = p_free + 4;               // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  // p_full / p_free are per P buffer: a softmax warpgroup may finish tile j+1 before the MMA warp
+  // consumes tile j, so one barrier per tile could complete two phases ahead of its waiter.
+  uint64_t* p_full = s_empty + 2;              // [2 tiles][2 buffers]
+  uint64_t* p_free = p_full + 4;               // [2 tiles][2 buffers]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_free + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -450,10 +451,11 @@ __global__ void __launch_bounds__(320, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&o_done[i], 1);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&p_free[i], 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_free[i], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t v_addr = smem_u32(sKV + prev_stage * STAGE_BYTES + K_BYTES);
           bool pok = true;
           for (int x = 0; x < NQ; ++x) {
-            if (!mbar_wait(&p_full[x], jj & 1, 25, abort_flag)) {
+            if (!mbar_wait(&p_full[x * 2 + (jj & 1)], (jj >> 1) & 1, 25, abort_flag)) {
               pok = false;
               break;
             }
@@ -530,7 +532,6 @@ __global__ void __launch_bounds__(320, 1)
               umma_f16(t_o0 + x * DVP, sdesc_none(pa + kk * 2 * kLbo, kLbo, kSbo),
                        sdesc_none(v_addr + kk * 256, 128, kFaBN * 16), idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
             umma_commit(&p_free[x * 2 + (jj & 1)]);
-            umma_commit(&o_done[x]);
           }
           if (!pok) break;
           umma_commit(&kv_empty[prev_stage]);
@@ -588,7 +589,10 @@ __global__ void __launch_bounds__(320, 1)
           // O holds the sum over the previous tiles: wait for the last PV, then rescale in TMEM
           const float m_new = need ? mt : m_used;
           const float corr = ex2(m_used - m_new);
-          if (!mbar_wait(&o_done[x], (j - 1) & 1, 27, abort_flag)) {
+          // PV_{j-1} released P buffer (j-1)&1 (its use number (j-1)>>1); commits complete in issue
+          // order, so this also covers every earlier PV.  Phases of p_free are consumed in order,
+          // which keeps the parity test unambiguous.
+          if (!mbar_wait(&p_free[x * 2 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, 27, abort_flag)) {
             ok = false;
             break;
           }
@@ -648,13 +652,13 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       mbar_arrive(&s_empty[x]);
       fence_proxy_async_smem();
-      mbar_arrive(&p_full[x]);
+      mbar_arrive(&p_full[x * 2 + (j & 1)]);
       float s0, s1;
       f2_unpack(sum2, s0, s1);
       l_run += s0 + s1;
     }
     // final: O (all PV products accumulated) / l
-    if (ok && mbar_wait(&o_done[x], (n_tiles - 1) & 1, 29, abort_flag)) {
+    if (ok && mbar_wait(&p_free[x * 2 + ((n_tiles - 1) & 1)], ((n_tiles - 1) >> 1) & 1, 29, abort_flag)) {
       tc_fence_after();
       float o[DVP];
 #pragma unroll
