@@ -34,7 +34,8 @@ struct FaParams {
   int64_t os[4];
   int Dv;
   int out_dtype;
-  int stages;
+  int stages;    // KV stages (K and V tiles together); the lazy kernel: K stages
+  int stages_v;  // lazy kernel: V stages
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -408,7 +409,6 @@ __global__ void __launch_bounds__(320, 1)
   constexpr int K_BYTES = kFaBN * DP * 2;
   constexpr int V_BYTES = kFaBN * DVP * 2;
   constexpr int P_BYTES = kFaBM * kFaBN * 2;
-  constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
   constexpr uint32_t kLbo = kFaBM * 16;
   constexpr uint32_t kSbo = 128;
   constexpr int FMT = F16 ? 0 : 1;
@@ -420,12 +420,18 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                    // [2][Q]
   uint8_t* sP = sQ + NQ * Q_BYTES;       // [2 tiles][2 buffers][P]
-  uint8_t* sKV = sP + NQ * 2 * P_BYTES;  // [stages][K, V]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + p.stages * STAGE_BYTES);
+  // K and V in separate rings: a K tile is released once both QK^T products have read it, a V
+  // tile only after both PV products, so loading K ahead never waits for the softmax.
+  const int stages_k = p.stages, stages_v = p.stages_v;
+  uint8_t* sK = sP + NQ * 2 * P_BYTES;  // [stages_k][K]
+  uint8_t* sV = sK + stages_k * K_BYTES;  // [stages_v][V]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + stages_v * V_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + kFaMaxStages;
-  uint64_t* s_full = kv_empty + kFaMaxStages;  // [2]
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + kFaMaxStages;
+  uint64_t* v_full = k_empty + kFaMaxStages;
+  uint64_t* v_empty = v_full + kFaMaxStages;
+  uint64_t* s_full = v_empty + kFaMaxStages;  // [2]
   uint64_t* s_empty = s_full + 2;              // [2]
   // p_full / p_free are per P buffer: a softmax warpgroup may finish tile j+1 before the MMA warp
   // consumes tile j, so one barrier per tile could complete two phases ahead of its waiter.
@@ -435,7 +441,6 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int stages = p.stages;
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int hk = h / (p.H / p.Hkv);
@@ -444,9 +449,11 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < stages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < kFaMaxStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -476,17 +483,28 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tmV);
       mbar_arrive_expect_tx(q_full, NQ * Q_BYTES);
       for (int x = 0; x < NQ; ++x) tma_load_5d(sQ + x * Q_BYTES, &tmQ, q_full, 0, qbase + x * kFaBM, 0, h, b);
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int j = 0; j < n_tiles; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1, 21, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[stage], STAGE_BYTES);
-        uint8_t* sk = sKV + stage * STAGE_BYTES;
-        tma_load_5d(sk, &tmK, &kv_full[stage], 0, j * kFaBN, 0, hk, b);
-        tma_load_5d(sk + K_BYTES, &tmV, &kv_full[stage], 0, j * kFaBN, 0, hk, b);
-        if (++stage == stages) {
-          stage = 0;
-          phase ^= 1;
+      // order: K(0), then K(j+1) before V(j) — the next QK^T needs its K before this PV needs V
+      int ks = 0, vs = 0;
+      uint32_t kph = 0, vph = 0;
+      bool ok = true;
+      for (int j = -1; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles) {
+          if (!mbar_wait(&k_empty[ks], kph ^ 1, 21, abort_flag)) break;
+          mbar_arrive_expect_tx(&k_full[ks], K_BYTES);
+          tma_load_5d(sK + ks * K_BYTES, &tmK, &k_full[ks], 0, (j + 1) * kFaBN, 0, hk, b);
+          if (++ks == stages_k) {
+            ks = 0;
+            kph ^= 1;
+          }
+        }
+        if (j >= 0) {
+          if (!mbar_wait(&v_empty[vs], vph ^ 1, 20, abort_flag)) break;
+          mbar_arrive_expect_tx(&v_full[vs], V_BYTES);
+          tma_load_5d(sV + vs * V_BYTES, &tmV, &v_full[vs], 0, j * kFaBN, 0, hk, b);
+          if (++vs == stages_v) {
+            vs = 0;
+            vph ^= 1;
+          }
         }
       }
     }
@@ -494,12 +512,12 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, 22, abort_flag);
-      int stage = 0, prev_stage = 0;
-      uint32_t phase = 0;
+      int ks = 0, vs = 0;
+      uint32_t kph = 0, vph = 0;
       for (int j = 0; ok && j <= n_tiles; ++j) {
         if (j < n_tiles) {
-          if (!mbar_wait(&kv_full[stage], phase, 23, abort_flag)) break;
-          const uint32_t k_addr = smem_u32(sKV + stage * STAGE_BYTES);
+          if (!mbar_wait(&k_full[ks], kph, 23, abort_flag)) break;
+          const uint32_t k_addr = smem_u32(sK + ks * K_BYTES);
           bool sok = true;
           for (int x = 0; x < NQ && sok; ++x) {
             if (!mbar_wait(&s_empty[x], (j & 1) ^ 1, 24, abort_flag)) {
@@ -515,10 +533,16 @@ __global__ void __launch_bounds__(320, 1)
             umma_commit(&s_full[x]);
           }
           if (!sok) break;
+          umma_commit(&k_empty[ks]);
+          if (++ks == stages_k) {
+            ks = 0;
+            kph ^= 1;
+          }
         }
         if (j > 0) {
           const int jj = j - 1;
-          const uint32_t v_addr = smem_u32(sKV + prev_stage * STAGE_BYTES + K_BYTES);
+          if (!mbar_wait(&v_full[vs], vph, 30, abort_flag)) break;
+          const uint32_t v_addr = smem_u32(sV + vs * V_BYTES);
           bool pok = true;
           for (int x = 0; x < NQ; ++x) {
             if (!mbar_wait(&p_full[x * 2 + (jj & 1)], (jj >> 1) & 1, 25, abort_flag)) {
@@ -534,13 +558,10 @@ __global__ void __launch_bounds__(320, 1)
             umma_commit(&p_free[x * 2 + (jj & 1)]);
           }
           if (!pok) break;
-          umma_commit(&kv_empty[prev_stage]);
-        }
-        if (j < n_tiles) {
-          prev_stage = stage;
-          if (++stage == stages) {
-            stage = 0;
-            phase ^= 1;
+          umma_commit(&v_empty[vs]);
+          if (++vs == stages_v) {
+            vs = 0;
+            vph ^= 1;
           }
         }
       }
@@ -765,13 +786,14 @@ static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
 template <int DP, int DVP, bool F16>
 static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched) {
   constexpr int FIXED = 2 * (kFaBM * DP * 2 + 2 * kFaBM * kFaBN * 2);
-  constexpr int STAGE = kFaBN * (DP + DVP) * 2;
+  constexpr int K_BYTES = kFaBN * DP * 2, V_BYTES = kFaBN * DVP * 2;
   constexpr int SMEM_MAX = 224 * 1024;
-  int stages = (SMEM_MAX - 2048 - FIXED) / STAGE;
-  if (stages > kFaMaxStages) stages = kFaMaxStages;
+  const int stages_v = 2;
+  int stages_k = (SMEM_MAX - 2048 - FIXED - stages_v * V_BYTES) / K_BYTES;
+  if (stages_k > kFaMaxStages) stages_k = kFaMaxStages;
   *launched = false;
-  if (stages < 2) return MT_OK;
-  const int smem = FIXED + stages * STAGE + 2048 + 1024;
+  if (stages_k < 2) return MT_OK;
+  const int smem = FIXED + stages_k * K_BYTES + stages_v * V_BYTES + 2048 + 1024;
   auto kern = fa_lazy_sm100_kernel<DP, DVP, F16>;
   static bool attr[64] = {false};
   int dev = 0;
@@ -794,7 +816,8 @@ static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched
   for (int i = 0; i < 4; ++i) p.os[i] = d.o_strides[i];
   p.Dv = (int)d.Dv;
   p.out_dtype = d.dtype;
-  p.stages = stages;
+  p.stages = stages_k;
+  p.stages_v = stages_v;
   dim3 grid((unsigned)((d.Sq + 2 * kFaBM - 1) / (2 * kFaBM)), (unsigned)(d.B * d.H));
   kern<<<grid, 320, smem, st>>>(mq, mk, mv, p);
   *launched = true;
