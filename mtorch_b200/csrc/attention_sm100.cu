@@ -646,6 +646,10 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
+        if (c0 == kFaBN - 64) {  // the last read of S: the next QK^T may overwrite it
+          tc_fence_before();
+          mbar_arrive(&s_empty[x]);
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint32_t pk[8];
@@ -670,8 +674,6 @@ __global__ void __launch_bounds__(320, 1)
           *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[x]);
       fence_proxy_async_smem();
       mbar_arrive(&p_full[x * 2 + (j & 1)]);
       float s0, s1;
