@@ -48,6 +48,26 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// three-input maximum (sm_100 max.f32 with three sources)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// maximum of 64 scores as a tree of independent three-input maxima (no serial chain)
+__device__ __forceinline__ float max64(const uint32_t (&r)[64]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmax3(__uint_as_float(r[i]), __uint_as_float(r[8 + i]), __uint_as_float(r[16 + i]));
+#pragma unroll
+  for (int k = 24; k < 64; k += 16)
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m[i] = fmax3(m[i], __uint_as_float(r[k + i]), __uint_as_float(r[k + 8 + i]));
+  return fmaxf(fmax3(m[0], m[1], m[2]), fmax3(fmax3(m[3], m[4], m[5]), m[6], m[7]));
+}
+
 __device__ __forceinline__ uint64_t f2_bits(float a, float b) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
@@ -280,8 +300,7 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
         tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
         if (full) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+          mx = fmaxf(mx, max64(r));
         } else {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
@@ -593,8 +612,7 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
         if (full) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+          mx = fmaxf(mx, max64(r));
         } else {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
