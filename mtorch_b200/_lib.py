@@ -125,7 +125,7 @@ def lib():
     if _LIB is None:
         if not LIB_PATH.exists():
             raise ImportError(
-                f"mtorch_b200 kernel library not built ({LIB_PATH}); run `python -m mtorch_b200.build` "
+                f"mtorch_b200 kernel library not built ({LIB_PATH}); run `python mtorch_b200/build.py` "
                 "or __graft_entry__.build()")
         L = C.CDLL(os.fspath(LIB_PATH))
         for name, (res, args) in SIGNATURES.items():
