@@ -61,10 +61,12 @@ __device__ __forceinline__ float max64(const uint32_t (&r)[64]) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) m[i] = fmax3(__uint_as_float(r[i]), __uint_as_float(r[8 + i]), __uint_as_float(r[16 + i]));
 #pragma unroll
-  for (int k = 24; k < 64; k += 16)
+  for (int k = 24; k < 56; k += 16)  // columns 24..55
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       m[i] = fmax3(m[i], __uint_as_float(r[k + i]), __uint_as_float(r[k + 8 + i]));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], __uint_as_float(r[56 + i]));  // columns 56..63
   return fmaxf(fmax3(m[0], m[1], m[2]), fmax3(fmax3(m[3], m[4], m[5]), m[6], m[7]));
 }
 
@@ -414,12 +416,101 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
 // Same roles and two query tiles per CTA, but the PV products accumulate into O in TMEM and the
 // running max is only raised when a row's new maximum exceeds the one in use by more than 2^8
 // ("lazy rescale"): p = 2^(s*scale*log2e - m_used) then stays <= 256, exact enough in bf16 / fp32.
+// For head dims of at most DVP - 8 the row sum comes from the tensor core as well (a column of
+// ones in the padding of V), so the softmax warps only evaluate, round and store p.
 // A rescale (rare after the first tile) waits for the previous PV, multiplies the row of O in
 // TMEM and continues.  P is double-buffered in shared memory, so a softmax warpgroup never waits
 // for its previous PV product — only for the S tile it consumes.
-constexpr float kLazyThreshold = 8.0f;  // log2 of the largest p allowed before rescaling
+constexpr float kLazyLimit = 256.0f;  // largest p allowed before the maximum is raised
 
-template <int DP, int DVP, bool F16>
+// Maximum of two packed 16-bit pairs.
+template <bool F16>
+__device__ __forceinline__ uint32_t hmax2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if (F16)
+    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+template <bool F16>
+__device__ __forceinline__ void unpack16x2(uint32_t w, float& lo, float& hi) {
+  if (F16) {
+    const __half2 h = *reinterpret_cast<const __half2*>(&w);
+    lo = __low2float(h);
+    hi = __high2float(h);
+  } else {
+    const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w);
+    lo = __low2float(h);
+    hi = __high2float(h);
+  }
+}
+
+// p = 2^(s * scale_log2 - m) for one 64-column chunk of a score row, written as 16-bit values into
+// the core-matrix layout of the P tile (row `row`, columns c0..c0+63).  Returns the largest p as
+// rounded (the overflow check of the lazy maximum); with SUM it also adds the chunk's fp32 sum to
+// `sum`.  Masked columns hold -inf and give 0.
+template <bool F16, bool SUM>
+__device__ __forceinline__ float fa_exp_chunk(const uint32_t (&r)[64], uint64_t sl2, float m, uint8_t* sPx,
+                                              int c0, int row, float& sum) {
+  const uint64_t negm2 = f2_bits(-m, -m);
+  uint64_t sum_a = f2_bits(0.f, 0.f), sum_b = sum_a;
+  uint32_t mx[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t pk[8];
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const int k = q * 16 + i;
+      const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[k]), __uint_as_float(r[k + 1])), sl2, negm2);
+      float a0, a1;
+      f2_unpack(arg, a0, a1);
+      const float e0 = ex2(a0), e1 = ex2(a1);
+      if (SUM) {
+        if ((i & 2) == 0)
+          sum_a = fadd2(sum_a, f2_bits(e0, e1));
+        else
+          sum_b = fadd2(sum_b, f2_bits(e0, e1));
+      }
+      pk[i / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+      mx[(i / 2) & 3] = hmax2<F16>(mx[(i / 2) & 3], pk[i / 2]);
+    }
+    const int c = c0 + q * 16;
+    uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
+    uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
+    *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  }
+  if (SUM) {
+    float s0, s1, s2, s3;
+    f2_unpack(sum_a, s0, s1);
+    f2_unpack(sum_b, s2, s3);
+    sum += (s0 + s1) + (s2 + s3);
+  }
+  float lo, hi;
+  unpack16x2<F16>(hmax2<F16>(hmax2<F16>(mx[0], mx[1]), hmax2<F16>(mx[2], mx[3])), lo, hi);
+  return fmaxf(lo, hi);
+}
+
+// Multiplies columns [0, c_end) of one row of a P tile by `corr` (a power of two: exact).
+template <bool F16>
+__device__ __forceinline__ void fa_scale_p(uint8_t* sPx, int c_end, int row, float corr) {
+  for (int c = 0; c < c_end; c += 8) {
+    uint4* d = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
+    uint4 v = *d;
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float lo, hi;
+      unpack16x2<F16>(w[i], lo, hi);
+      w[i] = F16 ? pack_f16x2(lo * corr, hi * corr) : pack_bf16x2(lo * corr, hi * corr);
+    }
+    *d = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <int DP, int DVP, bool F16, bool SUMCOL>
 __global__ void __launch_bounds__(320, 1)
     fa_lazy_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const FaParams p) {
@@ -427,6 +518,9 @@ __global__ void __launch_bounds__(320, 1)
   constexpr int Q_BYTES = kFaBM * DP * 2;
   constexpr int K_BYTES = kFaBN * DP * 2;
   constexpr int V_BYTES = kFaBN * DVP * 2;
+  // SUMCOL: the last 8-column chunk of each V stage is not loaded; its first column holds ones, so
+  // the PV product also accumulates the row sum of P into column DVP - 8 of O.
+  constexpr int V_TX = SUMCOL ? V_BYTES - kFaBN * 16 : V_BYTES;
   constexpr int P_BYTES = kFaBM * kFaBN * 2;
   constexpr uint32_t kLbo = kFaBM * 16;
   constexpr uint32_t kSbo = 128;
@@ -485,6 +579,13 @@ __global__ void __launch_bounds__(320, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
+  if (SUMCOL) {
+    for (int i = threadIdx.x; i < stages_v * kFaBN; i += blockDim.x) {
+      uint4* d = reinterpret_cast<uint4*>(sV + (i / kFaBN) * V_BYTES + (DVP / 8 - 1) * kFaBN * 16) + (i % kFaBN);
+      *d = make_uint4(F16 ? 0x3C00u : 0x3F80u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -518,7 +619,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         if (j >= 0) {
           if (!mbar_wait(&v_empty[vs], vph ^ 1, 20, abort_flag)) break;
-          mbar_arrive_expect_tx(&v_full[vs], V_BYTES);
+          mbar_arrive_expect_tx(&v_full[vs], V_TX);
           tma_load_5d(sV + vs * V_BYTES, &tmV, &v_full[vs], 0, j * kFaBN, 0, hk, b);
           if (++vs == stages_v) {
             vs = 0;
@@ -604,60 +705,16 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const int kvalid = min(kFaBN, p.Sk - j * kFaBN);
       const bool full = kvalid == kFaBN;
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
-        uint32_t r[64];
-        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-        tmem_ld_wait();
-        if (full) {
-          mx = fmaxf(mx, max64(r));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (c0 + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
-        }
-      }
-      const float mt = mx * sl;
-      if (j == 0) {
-        m_used = mt;
-      } else {
-        const bool need = mt > m_used + kLazyThreshold;
-        if (__any_sync(0xffffffffu, need)) {
-          // O holds the sum over the previous tiles: wait for the last PV, then rescale in TMEM
-          const float m_new = need ? mt : m_used;
-          const float corr = ex2(m_used - m_new);
-          // PV_{j-1} released P buffer (j-1)&1 (its use number (j-1)>>1); commits complete in issue
-          // order, so this also covers every earlier PV.  Phases of p_free are consumed in order,
-          // which keeps the parity test unambiguous.
-          if (!mbar_wait(&p_free[x * 2 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, 27, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int c0 = 0; c0 < DVP; c0 += 16) {
-            uint32_t r[16];
-            tmem_ld16_raw(t_o + c0, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-            tmem_st16(t_o + c0, r);
-          }
-          tmem_st_wait();
-          l_run *= corr;
-          m_used = m_new;
-        }
-      }
       // the P buffer this tile writes was read by the PV two tiles back
       if (!mbar_wait(&p_free[x * 2 + (j & 1)], ((j >> 1) & 1) ^ 1, 28, abort_flag)) {
         ok = false;
         break;
       }
       uint8_t* sPx = sP + (x * 2 + (j & 1)) * P_BYTES;
-      const uint64_t negm2 = f2_bits(-m_used, -m_used);
-      uint64_t sum2 = f2_bits(0.f, 0.f);
+      // One pass per 64-column chunk: the exponentials use the maximum already in use, and the
+      // largest rounded p is checked against the limit.  When it is exceeded (rare after the first
+      // tile), the maximum is raised by a whole number, so O, the row sum and the P chunks already
+      // written scale by an exact power of two, and the chunk is recomputed.
 #pragma unroll 1
       for (int c0 = 0; c0 < kFaBN; c0 += 64) {
         uint32_t r[64];
@@ -668,35 +725,52 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_before();
           mbar_arrive(&s_empty[x]);
         }
+        if (!full) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t pk[8];
-#pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            const int k = q * 16 + i;
-            const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[k]), __uint_as_float(r[k + 1])), sl2, negm2);
-            float a0, a1;
-            f2_unpack(arg, a0, a1);
-            float e0 = ex2(a0), e1 = ex2(a1);
-            if (!full) {
-              if (c0 + k >= kvalid) e0 = 0.f;
-              if (c0 + k + 1 >= kvalid) e1 = 0.f;
-            }
-            sum2 = fadd2(sum2, f2_bits(e0, e1));
-            pk[i / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
-          }
-          const int c = c0 + q * 16;
-          uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
-          uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
-          *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          for (int i = 0; i < 64; ++i)
+            if (c0 + i >= kvalid) r[i] = __float_as_uint(-INFINITY);
         }
+        if (j == 0 && c0 == 0) m_used = max64(r) * sl;
+        float csum = 0.f;
+        const float pmax = fa_exp_chunk<F16, !SUMCOL>(r, sl2, m_used, sPx, c0, row, csum);
+        const bool need = !(pmax <= kLazyLimit);
+        if (__any_sync(0xffffffffu, need)) {
+          const float cm = max64(r) * sl;
+          const float m_new = need ? m_used + ceilf(cm - m_used) : m_used;
+          const float corr = ex2(m_used - m_new);  // a power of two
+          if (j > 0) {
+            // O holds the sum over the previous tiles: wait for the last PV, then rescale in TMEM.
+            // PV_{j-1} released P buffer (j-1)&1; commits complete in issue order, so this also
+            // covers every earlier PV.
+            if (!mbar_wait(&p_free[x * 2 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, 27, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < DVP; c += 16) {
+              uint32_t o[16];
+              tmem_ld16_raw(t_o + c, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+              tmem_st16(t_o + c, o);
+            }
+            tmem_st_wait();
+          }
+          if (c0 > 0) fa_scale_p<F16>(sPx, c0, row, corr);
+          l_run *= corr;
+          m_used = m_new;
+          csum = 0.f;
+          fa_exp_chunk<F16, !SUMCOL>(r, sl2, m_used, sPx, c0, row, csum);
+        }
+        l_run += csum;
       }
+      if (!ok) break;
+      // orders a rescale of O in the last chunk (tcgen05.st) and the P stores before the PV
+      tc_fence_before();
       fence_proxy_async_smem();
       mbar_arrive(&p_full[x * 2 + (j & 1)]);
-      float s0, s1;
-      f2_unpack(sum2, s0, s1);
-      l_run += s0 + s1;
     }
     // final: O (all PV products accumulated) / l
     if (ok && mbar_wait(&p_free[x * 2 + ((n_tiles - 1) & 1)], ((n_tiles - 1) >> 1) & 1, 29, abort_flag)) {
@@ -712,7 +786,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       const int qi = qbase + x * kFaBM + row;
       if (qi < p.Sq) {
-        const float inv = 1.0f / l_run;
+        const float inv = 1.0f / (SUMCOL ? o[DVP - 8] : l_run);
         char* base = static_cast<char*>(p.o);
         const int64_t off = (int64_t)b * p.os[0] + (int64_t)h * p.os[1] + (int64_t)qi * p.os[2];
         if (p.os[3] == 1 && (p.Dv % 8) == 0 && ((reinterpret_cast<uintptr_t>(base) + off * 2) % 16) == 0) {
@@ -803,7 +877,7 @@ static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
 }
 
 // Launch of the lazy-rescale variant; returns false (not launched) when two KV stages do not fit.
-template <int DP, int DVP, bool F16>
+template <int DP, int DVP, bool F16, bool SUMCOL>
 static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched) {
   constexpr int FIXED = 2 * (kFaBM * DP * 2 + 2 * kFaBM * kFaBN * 2);
   constexpr int K_BYTES = kFaBN * DP * 2, V_BYTES = kFaBN * DVP * 2;
@@ -814,7 +888,7 @@ static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched
   *launched = false;
   if (stages_k < 2) return MT_OK;
   const int smem = FIXED + stages_k * K_BYTES + stages_v * V_BYTES + 2048 + 1024;
-  auto kern = fa_lazy_sm100_kernel<DP, DVP, F16>;
+  auto kern = fa_lazy_sm100_kernel<DP, DVP, F16, SUMCOL>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -827,7 +901,7 @@ static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched
   CUtensorMap mq, mk, mv;
   int rc = fa_map(&mq, d.dtype, d.q, d.B, d.H, d.Sq, d.D, d.q_strides, DP / 8);
   if (!rc) rc = fa_map(&mk, d.dtype, d.k, d.B, d.Hkv, d.Sk, d.D, d.k_strides, DP / 8);
-  if (!rc) rc = fa_map(&mv, d.dtype, d.v, d.B, d.Hkv, d.Sk, d.Dv, d.v_strides, DVP / 8);
+  if (!rc) rc = fa_map(&mv, d.dtype, d.v, d.B, d.Hkv, d.Sk, d.Dv, d.v_strides, SUMCOL ? DVP / 8 - 1 : DVP / 8);
   if (rc) return rc;
   FaParams p{};
   p.Sq = (int)d.Sq; p.Sk = (int)d.Sk; p.H = (int)d.H; p.Hkv = (int)d.Hkv; p.B = (int)d.B;
@@ -853,9 +927,10 @@ static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, cudaStream_t st, bool*
   // two query tiles per CTA when there are enough queries to fill them
   const bool two = d.Sq > kFaBM;
   *handled = true;
-  if (two && Dp == 48 && !getenv("MT_FA_NO_LAZY")) {
+  if (two && Dp == 48 && d.scale > 0 && !getenv("MT_FA_NO_LAZY")) {
     bool launched = false;
-    const int rc = fa_lazy_launch<48, 48, F16>(d, st, &launched);
+    const int rc = d.Dv <= 40 ? fa_lazy_launch<48, 48, F16, true>(d, st, &launched)
+                              : fa_lazy_launch<48, 48, F16, false>(d, st, &launched);
     if (rc || launched) return rc;
   }
   switch (Dp) {

@@ -318,6 +318,22 @@ def test_sdpa_bf16_growing_scores_rescale():
     check(got, ref, BF16_RTOL)
 
 
+@pytest.mark.parametrize("D", [40, 48])
+def test_sdpa_bf16_max_jumps_inside_key_tiles(D):
+    """The score maximum jumps in the second half of key tiles (the P columns already written for
+    the tile are rescaled) and the last key tile is ragged.  D 40 takes the row sum from the
+    tensor core (a ones column in the padding of V); D 48 has no padding and sums on the SIMT side."""
+    B, H, S = 2, 4, 600
+    q = rnd(B, H, S, D, scale=2.0)
+    k = rnd(B, H, S, D, seed=1)
+    pos = np.arange(S)
+    k *= (1.0 + (pos % 128 >= 64) * (pos // 128 + 1) * 1.2)[None, None, :, None].astype(np.float32)
+    v = rnd(B, H, S, D, seed=2)
+    ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
+    got = mt.scaled_dot_product_attention(cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")).numpy()
+    check(got, ref, BF16_RTOL)
+
+
 def test_sdpa_fp32_strided_heads():
     """Q/K/V as head-split views of [B, S, H*D] projections (no copies)."""
     B, S, H, D = 2, 100, 8, 40
