@@ -416,99 +416,12 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
 // Same roles and two query tiles per CTA, but the PV products accumulate into O in TMEM and the
 // running max is only raised when a row's new maximum exceeds the one in use by more than 2^8
 // ("lazy rescale"): p = 2^(s*scale*log2e - m_used) then stays <= 256, exact enough in bf16 / fp32.
-// For head dims of at most DVP - 8 the row sum comes from the tensor core as well (a column of
-// ones in the padding of V), so the softmax warps only evaluate, round and store p.
+// For head dims of at most DVP - 8 the row sum comes from the tensor core (a column of ones in the
+// padding of V accumulates it into O), so the softmax warps only evaluate, round and store p.
 // A rescale (rare after the first tile) waits for the previous PV, multiplies the row of O in
 // TMEM and continues.  P is double-buffered in shared memory, so a softmax warpgroup never waits
 // for its previous PV product — only for the S tile it consumes.
-constexpr float kLazyLimit = 256.0f;  // largest p allowed before the maximum is raised
-
-// Maximum of two packed 16-bit pairs.
-template <bool F16>
-__device__ __forceinline__ uint32_t hmax2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  if (F16)
-    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  else
-    asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-template <bool F16>
-__device__ __forceinline__ void unpack16x2(uint32_t w, float& lo, float& hi) {
-  if (F16) {
-    const __half2 h = *reinterpret_cast<const __half2*>(&w);
-    lo = __low2float(h);
-    hi = __high2float(h);
-  } else {
-    const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w);
-    lo = __low2float(h);
-    hi = __high2float(h);
-  }
-}
-
-// p = 2^(s * scale_log2 - m) for one 64-column chunk of a score row, written as 16-bit values into
-// the core-matrix layout of the P tile (row `row`, columns c0..c0+63).  Returns the largest p as
-// rounded (the overflow check of the lazy maximum); with SUM it also adds the chunk's fp32 sum to
-// `sum`.  Masked columns hold -inf and give 0.
-template <bool F16, bool SUM>
-__device__ __forceinline__ float fa_exp_chunk(const uint32_t (&r)[64], uint64_t sl2, float m, uint8_t* sPx,
-                                              int c0, int row, float& sum) {
-  const uint64_t negm2 = f2_bits(-m, -m);
-  uint64_t sum_a = f2_bits(0.f, 0.f), sum_b = sum_a;
-  uint32_t mx[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint32_t pk[8];
-#pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      const int k = q * 16 + i;
-      const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[k]), __uint_as_float(r[k + 1])), sl2, negm2);
-      float a0, a1;
-      f2_unpack(arg, a0, a1);
-      const float e0 = ex2(a0), e1 = ex2(a1);
-      if (SUM) {
-        if ((i & 2) == 0)
-          sum_a = fadd2(sum_a, f2_bits(e0, e1));
-        else
-          sum_b = fadd2(sum_b, f2_bits(e0, e1));
-      }
-      pk[i / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
-      mx[(i / 2) & 3] = hmax2<F16>(mx[(i / 2) & 3], pk[i / 2]);
-    }
-    const int c = c0 + q * 16;
-    uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
-    uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
-    *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-  }
-  if (SUM) {
-    float s0, s1, s2, s3;
-    f2_unpack(sum_a, s0, s1);
-    f2_unpack(sum_b, s2, s3);
-    sum += (s0 + s1) + (s2 + s3);
-  }
-  float lo, hi;
-  unpack16x2<F16>(hmax2<F16>(hmax2<F16>(mx[0], mx[1]), hmax2<F16>(mx[2], mx[3])), lo, hi);
-  return fmaxf(lo, hi);
-}
-
-// Multiplies columns [0, c_end) of one row of a P tile by `corr` (a power of two: exact).
-template <bool F16>
-__device__ __forceinline__ void fa_scale_p(uint8_t* sPx, int c_end, int row, float corr) {
-  for (int c = 0; c < c_end; c += 8) {
-    uint4* d = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
-    uint4 v = *d;
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float lo, hi;
-      unpack16x2<F16>(w[i], lo, hi);
-      w[i] = F16 ? pack_f16x2(lo * corr, hi * corr) : pack_bf16x2(lo * corr, hi * corr);
-    }
-    *d = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-}
+constexpr float kLazyThreshold = 8.0f;  // log2 of the largest p allowed before rescaling
 
 template <int DP, int DVP, bool F16, bool SUMCOL>
 __global__ void __launch_bounds__(320, 1)
@@ -705,16 +618,60 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const int kvalid = min(kFaBN, p.Sk - j * kFaBN);
       const bool full = kvalid == kFaBN;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
+        uint32_t r[64];
+        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld_wait();
+        if (full) {
+          mx = fmaxf(mx, max64(r));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (c0 + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
+      }
+      const float mt = mx * sl;
+      if (j == 0) {
+        m_used = mt;
+      } else {
+        const bool need = mt > m_used + kLazyThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          // O holds the sum over the previous tiles: wait for the last PV, then rescale in TMEM
+          const float m_new = need ? mt : m_used;
+          const float corr = ex2(m_used - m_new);
+          // PV_{j-1} released P buffer (j-1)&1 (its use number (j-1)>>1); commits complete in issue
+          // order, so this also covers every earlier PV.  Phases of p_free are consumed in order,
+          // which keeps the parity test unambiguous.
+          if (!mbar_wait(&p_free[x * 2 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, 27, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c0 = 0; c0 < DVP; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16_raw(t_o + c0, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+            tmem_st16(t_o + c0, r);
+          }
+          tmem_st_wait();
+          l_run *= corr;
+          m_used = m_new;
+        }
+      }
       // the P buffer this tile writes was read by the PV two tiles back
       if (!mbar_wait(&p_free[x * 2 + (j & 1)], ((j >> 1) & 1) ^ 1, 28, abort_flag)) {
         ok = false;
         break;
       }
       uint8_t* sPx = sP + (x * 2 + (j & 1)) * P_BYTES;
-      // One pass per 64-column chunk: the exponentials use the maximum already in use, and the
-      // largest rounded p is checked against the limit.  When it is exceeded (rare after the first
-      // tile), the maximum is raised by a whole number, so O, the row sum and the P chunks already
-      // written scale by an exact power of two, and the chunk is recomputed.
+      const uint64_t negm2 = f2_bits(-m_used, -m_used);
+      uint64_t sum2 = f2_bits(0.f, 0.f);
 #pragma unroll 1
       for (int c0 = 0; c0 < kFaBN; c0 += 64) {
         uint32_t r[64];
@@ -725,52 +682,35 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_before();
           mbar_arrive(&s_empty[x]);
         }
-        if (!full) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (c0 + i >= kvalid) r[i] = __float_as_uint(-INFINITY);
-        }
-        if (j == 0 && c0 == 0) m_used = max64(r) * sl;
-        float csum = 0.f;
-        const float pmax = fa_exp_chunk<F16, !SUMCOL>(r, sl2, m_used, sPx, c0, row, csum);
-        const bool need = !(pmax <= kLazyLimit);
-        if (__any_sync(0xffffffffu, need)) {
-          const float cm = max64(r) * sl;
-          const float m_new = need ? m_used + ceilf(cm - m_used) : m_used;
-          const float corr = ex2(m_used - m_new);  // a power of two
-          if (j > 0) {
-            // O holds the sum over the previous tiles: wait for the last PV, then rescale in TMEM.
-            // PV_{j-1} released P buffer (j-1)&1; commits complete in issue order, so this also
-            // covers every earlier PV.
-            if (!mbar_wait(&p_free[x * 2 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, 27, abort_flag)) {
-              ok = false;
-              break;
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const int k = q * 16 + i;
+            const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[k]), __uint_as_float(r[k + 1])), sl2, negm2);
+            float a0, a1;
+            f2_unpack(arg, a0, a1);
+            float e0 = ex2(a0), e1 = ex2(a1);
+            if (!full) {
+              if (c0 + k >= kvalid) e0 = 0.f;
+              if (c0 + k + 1 >= kvalid) e1 = 0.f;
             }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < DVP; c += 16) {
-              uint32_t o[16];
-              tmem_ld16_raw(t_o + c, o);
-              tmem_ld_wait();
-#pragma unroll
-              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-              tmem_st16(t_o + c, o);
-            }
-            tmem_st_wait();
+            if (!SUMCOL) sum2 = fadd2(sum2, f2_bits(e0, e1));
+            pk[i / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
           }
-          if (c0 > 0) fa_scale_p<F16>(sPx, c0, row, corr);
-          l_run *= corr;
-          m_used = m_new;
-          csum = 0.f;
-          fa_exp_chunk<F16, !SUMCOL>(r, sl2, m_used, sPx, c0, row, csum);
+          const int c = c0 + q * 16;
+          uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
+          uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
+          *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
-        l_run += csum;
       }
-      if (!ok) break;
-      // orders a rescale of O in the last chunk (tcgen05.st) and the P stores before the PV
-      tc_fence_before();
       fence_proxy_async_smem();
       mbar_arrive(&p_full[x * 2 + (j & 1)]);
+      float s0, s1;
+      f2_unpack(sum2, s0, s1);
+      l_run += s0 + s1;
     }
     // final: O (all PV products accumulated) / l
     if (ok && mbar_wait(&p_free[x * 2 + ((n_tiles - 1) & 1)], ((n_tiles - 1) >> 1) & 1, 29, abort_flag)) {
