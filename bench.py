@@ -31,6 +31,10 @@ sys.path.insert(0, str(ROOT))
 BATCH = 64
 H = W = 64
 CTX = 77
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch per sample, from one ncu
+# capture of `bench.py --kernel attn|conv --batch 64` (the ncu summaries under profiles/): 654.3 MB
+# and 291.2 MB per 64-sample launch.
+DRAM_BYTES_PER_SAMPLE = {"attn": (503461632 + 150793472) / 64, "conv": (169972224 + 121186816) / 64}
 METRIC = "UNet denoise steps/s (SD-1.5 shape, bf16, batch 64 latents 64x64, context 77x768)"
 
 
@@ -307,28 +311,44 @@ def run_ours(args):
     e2e = {"value": 1000.0 * args.steps / ms_e2e, "unit": "steps/s", "h2d_bytes_per_step": h2d * world,
            "d2h_bytes_per_step": d2h * world}
 
-    # ---- roofline of the dominant kernel: the implicit-GEMM 3x3 conv (tcgen05) ----
+    # ---- rooflines: the dominant kernel (level-0 flash attention) and the 3x3 conv ----
     hbm, tf_burst, tf_sust, peak_kind = peaks()
+
+    def timed(fn, reps=10):
+        for _ in range(3):
+            fn()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        for _ in range(reps):
+            fn()
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+        return ev[0].elapsed_time(ev[1]) / reps
+
+    # self-attention of the 64x64 level: 8 heads x 4096 tokens x head dim 40 (Q, K, V, O 168 MB
+    # each at nb = 64, > L2); the same kernel the UNet launches for these shapes
+    q, k, v = (mt.empty(nb, 8, H * W, 40, dtype="bfloat16", device=dev).uniform_(-1, 1) for _ in range(3))
+    attn_ms = timed(lambda: mt.scaled_dot_product_attention(q, k, v))
+    attn_flops = 4.0 * nb * 8 * (H * W) ** 2 * 40
+    achieved = attn_flops / (attn_ms * 1e-3) / 1e12
+    del q, k, v
+    # per-launch DRAM bytes of one ncu capture at nb = 64, scaled by nb
+    traffic = DRAM_BYTES_PER_SAMPLE["attn"] * nb
+    roofline = {"bound": "tensor", "kernel": f"fa_lazy_sm100_kernel<48,48,bf16,sumcol> (8 heads x 4096 x 40, "
+                f"batch {nb})", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
+                "frac": achieved / tf_burst, "peak_kind": f"{peak_kind} bf16 burst", "traffic": traffic,
+                "algorithmic_bytes": 4 * nb * 8 * H * W * 40 * 2, "ms_per_launch": attn_ms,
+                "step_tflops": unet_flops_per_sample() * nb / (ms_per_step * 1e-3) / 1e12}
     conv = unet.down[0].conv2  # 320 -> 320, 3x3 at 64x64 (the UNet's most frequent conv shape)
     xin = mt.empty(nb, 320, H, W, dtype="bfloat16", device=dev).uniform_(-1, 1).contiguous(
         memory_format=mt.channels_last)
-    for _ in range(3):
-        conv(xin)
-    reps = 10
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    torch.cuda.synchronize()
-    ev[0].record(stream)
-    for _ in range(reps):
-        conv(xin)  # input 168 MB at nb=64 > L2 (126 MB); at small nb L2 may hold it
-    ev[1].record(stream)
-    torch.cuda.synchronize()
-    conv_ms = ev[0].elapsed_time(ev[1]) / reps
-    conv_flops = 2.0 * nb * H * W * 320 * 320 * 9
-    achieved = conv_flops / (conv_ms * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "kernel": "gemm_sm100_kernel<160,false,true> (conv 3x3 320->320, 64x64, "
-                f"batch {nb})", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
-                "frac": achieved / tf_burst, "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
-                "step_tflops": unet_flops_per_sample() * nb / (ms_per_step * 1e-3) / 1e12}
+    conv_ms = timed(lambda: conv(xin))  # input 168 MB at nb = 64 > L2
+    conv_ach = 2.0 * nb * H * W * 320 * 320 * 9 / (conv_ms * 1e-3) / 1e12
+    roofline_conv = {"bound": "tensor", "kernel": f"gemm_sm100_kernel<160,bf16,implicit conv> (3x3 320->320, "
+                     f"64x64, batch {nb})", "achieved": conv_ach, "peak": tf_burst, "unit": "TFLOP/s",
+                     "frac": conv_ach / tf_burst, "peak_kind": f"{peak_kind} bf16 burst",
+                     "traffic": DRAM_BYTES_PER_SAMPLE["conv"] * nb, "ms_per_launch": conv_ms}
 
     if rank == 0:
         clk = clocks.summary(gpu_index=None)
@@ -343,7 +363,8 @@ def run_ours(args):
                 "[64,77,768], 1 UNet eval + DDIM update per step", "model": "SD-1.5-shaped UNet (859.5M params)",
                 "global_batch": BATCH, "seq_len": H * W, "parallelism": f"batch-shard dp{world} + NCCL all-gather",
                 "l2": "activations > L2 (126 MB) at batch 64/GPU; no flush"},
-                "gpu_launches": int(launches), "e2e": e2e, "roofline": roofline, "cpu_baseline": base,
+                "gpu_launches": int(launches), "e2e": e2e, "roofline": roofline, "roofline_conv": roofline_conv,
+                "cpu_baseline": base,
                 "clocks": clk}
         print(json.dumps(line))
     if dist:
