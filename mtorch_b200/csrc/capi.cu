@@ -65,7 +65,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
 
 int make_tensor_map(CUtensorMap* map, int dtype, int rank, const void* base, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box, int swizzle) {
+                    const uint64_t* strides_bytes, const uint32_t* box, int swizzle, const uint32_t* elem_strides) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -85,6 +85,11 @@ int make_tensor_map(CUtensorMap* map, int dtype, int rank, const void* base, con
   for (int i = 0; i + 1 < rank; ++i)
     if (strides_bytes[i] % 16 != 0) return fail(MT_ERR_INVALID, "tensor map: stride not a multiple of 16 bytes");
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  if (elem_strides)
+    for (int i = 0; i < rank; ++i) {
+      if (elem_strides[i] < 1 || elem_strides[i] > 8) return fail(MT_ERR_INVALID, "tensor map: element stride out of range");
+      estr[i] = elem_strides[i];
+    }
   const CUtensorMapSwizzle sw = swizzle == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                 : swizzle == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                 : swizzle == 32 ? CU_TENSOR_MAP_SWIZZLE_32B

@@ -30,7 +30,7 @@ struct TileParams {
   int a_batched, b_batched;
   // implicit convolution
   int tw, th, tn, tiles_q, tiles_p;
-  int c_chunks, R, S, pad_h, pad_w, dil_h, dil_w;
+  int c_chunks, R, S, pad_h, pad_w, dil_h, dil_w, stride_h, stride_w;
   int bk;  // elements per 128-byte K chunk
 };
 
@@ -210,7 +210,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (CONV) {
             const int rs = kk / tp.c_chunks, cc = kk - rs * tp.c_chunks;
             const int r = rs / tp.S, s = rs - r * tp.S;
-            const int cx = cc * tp.bk, wx = q0 + s * tp.dil_w - tp.pad_w, hy = p0 + r * tp.dil_h - tp.pad_h;
+            const int cx = cc * tp.bk, wx = q0 * tp.stride_w + s * tp.dil_w - tp.pad_w,
+                      hy = p0 * tp.stride_h + r * tp.dil_h - tp.pad_h;
             tma_load_4d(sa, &tmA, &full[stage], cx, wx, hy, i0);
             tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, 0);
             if (TF32) {
@@ -675,9 +676,12 @@ int run_gemm(const mt_gemm_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st)
 // ---------------------------------------------------------------------------------------------
 // Convolution.
 
+// Implicit GEMM needs whole 128-byte channel chunks; strides 1 and 2 (the tensor map walks the
+// input with that element stride, so a stride-2 box spans twice the output tile's extent).
 static bool conv_implicit_ok(const mt_conv2d_desc& d) {
   const int bk = 128 / dtype_size(d.dtype);
-  return d.stride_h == 1 && d.stride_w == 1 && d.C % bk == 0 && d.groups == 1;
+  return d.stride_h >= 1 && d.stride_h <= 2 && d.stride_w >= 1 && d.stride_w <= 2 && d.C % bk == 0 &&
+         d.groups == 1;
 }
 
 int64_t conv_packed_channels(int64_t C, int64_t R, int64_t S, int dtype) {
@@ -801,12 +805,15 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
     tp.c_chunks = (int)(d.C / tp.bk);
     tp.R = (int)d.R; tp.S = (int)d.S;
     tp.pad_h = d.pad_h; tp.pad_w = d.pad_w; tp.dil_h = d.dil_h; tp.dil_w = d.dil_w;
+    tp.stride_h = d.stride_h; tp.stride_w = d.stride_w;
     tp.k_iters = (int)(d.R * d.S * tp.c_chunks);
     uint64_t dims[4] = {(uint64_t)d.C, (uint64_t)d.W, (uint64_t)d.H, (uint64_t)d.N};
     uint64_t strides[3] = {(uint64_t)(d.C * es), (uint64_t)(d.W * d.C * es), (uint64_t)(d.H * d.W * d.C * es)};
-    uint32_t box[4] = {(uint32_t)tp.bk, (uint32_t)tw, (uint32_t)th, (uint32_t)tn};
-    rc = make_tensor_map(&L->a, d.dtype, 4, a, dims, strides, box, 128);
-    if (!rc && tf32) rc = make_tensor_map(&L->alo, MT_F32, 4, alo, dims, strides, box, 128);
+    // tw, th <= 128, so a stride-2 box (2 tw x 2 th input pixels) stays within TMA's 256 limit
+    uint32_t box[4] = {(uint32_t)tp.bk, (uint32_t)(tw * d.stride_w), (uint32_t)(th * d.stride_h), (uint32_t)tn};
+    const uint32_t estr[4] = {1, (uint32_t)d.stride_w, (uint32_t)d.stride_h, 1};
+    rc = make_tensor_map(&L->a, d.dtype, 4, a, dims, strides, box, 128, estr);
+    if (!rc && tf32) rc = make_tensor_map(&L->alo, MT_F32, 4, alo, dims, strides, box, 128, estr);
   } else {
     tp.num_m_tiles = (int)((M + kBM - 1) / kBM);
     tp.k_iters = (int)((Kg + tp.bk - 1) / tp.bk);

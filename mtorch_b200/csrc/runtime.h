@@ -33,9 +33,12 @@ inline int dtype_size(int dtype) {
 int num_sms();  // SM count of the current device (148 on B200)
 
 // TMA tensor map over a dense tensor: dims innermost first; strides in BYTES for dims
-// 1..rank-1; box in elements.  swizzle: 0 none, 128 = 128-byte.
+// 1..rank-1; box in elements.  swizzle: 0 none, 128 = 128-byte.  elem_strides (optional): the
+// traversal stride of each dimension; a box then holds ceil(box[i] / elem_strides[i]) elements
+// along dimension i, taken every elem_strides[i]-th element from the start coordinate.
 int make_tensor_map(CUtensorMap* map, int dtype, int rank, const void* base, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box, int swizzle);
+                    const uint64_t* strides_bytes, const uint32_t* box, int swizzle,
+                    const uint32_t* elem_strides = nullptr);
 
 // elementwise.cu
 int launch_copy_strided(void* dst, int dd, const int64_t* dst_st, const void* src, int sd, const int64_t* src_st,

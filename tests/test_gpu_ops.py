@@ -241,22 +241,27 @@ def test_conv2d_fp32_golden(golden, name):
     check(got, golden[f"{name}.y"], FP32_RTOL)
 
 
-@pytest.mark.parametrize("shape,K,k,pad", [((2, 64, 16, 16), 64, 3, 1), ((1, 96, 9, 11), 40, 3, 1),
-                                           ((2, 32, 8, 8), 48, 1, 0)])
-def test_conv2d_fp32_implicit(shape, K, k, pad):
+@pytest.mark.parametrize("shape,K,k,pad,stride", [((2, 64, 16, 16), 64, 3, 1, 1), ((1, 96, 9, 11), 40, 3, 1, 1),
+                                                  ((2, 32, 8, 8), 48, 1, 0, 1), ((2, 64, 16, 16), 64, 3, 1, 2),
+                                                  ((1, 96, 9, 11), 40, 3, 1, 2)])
+def test_conv2d_fp32_implicit(shape, K, k, pad, stride):
     x, w, b = rnd(*shape), rnd(K, shape[1], k, k, seed=1, scale=0.1), rnd(K, seed=2)
-    ref = oracle.conv2d_f32(x, w, b, 1, pad)
-    check(mt.conv2d(cu(x), cu(w), cu(b), 1, pad).numpy(), ref, FP32_RTOL)
+    ref = oracle.conv2d_f32(x, w, b, stride, pad)
+    check(mt.conv2d(cu(x), cu(w), cu(b), stride, pad).numpy(), ref, FP32_RTOL)
     xl = cu(x).contiguous(memory_format=mt.channels_last)
-    y = mt.conv2d(xl, cu(w), cu(b), 1, pad)
+    y = mt.conv2d(xl, cu(w), cu(b), stride, pad)
     assert y.is_contiguous(mt.channels_last)
     check(y.numpy(), ref, FP32_RTOL)
 
 
 @pytest.mark.parametrize("shape,K,k,stride,pad", [((2, 320, 32, 32), 320, 3, 1, 1), ((2, 128, 8, 8), 256, 3, 1, 1),
                                                   ((1, 640, 16, 16), 1280, 1, 1, 0), ((2, 4, 32, 32), 320, 3, 1, 1),
-                                                  ((2, 320, 16, 16), 320, 3, 2, 1), ((1, 320, 64, 64), 4, 3, 1, 1)])
+                                                  ((2, 320, 16, 16), 320, 3, 2, 1), ((1, 320, 64, 64), 4, 3, 1, 1),
+                                                  ((2, 320, 64, 64), 320, 3, 2, 1), ((1, 128, 15, 17), 64, 3, 2, 1),
+                                                  ((2, 1280, 16, 16), 1280, 3, 2, 1), ((1, 64, 9, 9), 64, 1, 2, 0)])
 def test_conv2d_bf16(shape, K, k, stride, pad):
+    """Includes stride-2 implicit convolutions (the UNet's downsamplers, a ragged odd-sized input and a
+    strided 1x1): the tensor map walks the input every other pixel."""
     x, w, b = rnd(*shape), rnd(K, shape[1], k, k, seed=1, scale=0.05), rnd(K, seed=2)
     ref = oracle.conv2d_f32(bf16_round(x), bf16_round(w), bf16_round(b), stride, pad)
     conv = mt.nn.Conv2d(shape[1], K, k, stride=stride, padding=pad).cuda().to("bfloat16")
