@@ -48,10 +48,38 @@ struct EpiParams {
   int bias_vec;  // bias rows 16-byte aligned and bf16 / fp32: vector loads
 };
 
+// 256-bit global accesses (sm_100): one instruction covers a whole 32-byte sector, so a warp whose
+// threads each own a row writes full sectors instead of two half-sector writes per sector.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+__device__ __forceinline__ void ld_global_v8(const void* p, uint32_t (&w)[8]) {
+  asm volatile("ld.global.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+               : "l"(p));
+}
+
 // 32 consecutive values of one row: load (accumulate scale*x into v) / store, runtime dtype.
 __device__ __forceinline__ void row_load_add(const void* p, int dtype, int64_t off, int nvalid, bool vec, float scale,
                                              float (&v)[32]) {
   if (vec && nvalid >= 32) {
+    if (dtype == MT_BF16 && (reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16*>(p) + off) & 31) == 0) {
+      const uint8_t* q = reinterpret_cast<const uint8_t*>(static_cast<const __nv_bfloat16*>(p) + off);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        uint32_t w[8];
+        ld_global_v8(q + 32 * i, w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+          v[i * 16 + 2 * j] += scale * f.x;
+          v[i * 16 + 2 * j + 1] += scale * f.y;
+        }
+      }
+      return;
+    }
     if (dtype == MT_BF16) {
       const uint4* q = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p) + off);
 #pragma unroll
@@ -87,6 +115,19 @@ __device__ __forceinline__ void row_load_add(const void* p, int dtype, int64_t o
 
 __device__ __forceinline__ void row_store(void* p, int dtype, int64_t off, int nvalid, bool vec, const float (&v)[32]) {
   if (vec && nvalid >= 32) {
+    if ((dtype == MT_BF16 || dtype == MT_F16) && (reinterpret_cast<uintptr_t>(static_cast<uint16_t*>(p) + off) & 31) == 0) {
+      uint8_t* q = reinterpret_cast<uint8_t*>(static_cast<uint16_t*>(p) + off);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          w[j] = dtype == MT_BF16 ? pack_bf16x2(v[16 * i + 2 * j], v[16 * i + 2 * j + 1])
+                                  : pack_f16x2(v[16 * i + 2 * j], v[16 * i + 2 * j + 1]);
+        st_global_v8(q + 32 * i, w);
+      }
+      return;
+    }
     if (dtype == MT_BF16) {
       uint4* q = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p) + off);
 #pragma unroll
