@@ -32,6 +32,7 @@ struct TileParams {
   int tw, th, tn, tiles_q, tiles_p;
   int c_chunks, R, S, pad_h, pad_w, dil_h, dil_w, stride_h, stride_w;
   int bk;  // elements per 128-byte K chunk
+  int a_stages;  // B-resident variant: A-only stages behind the resident B tile
 };
 
 struct EpiParams {
@@ -163,6 +164,10 @@ __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b,
   b = rest / tp.num_m_tiles;
 }
 
+// Shared memory of the B-resident variant's operand region (B tile + A stages).
+constexpr int kResBytes = 200 * 1024;
+constexpr int kMaxResStages = 8;
+
 template <int BN, bool TF32>
 struct GemmCfg {
   static constexpr int A_BYTES = kBM * 128;
@@ -177,22 +182,34 @@ struct GemmCfg {
                                    : (2 * BN <= 256) ? 256
                                                      : 512;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  // B-resident variant: [B tile, all K chunks][A stages] within kResBytes, barriers after it.
+  static constexpr int RES_SMEM_BYTES = kResBytes + 1024 + 256;
 };
 
-template <int BN, bool TF32, bool CONV>
+// BRES (B resident): every tile of this CTA has the same column tile (the grid is a multiple of
+// the number of column tiles), so the whole [BN x K] B tile is loaded into shared memory once and
+// only A streams through the stage ring; for the short-K projections this removes the re-reads
+// of B from L2 that otherwise cost more than the A traffic.
+template <int BN, bool TF32, bool CONV, bool BRES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmAlo, const __grid_constant__ CUtensorMap tmBlo,
                       const TileParams tp, const EpiParams ep, const uint32_t idesc) {
   using Cfg = GemmCfg<BN, TF32>;
-  constexpr int STAGES = Cfg::STAGES;
+  static_assert(!BRES || (!TF32 && !CONV), "B-resident variant: 16-bit GEMMs only");
+  const int STAGES = BRES ? tp.a_stages : Cfg::STAGES;
+  // stage s: A at stage_base + s * STAGE_BYTES; B (not BRES) right after it
+  constexpr int STAGE_BYTES = BRES ? Cfg::A_BYTES : Cfg::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint8_t* sbres = smem;  // BRES: k_iters chunks of B_BYTES
+  uint8_t* stage_base = BRES ? smem + tp.k_iters * Cfg::B_BYTES : smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (BRES ? kResBytes : Cfg::STAGES * Cfg::STAGE_BYTES));
+  uint64_t* empty = full + (BRES ? kMaxResStages : Cfg::STAGES);
+  uint64_t* tfull = empty + (BRES ? kMaxResStages : Cfg::STAGES);
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* b_full = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -205,6 +222,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 256);
     }
+    mbar_init(b_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -231,6 +249,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      if (BRES && blockIdx.x < total_tiles) {
+        int b, mt, nt;
+        decode_tile(tp, blockIdx.x, b, mt, nt);
+        mbar_arrive_expect_tx(b_full, tp.k_iters * Cfg::B_BYTES);
+        for (int kk = 0; kk < tp.k_iters; ++kk)
+          tma_load_3d(sbres + kk * Cfg::B_BYTES, &tmB, b_full, kk * tp.bk, nt * BN, 0);
+      }
       for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
         int b, mt, nt;
         decode_tile(tp, t, b, mt, nt);
@@ -243,8 +268,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int kk = 0; kk < tp.k_iters; ++kk) {
           if (!mbar_wait(&empty[stage], phase ^ 1, 1, abort_flag)) break;
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          uint8_t* sa = stage_base + stage * STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
           uint8_t* salo = sb + Cfg::B_BYTES;
           uint8_t* sblo = salo + Cfg::A_BYTES;
@@ -262,7 +287,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           } else {
             const int ab = tp.a_batched ? b : 0, bb = tp.b_batched ? b : 0;
             tma_load_3d(sa, &tmA, &full[stage], kk * tp.bk, mt * kBM, ab);
-            tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, bb);
+            if (!BRES) tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, bb);
             if (TF32) {
               tma_load_3d(salo, &tmAlo, &full[stage], kk * tp.bk, mt * kBM, ab);
               tma_load_3d(sblo, &tmBlo, &full[stage], kk * tp.bk, n0, bb);
@@ -281,7 +306,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, ++local) {
+      if (BRES && blockIdx.x < total_tiles && !mbar_wait(b_full, 0, 4, abort_flag)) local = -1;
+      for (int t = blockIdx.x; local >= 0 && t < total_tiles && !*abort_flag; t += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t tph = (local >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1, 2, abort_flag)) break;
@@ -290,8 +316,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kk = 0; kk < tp.k_iters; ++kk) {
           if (!mbar_wait(&full[stage], phase, 3, abort_flag)) break;
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+          const uint32_t a_addr = smem_u32(stage_base + stage * STAGE_BYTES);
+          const uint32_t b_addr = BRES ? smem_u32(sbres + kk * Cfg::B_BYTES) : a_addr + Cfg::A_BYTES;
           const uint32_t alo_addr = b_addr + Cfg::B_BYTES;
           const uint32_t blo_addr = alo_addr + Cfg::A_BYTES;
 #pragma unroll
@@ -446,29 +472,49 @@ struct GemmLaunch {
   bool conv;
 };
 
-template <int BN, bool TF32, bool CONV>
+template <int BN, bool TF32, bool CONV, bool BRES = false>
 static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
   using Cfg = GemmCfg<BN, TF32>;
-  auto kern = gemm_sm100_kernel<BN, TF32, CONV>;
+  constexpr int smem = BRES ? Cfg::RES_SMEM_BYTES : Cfg::SMEM_BYTES;
+  auto kern = gemm_sm100_kernel<BN, TF32, CONV, BRES>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES),
+    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                         "gemm smem attribute");
     if (rc) return rc;
     attr_set[dev & 63] = true;
   }
   const int64_t tiles = (int64_t)L.tp.num_m_tiles * L.tp.num_n_tiles * L.tp.batch;
   if (tiles > 0x7fffffffLL) return fail(MT_ERR_UNSUPPORTED, "gemm: too many tiles");
-  const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  int grid = (int)std::min<int64_t>(tiles, num_sms());
+  if (BRES) grid = num_sms() / L.tp.num_n_tiles * L.tp.num_n_tiles;  // one column tile per CTA
   const int fmt = L.kind == MT_BF16 ? 1 : L.kind == MT_F16 ? 0 : 2;
   const uint32_t idesc = make_idesc(fmt, kBM, BN);
-  kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, st>>>(L.a, L.b, L.alo, L.blo, L.tp, L.ep, idesc);
+  kern<<<grid, kGemmThreads, smem, st>>>(L.a, L.b, L.alo, L.blo, L.tp, L.ep, idesc);
   return check_launch("gemm_sm100");
 }
 
-static int dispatch(const GemmLaunch& L, cudaStream_t st) {
+// Whether the B-resident variant pays: 16-bit, unbatched, the [BN x K] B tile leaves room for at
+// least 3 A stages, a grid that is a multiple of the column-tile count loses at most 4% of the SMs,
+// and every CTA gets at least 8 tiles to amortise its B load.  A_stages is set as a side effect.
+static bool use_bres(GemmLaunch& L) {
+  static const bool off = getenv("MT_GEMM_NO_BRES") != nullptr;
+  if (off || L.kind == MT_F32 || L.conv || L.tp.batch != 1) return false;
+  const int b_bytes = L.bn * 128 * L.tp.k_iters;
+  const int stages = std::min(kMaxResStages, (kResBytes - b_bytes) / (kBM * 128));
+  if (stages < 3) return false;
+  const int sms = num_sms(), nn = L.tp.num_n_tiles;
+  if (nn > sms) return false;
+  const int grid = sms / nn * nn;
+  if ((sms - grid) * 25 > sms) return false;
+  if ((int64_t)L.tp.num_m_tiles * nn < 8LL * grid) return false;
+  L.tp.a_stages = stages;
+  return true;
+}
+
+static int dispatch(GemmLaunch& L, cudaStream_t st) {
   if (L.kind == MT_F32) {
     if (L.conv) return launch_variant<128, true, true>(L, st);
     if (L.bn == 64) return launch_variant<64, true, false>(L, st);
@@ -480,6 +526,14 @@ static int dispatch(const GemmLaunch& L, cudaStream_t st) {
       case 128: return launch_variant<128, false, true>(L, st);
       case 160: return launch_variant<160, false, true>(L, st);
       default: return launch_variant<256, false, true>(L, st);
+    }
+  }
+  if (use_bres(L)) {
+    switch (L.bn) {
+      case 64: return launch_variant<64, false, false, true>(L, st);
+      case 128: return launch_variant<128, false, false, true>(L, st);
+      case 160: return launch_variant<160, false, false, true>(L, st);
+      default: return launch_variant<256, false, false, true>(L, st);
     }
   }
   switch (L.bn) {
