@@ -339,6 +339,20 @@ def test_sdpa_bf16_max_jumps_inside_key_tiles(D):
     check(got, ref, BF16_RTOL)
 
 
+@pytest.mark.parametrize("Sq,Sk,D", [(1100, 300, 40), (1024, 77, 40), (1536, 1000, 48)])
+def test_sdpa_bf16_ragged_long_queries(Sq, Sk, D):
+    """Long query sequences with ragged query counts (a CTA's second query tile partly or wholly
+    past the end), ragged and short key counts (cross-attention to 77 tokens) and head dim 48
+    (row sum on the SIMT side)."""
+    B, H = 2, 3
+    q = rnd(B, H, Sq, D, scale=1.5)
+    k = rnd(B, H, Sk, D, seed=1)
+    v = rnd(B, H, Sk, D, seed=2)
+    ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
+    got = mt.scaled_dot_product_attention(cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")).numpy()
+    check(got, ref, BF16_RTOL)
+
+
 def test_sdpa_fp32_strided_heads():
     """Q/K/V as head-split views of [B, S, H*D] projections (no copies)."""
     B, S, H, D = 2, 100, 8, 40
