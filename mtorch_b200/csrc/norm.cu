@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_cl_kernel(const void* x
 // Channels-last bf16 partial sums, 8 channels (16 bytes) per load: V = C/8 vectors per pixel,
 // thread t owns vector t % V of pixel lane t / V; one (lane, channel) slot per thread and
 // channel in shared memory keeps the reduction order fixed.
-__global__ void __launch_bounds__(kGnThreads) gn_partial_cl_bf16x8_kernel(const __nv_bfloat16* x, int64_t sn,
+__global__ void __launch_bounds__(kGnThreads, 6) gn_partial_cl_bf16x8_kernel(const __nv_bfloat16* x, int64_t sn,
                                                                           int64_t C, int64_t HW, int64_t G,
                                                                           int chunks, double* part) {
   extern __shared__ float gn_sh[];  // [2][lanes * C]
@@ -366,6 +366,75 @@ __global__ void gn_table_kernel(const float* stats, const void* w, const void* b
   }
   if (b) sh += load_as_f32(b, c, wbd);
   tab[i] = make_float2(a, sh);
+}
+
+// Finalize + affine table in one pass: one warp per (image, group).  Lane l sums chunks l, l+32,
+// ... in double, then a fixed xor-shuffle tree combines the lanes, so the result depends only on
+// the per-image chunking (not on N) and is the same on every run.  The warp then writes the
+// (a, b) pairs of the group's channels: y = x * a + b.
+__global__ void gn_finalize_table_kernel(const double* part, const void* w, const void* b, int wbd, int64_t N,
+                                         int64_t C, int64_t G, int chunks, double count, double eps, float2* tab) {
+  const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= N * G) return;
+  const int64_t n = i / G, g = i % G;
+  double s = 0, q = 0;
+  for (int c = lane; c < chunks; c += 32) {
+    const double* p = part + ((n * chunks + c) * G + g) * 2;
+    s += p[0];
+    q += p[1];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+  const double mean = s / count;
+  double var = q / count - mean * mean;
+  if (var < 0) var = 0;
+  const float rstd = (float)(1.0 / sqrt(var + eps)), mf = (float)mean;
+  const int64_t Cg = C / G;
+  for (int64_t c = g * Cg + lane; c < (g + 1) * Cg; c += 32) {
+    float a = rstd, sh = -mf * rstd;
+    if (w) {
+      const float gm = load_as_f32(w, c, wbd);
+      a *= gm;
+      sh *= gm;
+    }
+    if (b) sh += load_as_f32(b, c, wbd);
+    tab[n * C + c] = make_float2(a, sh);
+  }
+}
+
+// Apply with one grid row per image and a grid stride that is a multiple of C/8: every thread
+// always meets the same 8 channels, so it holds their (a, b) pairs in registers and each 16 bytes
+// of x cost one load and one store.  32-bit indexing inside the image (HW * C / 8 < 2^31).
+__global__ void __launch_bounds__(256) gn_apply_img_bf16x8_kernel(__nv_bfloat16* y, const __nv_bfloat16* x,
+                                                                  const float2* tab, int per_img8, int C8, int silu) {
+  const int64_t n = blockIdx.y;
+  const uint4* xi = reinterpret_cast<const uint4*>(x) + n * per_img8;
+  uint4* yi = reinterpret_cast<uint4*>(y) + n * per_img8;
+  const int i0 = blockIdx.x * blockDim.x + threadIdx.x;
+  const int stride = gridDim.x * blockDim.x;
+  const float4* t = reinterpret_cast<const float4*>(tab + n * C8 * 8) + (i0 % C8) * 4;
+  float4 ab[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ab[j] = t[j];  // (a0, b0, a1, b1) for channel pairs 2j, 2j+1
+  for (int i = i0; i < per_img8; i += stride) {
+    uint4 v = xi[i];
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      float r0 = f.x * ab[j].x + ab[j].y, r1 = f.y * ab[j].z + ab[j].w;
+      if (silu) {
+        r0 = silu_f(r0);
+        r1 = silu_f(r1);
+      }
+      h[j] = __floats2bfloat162_rn(r0, r1);
+    }
+    yi[i] = v;
+  }
 }
 
 __global__ void gn_apply_cl_bf16x8_tab_kernel(__nv_bfloat16* y, const __nv_bfloat16* x, const float2* tab, int64_t HW,
@@ -529,8 +598,11 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
   double* part = (double*)ws;
   float* stats = (float*)((char*)ws + gn_part_bytes(N, G));
   float2* tab = (float2*)((char*)ws + gn_part_bytes(N, G) + gn_stats_bytes(N, G));
-  const int chunks = gn_chunks(C, HW, G, cl);
   const bool vec_in = cl && xd == MT_BF16 && C % 8 == 0 && (uintptr_t)x % 16 == 0 && (xs[0] * 2) % 16 == 0;
+  // the vectorised channels-last path walks chunks of 40960 / C pixels (128 at 320 channels, 32 at
+  // 1280; between 16 and 128): long enough CTAs for narrow images, enough CTAs for wide ones
+  const int64_t gn_px = std::max<int64_t>(16, std::min<int64_t>(128, 40960 / C));
+  const int chunks = vec_in ? (int)std::min<int64_t>(kGnMaxChunks, (HW + gn_px - 1) / gn_px) : gn_chunks(C, HW, G, cl);
   if (vec_in) {
     const int64_t V = C / 8;
     const int64_t slots = (V >= kGnThreads ? 1 : kGnThreads / V) * C;
@@ -548,12 +620,33 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
   }
   int rc = check_launch("group_norm partial");
   if (rc) return rc;
+  const bool ycl = (ys[1] == 1 && ys[2] == C && ys[0] == HW * C);
+  const int64_t total = N * C * HW;
+  if (vec_in && ycl && xs[0] == HW * C && yd == MT_BF16 && (uintptr_t)y % 16 == 0 && HW * C / 8 < (1LL << 31)) {
+    gn_finalize_table_kernel<<<(unsigned)((N * G * 32 + 255) / 256), 256, 0, st>>>(
+        part, w, b, wbd, N, C, G, chunks, (double)(C / G) * (double)HW, eps, tab);
+    rc = check_launch("group_norm finalize");
+    if (rc) return rc;
+    const int per_img8 = (int)(HW * C / 8);
+    const int C8 = (int)(C / 8);
+    // blocks per image: a multiple of C8 / gcd(C8, 256), so that the stride is a multiple of C8
+    int g = C8, r = 256;
+    while (r) {
+      const int t = g % r;
+      g = r;
+      r = t;
+    }
+    const int unit = C8 / g;
+    int bx = (int)std::max<int64_t>(1, std::min<int64_t>((per_img8 + 255) / 256, (int64_t)num_sms() * 16 / N + 1));
+    bx = (bx + unit - 1) / unit * unit;
+    gn_apply_img_bf16x8_kernel<<<dim3((unsigned)bx, (unsigned)N), 256, 0, st>>>(
+        (__nv_bfloat16*)y, (const __nv_bfloat16*)x, tab, per_img8, (int)(C / 8), silu);
+    return check_launch("group_norm apply");
+  }
   gn_finalize_kernel<<<(unsigned)((N * G + 127) / 128), 128, 0, st>>>(part, stats, N, G, chunks,
                                                                       (double)(C / G) * (double)HW, eps);
   rc = check_launch("group_norm finalize");
   if (rc) return rc;
-  const bool ycl = (ys[1] == 1 && ys[2] == C && ys[0] == HW * C);
-  const int64_t total = N * C * HW;
   if (vec_in && ycl && xs[0] == HW * C && yd == MT_BF16 && (uintptr_t)y % 16 == 0) {
     gn_table_kernel<<<(unsigned)((N * C + 255) / 256), 256, 0, st>>>(stats, w, b, wbd, N, C, G, tab);
     rc = check_launch("group_norm table");
