@@ -147,62 +147,107 @@ __global__ void __launch_bounds__(NT) layer_norm_kernel(void* y, int yd, const v
   }
 }
 
-// bf16 rows of cols = 8*k <= 8*32*VPL elements: one warp per row, 16-byte loads, the row held in
-// registers (VPL vectors per lane), two-pass mean / variance, 16-byte stores.
-template <int VPL>
+// Eight consecutive affine parameters starting at c0 (a multiple of 8) as floats: one 16-byte load
+// for bf16, two for fp32 when the array is 16-byte aligned, else element by element.
+__device__ __forceinline__ void load8_f32(const void* p, int dtype, int c0, float (&o)[8]) {
+  const bool al = (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+  if (dtype == MT_BF16 && al) {
+    const uint4 u = reinterpret_cast<const uint4*>(p)[c0 / 8];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      o[2 * j] = f.x;
+      o[2 * j + 1] = f.y;
+    }
+  } else if (dtype == MT_F32 && al) {
+    const float4 a = reinterpret_cast<const float4*>(p)[c0 / 4], b = reinterpret_cast<const float4*>(p)[c0 / 4 + 1];
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = load_as_f32(p, c0 + j, dtype);
+  }
+}
+
+// bf16 rows of cols = 8*k <= 8*32*VPL elements: RPW rows per warp (their loads all in flight before
+// any reduction), 16-byte loads, rows held in registers (VPL vectors per lane and row), two-pass
+// mean / variance, 16-byte stores, affine parameters loaded 8 at a time.
+template <int VPL, int RPW>
 __global__ void __launch_bounds__(256) layer_norm_bf16_warp_kernel(__nv_bfloat16* y, const __nv_bfloat16* x,
                                                                    const void* w, const void* b, int wbd,
                                                                    int64_t rows, int cols, float eps) {
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  if (row0 >= rows) return;
   const int nv = cols / 8;
-  const uint4* src = reinterpret_cast<const uint4*>(x + row * cols);
-  float v[VPL][8];
-  float s = 0.f;
+  float v[RPW][VPL][8];
+  float s[RPW];
 #pragma unroll
-  for (int k = 0; k < VPL; ++k) {
-    const int vi = lane + 32 * k;
-    if (vi < nv) {
-      uint4 u = src[vi];
+  for (int r = 0; r < RPW; ++r) {
+    s[r] = 0.f;
+    const bool live = row0 + r < rows;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (row0 + r) * cols);
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int vi = lane + 32 * k;
+      uint4 u = make_uint4(0u, 0u, 0u, 0u);
+      if (live && vi < nv) u = src[vi];
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __bfloat1622float2(h[j]);
-        v[k][2 * j] = f.x;
-        v[k][2 * j + 1] = f.y;
-        s += f.x + f.y;
+        v[r][k][2 * j] = f.x;
+        v[r][k][2 * j + 1] = f.y;
       }
     }
   }
-  const float mean = warp_sum(s) / (float)cols;
-  float q = 0.f;
 #pragma unroll
-  for (int k = 0; k < VPL; ++k)
-    if (lane + 32 * k < nv)
+  for (int r = 0; r < RPW; ++r)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) q += (v[k][j] - mean) * (v[k][j] - mean);
-  const float inv = rsqrtf(warp_sum(q) / (float)cols + eps);
-  uint4* dst = reinterpret_cast<uint4*>(y + row * cols);
+    for (int k = 0; k < VPL; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[r] += v[r][k][j];
+  float mean[RPW], inv[RPW], q[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) mean[r] = warp_sum(s[r]) / (float)cols;
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    q[r] = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k)
+      if (lane + 32 * k < nv)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[r] += (v[r][k][j] - mean[r]) * (v[r][k][j] - mean[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) inv[r] = rsqrtf(warp_sum(q[r]) / (float)cols + eps);
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
     const int vi = lane + 32 * k;
-    if (vi < nv) {
+    if (vi >= nv) continue;
+    float gw[8], gb[8];
+    if (w) {
+      load8_f32(w, wbd, vi * 8, gw);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gw[j] = 1.f;
+    }
+    if (b) {
+      load8_f32(b, wbd, vi * 8, gb);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gb[j] = 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      if (row0 + r >= rows) break;
       uint32_t o[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float r[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int c = vi * 8 + 2 * j + e;
-          float t = (v[k][2 * j + e] - mean) * inv;
-          if (w) t *= load_as_f32(w, c, wbd);
-          if (b) t += load_as_f32(b, c, wbd);
-          r[e] = t;
-        }
-        o[j] = pack_bf16x2(r[0], r[1]);
-      }
-      dst[vi] = make_uint4(o[0], o[1], o[2], o[3]);
+      for (int j = 0; j < 4; ++j)
+        o[j] = pack_bf16x2((v[r][k][2 * j] - mean[r]) * inv[r] * gw[2 * j] + gb[2 * j],
+                           (v[r][k][2 * j + 1] - mean[r]) * inv[r] * gw[2 * j + 1] + gb[2 * j + 1]);
+      reinterpret_cast<uint4*>(y + (row0 + r) * cols)[vi] = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
@@ -213,17 +258,17 @@ int launch_layer_norm(void* y, int yd, const void* x, int xd, const void* w, con
   if (rows > 0x7fffffffLL) return fail(MT_ERR_UNSUPPORTED, "layer_norm: too many rows");
   if (xd == MT_BF16 && yd == MT_BF16 && cols % 8 == 0 && cols <= 8 * 32 * 8 && (uintptr_t)x % 16 == 0 &&
       (uintptr_t)y % 16 == 0 && rows / 8 < 0x7fffffffLL) {
-    const unsigned grid = (unsigned)((rows + 7) / 8);
     const int vpl = (int)((cols / 8 + 31) / 32);
+    const unsigned grid2 = (unsigned)((rows + 15) / 16), grid1 = (unsigned)((rows + 7) / 8);
     if (vpl <= 2)
-      layer_norm_bf16_warp_kernel<2><<<grid, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd, rows,
-                                                           (int)cols, (float)eps);
+      layer_norm_bf16_warp_kernel<2, 2><<<grid2, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd,
+                                                               rows, (int)cols, (float)eps);
     else if (vpl <= 4)
-      layer_norm_bf16_warp_kernel<4><<<grid, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd, rows,
-                                                           (int)cols, (float)eps);
+      layer_norm_bf16_warp_kernel<4, 2><<<grid2, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd,
+                                                               rows, (int)cols, (float)eps);
     else
-      layer_norm_bf16_warp_kernel<8><<<grid, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd, rows,
-                                                           (int)cols, (float)eps);
+      layer_norm_bf16_warp_kernel<8, 1><<<grid1, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd,
+                                                               rows, (int)cols, (float)eps);
     return check_launch("layer_norm_bf16_warp");
   }
   if (cols <= 512)
