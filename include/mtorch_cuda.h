@@ -207,6 +207,26 @@ int mt_cuda_conv2d_pack_weight(void* w_packed, void* w_lo, const void* w, int dt
                                int64_t R, int64_t S, void* stream);
 
 /*
+ * 3x3 convolution (stride 1, padding 1, dilation 1) of the nearest-2x upsample of x, without
+ * forming the upsampled tensor.  Replaces the up-block pair `interpolate(scale_factor=2,
+ * mode="nearest")` (tensor.cpp:10897) + `conv2d` (tensor.cpp:26490-27528) of the SD UNet
+ * (scenario benchmarking.py:5981-6000).  The descriptor is the convolution's own: x [N, C, H, W]
+ * at the SOURCE resolution, weight [K, C, 3, 3], R = S = 3, pad 1, stride 1, P = 2H, Q = 2W,
+ * output [N, K, 2H, 2W] channels-last with 16-byte aligned rows.  Each output parity (2i+a, 2j+b)
+ * is a 2x2 convolution of the source with taps summed from the 3x3 taps, so the work is 16/36
+ * of the upsample-then-convolve FLOPs.  Needs C to fill whole 128-byte chunks (C % 64 == 0 for
+ * bf16/f16, C % 32 == 0 for fp32); other cases return MT_ERR_UNSUPPORTED (the caller upsamples
+ * and convolves instead).  w_packed = 1: `w` holds mt_cuda_conv2d_up2x_packed_elems elements
+ * from mt_cuda_conv2d_up2x_pack_weight ([4 parities][K][2][2][Cp]), w_lo its tf32 low parts
+ * (MT_F32) or NULL.
+ */
+size_t mt_cuda_conv2d_up2x_workspace_size(const mt_conv2d_desc* desc);
+int mt_cuda_conv2d_up2x(const mt_conv2d_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+int64_t mt_cuda_conv2d_up2x_packed_elems(int64_t K, int64_t C, int dtype);
+int mt_cuda_conv2d_up2x_pack_weight(void* w_packed, void* w_lo, const void* w, int dtype, int64_t K, int64_t C,
+                                    void* stream);
+
+/*
  * Fused attention O = softmax(Q K^T * scale + mask) V.  Replaces
  * `scaled_dot_product_attention` (tensor.cpp:30930-31324; portable loop 31158-31207).
  * Q [B, H, Sq, D], K [B, Hkv, Sk, D], V [B, Hkv, Sk, Dv], O [B, H, Sq, Dv], each with element

@@ -105,6 +105,10 @@ SIGNATURES = {
     "mt_cuda_conv2d": (C.c_int, [C.POINTER(Conv2dDesc), VP, C.c_size_t, VP]),
     "mt_cuda_conv2d_packed_channels": (I64, [I64, I64, I64, C.c_int]),
     "mt_cuda_conv2d_pack_weight": (C.c_int, [VP, VP, VP, C.c_int, I64, I64, I64, I64, VP]),
+    "mt_cuda_conv2d_up2x_workspace_size": (C.c_size_t, [C.POINTER(Conv2dDesc)]),
+    "mt_cuda_conv2d_up2x": (C.c_int, [C.POINTER(Conv2dDesc), VP, C.c_size_t, VP]),
+    "mt_cuda_conv2d_up2x_packed_elems": (I64, [I64, I64, C.c_int]),
+    "mt_cuda_conv2d_up2x_pack_weight": (C.c_int, [VP, VP, VP, C.c_int, I64, I64, VP]),
     "mt_cuda_sdpa_workspace_size": (C.c_size_t, [C.POINTER(SdpaDesc)]),
     "mt_cuda_sdpa": (C.c_int, [C.POINTER(SdpaDesc), VP, C.c_size_t, VP]),
     "mt_rng_seed": (None, [C.POINTER(RngState), C.c_uint64]),

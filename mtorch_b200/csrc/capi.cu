@@ -238,6 +238,19 @@ int mt_cuda_conv2d_pack_weight(void* w_packed, void* w_lo, const void* w, int dt
   return launch_conv_pack_weight(w_packed, (float*)w_lo, w, dtype, K, C, R, S_, Cp, S(stream));
 }
 
+size_t mt_cuda_conv2d_up2x_workspace_size(const mt_conv2d_desc* desc) { return desc ? conv_up2x_workspace(*desc) : 0; }
+int mt_cuda_conv2d_up2x(const mt_conv2d_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!desc) return fail(MT_ERR_INVALID, "conv2d_up2x: null descriptor");
+  return run_conv2d_up2x(*desc, workspace, workspace_bytes, S(stream));
+}
+int64_t mt_cuda_conv2d_up2x_packed_elems(int64_t K, int64_t C, int dtype) { return conv_up2x_packed_elems(K, C, dtype); }
+int mt_cuda_conv2d_up2x_pack_weight(void* w_packed, void* w_lo, const void* w, int dtype, int64_t K, int64_t C,
+                                    void* stream) {
+  if (!w_packed && !w_lo) return fail(MT_ERR_INVALID, "conv2d_up2x pack: no output");
+  return launch_conv_up2x_pack_weight(w_packed, (float*)w_lo, w, dtype, K, C, conv_packed_channels(C, 2, 2, dtype),
+                                      S(stream));
+}
+
 size_t mt_cuda_sdpa_workspace_size(const mt_sdpa_desc* desc) { return desc ? sdpa_workspace(*desc) : 0; }
 int mt_cuda_sdpa(const mt_sdpa_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
   if (!desc) return fail(MT_ERR_INVALID, "sdpa: null descriptor");

@@ -260,6 +260,56 @@ __global__ void conv_pack_weight_kernel(T* out, float* lo, const T* w, int64_t K
   }
 }
 
+// Weights of a 3x3 convolution applied to a nearest-2x upsampled input, regrouped per output
+// parity.  Output row 2i+a reads upsampled rows 2i+a-1 .. 2i+a+1, i.e. source rows
+// a = 0: {i-1: tap 0, i: taps 1+2},  a = 1: {i: taps 0+1, i+1: tap 2}  (columns likewise), so each
+// parity (a, b) is a 2x2 convolution of the source whose taps are sums of the 3x3 taps.
+// out: [4 = 2a+b][K][2][2][Cp] (sums formed in fp32, then rounded once); lo: tf32 low parts.
+template <typename T>
+__global__ void conv_up2x_pack_weight_kernel(T* out, float* lo, const T* w, int64_t K, int64_t C, int64_t Cp) {
+  const int64_t n = 4 * K * 4 * Cp;
+  MT_GRID_STRIDE(i, n) {
+    const int64_t c = i % Cp;
+    int64_t t = i / Cp;
+    const int v = (int)(t % 2); t /= 2;
+    const int u = (int)(t % 2); t /= 2;
+    const int64_t k = t % K;
+    const int par = (int)(t / K);
+    const int a = par >> 1, b = par & 1;
+    // 3x3 taps [r0, r1] feeding 2x2 tap u (rows) for parity a; likewise columns
+    const int r0 = a == 0 ? (u == 0 ? 0 : 1) : (u == 0 ? 0 : 2);
+    const int r1 = a == 0 ? (u == 0 ? 0 : 2) : (u == 0 ? 1 : 2);
+    const int s0 = b == 0 ? (v == 0 ? 0 : 1) : (v == 0 ? 0 : 2);
+    const int s1 = b == 0 ? (v == 0 ? 0 : 2) : (v == 0 ? 1 : 2);
+    float acc = 0.f;
+    if (c < C)
+      for (int r = r0; r <= r1; ++r)
+        for (int s = s0; s <= s1; ++s) acc += to_f32<T>(w[((k * C + c) * 3 + r) * 3 + s]);
+    if (out) out[i] = from_f32<T>(acc);
+    if (lo) lo[i] = tf32_lo(acc);
+  }
+}
+
+int launch_conv_up2x_pack_weight(void* out, float* lo, const void* w, int dtype, int64_t K, int64_t C, int64_t Cp,
+                                 cudaStream_t st) {
+  const int64_t n = 16 * K * Cp;
+  switch (dtype) {
+    case MT_F32:
+      conv_up2x_pack_weight_kernel<float><<<grid_for(n, 256), 256, 0, st>>>((float*)out, lo, (const float*)w, K, C, Cp);
+      break;
+    case MT_BF16:
+      conv_up2x_pack_weight_kernel<__nv_bfloat16><<<grid_for(n, 256), 256, 0, st>>>(
+          (__nv_bfloat16*)out, nullptr, (const __nv_bfloat16*)w, K, C, Cp);
+      break;
+    case MT_F16:
+      conv_up2x_pack_weight_kernel<__half><<<grid_for(n, 256), 256, 0, st>>>((__half*)out, nullptr, (const __half*)w,
+                                                                              K, C, Cp);
+      break;
+    default: return fail(MT_ERR_UNSUPPORTED, "conv up2x weight pack: dtype");
+  }
+  return check_launch("conv_up2x_pack_weight");
+}
+
 // im2col for the general convolution path: col[(n*P+p)*Q+q][(r*S+s)*Cp + c] (zero padded in
 // space and channels); x addressed through its own (n, c, h, w) strides.
 template <typename T>

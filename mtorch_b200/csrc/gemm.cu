@@ -816,8 +816,12 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
       if (rc) return rc;
     }
   }
-  // Output / residual must be channels-last for the epilogue's unit column stride.
-  const bool y_cl = is_channels_last(d.y_strides, d.K, d.P, d.Q) && aligned16(d.y);
+  // The epilogue needs a unit channel stride; any (n, p, q) strides whose rows stay 16-byte
+  // aligned are written in place (dense channels-last, a channel slice, a parity sub-grid).
+  const int64_t oes_ = dtype_size(d.out_dtype);
+  const bool y_cl = d.y_strides[1] == 1 && aligned16(d.y) && (d.y_strides[0] * oes_) % 16 == 0 &&
+                    (d.y_strides[2] * oes_) % 16 == 0 && (d.y_strides[3] * oes_) % 16 == 0 &&
+                    d.y_strides[3] >= d.K;
   void* yout = d.y;
   int64_t ys[4] = {d.y_strides[0], d.y_strides[1], d.y_strides[2], d.y_strides[3]};
   if (!y_cl) {
@@ -985,6 +989,123 @@ int run_conv2d(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStream_t
     rc = launch_copy_strided(d.y, d.out_dtype, d.y_strides, L.ep.D, d.out_dtype, cl, sizes, 4, st);
   }
   return rc;
+}
+
+// ---------------------------------------------------------------------------------------------
+// 3x3 convolution (pad 1, stride 1) of a nearest-2x upsampled input without materialising it:
+// four 2x2 implicit-GEMM convolutions of the source, one per output parity (a, b), with taps
+// pre-summed per parity (launch_conv_up2x_pack_weight).  Parity (a, b) output (i, j) lands at
+// (2i + a, 2j + b) and reads source rows i - 1 + a .. i + a (columns likewise): top / left padding
+// 1 - a / 1 - b with P = H, Q = W.
+
+int64_t conv_up2x_packed_elems(int64_t K, int64_t C, int dtype) {
+  return 16 * K * conv_packed_channels(C, 2, 2, dtype);
+}
+
+static int validate_conv_up2x(const mt_conv2d_desc& d) {
+  if (d.N < 0 || d.C <= 0 || d.H <= 0 || d.W <= 0 || d.K <= 0) return fail(MT_ERR_INVALID, "conv2d_up2x: bad sizes");
+  if (d.R != 3 || d.S != 3 || d.stride_h != 1 || d.stride_w != 1 || d.pad_h != 1 || d.pad_w != 1 || d.dil_h != 1 ||
+      d.dil_w != 1 || d.groups != 1)
+    return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: only 3x3, stride 1, padding 1, dilation 1, groups 1");
+  if (d.P != 2 * d.H || d.Q != 2 * d.W) return fail(MT_ERR_INVALID, "conv2d_up2x: output must be [2H, 2W]");
+  if (d.dtype != MT_F32 && d.dtype != MT_BF16 && d.dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: dtype %d", d.dtype);
+  if (d.out_dtype != MT_F32 && d.out_dtype != MT_BF16 && d.out_dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: output dtype %d", d.out_dtype);
+  if (d.epilogue == MT_EPI_GEGLU) return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: GEGLU epilogue");
+  mt_conv2d_desc e = d;
+  e.R = e.S = 2;
+  if (!conv_implicit_ok(e)) return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: channels must fill whole 128-byte chunks");
+  const int oes = dtype_size(d.out_dtype);
+  if (d.y_strides[1] != 1 || (2 * d.y_strides[2] * oes) % 16 || (2 * d.y_strides[3] * oes) % 16 ||
+      (d.y_strides[0] * oes) % 16 || (reinterpret_cast<uintptr_t>(d.y) % 16))
+    return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: output must be channels-last with 16-byte aligned rows");
+  if (d.residual && (d.res_strides[1] != 1 || (2 * d.res_strides[2] * oes) % 16 || (2 * d.res_strides[3] * oes) % 16 ||
+                     (d.res_strides[0] * oes) % 16 || (reinterpret_cast<uintptr_t>(d.residual) % 16)))
+    return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: residual must be channels-last with 16-byte aligned rows");
+  if (d.N > 0 && (!d.x || !d.w || !d.y)) return fail(MT_ERR_INVALID, "conv2d_up2x: null operand");
+  return MT_OK;
+}
+
+// The per-parity descriptor: 2x2 taps over the source, packed weights of that parity.
+static mt_conv2d_desc up2x_parity_desc(const mt_conv2d_desc& d, int par, const void* wp, const float* wlo) {
+  const int a = par >> 1, b = par & 1;
+  const int oes = dtype_size(d.out_dtype);
+  const int64_t Cp = conv_packed_channels(d.C, 2, 2, d.dtype);
+  const int64_t per = d.K * 4 * Cp;
+  mt_conv2d_desc e = d;
+  e.R = e.S = 2;
+  e.P = d.H;
+  e.Q = d.W;
+  e.pad_h = 1 - a;
+  e.pad_w = 1 - b;
+  e.w = static_cast<const char*>(wp) + (size_t)par * per * dtype_size(d.dtype);
+  e.w_packed = 1;
+  e.w_lo = wlo ? wlo + (size_t)par * per : nullptr;
+  e.y = static_cast<char*>(d.y) + (a * d.y_strides[2] + b * d.y_strides[3]) * oes;
+  e.y_strides[2] = 2 * d.y_strides[2];
+  e.y_strides[3] = 2 * d.y_strides[3];
+  if (d.residual) {
+    e.residual = static_cast<const char*>(d.residual) + (a * d.res_strides[2] + b * d.res_strides[3]) * oes;
+    e.res_strides[2] = 2 * d.res_strides[2];
+    e.res_strides[3] = 2 * d.res_strides[3];
+  }
+  return e;
+}
+
+size_t conv_up2x_workspace(const mt_conv2d_desc& d) {
+  if (validate_conv_up2x(d) != MT_OK) return 0;
+  const bool tf32 = d.dtype == MT_F32;
+  const size_t elems = (size_t)conv_up2x_packed_elems(d.K, d.C, d.dtype);
+  size_t pack = 0;
+  if (!d.w_packed) pack += align_up(elems * dtype_size(d.dtype), 256);
+  if (tf32 && (!d.w_packed || !d.w_lo)) pack += align_up(elems * 4, 256);
+  // the four parity plans reuse one region after the packed weights (stream-ordered launches);
+  // with packed low parts present a plan needs no per-call weight split
+  mt_conv2d_desc e = up2x_parity_desc(d, 0, d.w, tf32 ? reinterpret_cast<const float*>(d.w) : nullptr);
+  WsCursor ws{nullptr, 0};
+  plan_conv(e, ws, false, nullptr, nullptr);
+  return pack + 256 + ws.off;
+}
+
+int run_conv2d_up2x(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st) {
+  int rc = validate_conv_up2x(d);
+  if (rc) return rc;
+  if (d.N == 0) return MT_OK;
+  const size_t need = conv_up2x_workspace(d);
+  if (need > 0 && (!wsp || ws_bytes < need))
+    return fail(MT_ERR_WORKSPACE, "conv2d_up2x: workspace of %zu bytes required", need);
+  const bool tf32 = d.dtype == MT_F32;
+  const int64_t Cp = conv_packed_channels(d.C, 2, 2, d.dtype);
+  const int64_t elems = conv_up2x_packed_elems(d.K, d.C, d.dtype);
+  WsCursor ws{(char*)wsp, 0};
+  const void* wp = d.w;
+  const float* wlo = static_cast<const float*>(d.w_lo);
+  if (!d.w_packed) {
+    void* dst = ws.take((size_t)elems * dtype_size(d.dtype));
+    float* lo = tf32 ? (float*)ws.take((size_t)elems * 4) : nullptr;
+    rc = launch_conv_up2x_pack_weight(dst, lo, d.w, d.dtype, d.K, d.C, Cp, st);
+    if (rc) return rc;
+    wp = dst;
+    wlo = lo;
+  } else if (tf32 && !wlo) {
+    float* lo = (float*)ws.take((size_t)elems * 4);
+    rc = launch_pack2d(nullptr, lo, d.w, MT_F32, 1, 4 * d.K, 4 * Cp, 4 * Cp, 1, 0, 4 * Cp, st);
+    if (rc) return rc;
+    wlo = lo;
+  }
+  const size_t base = align_up(ws.off, 256);
+  for (int par = 0; par < 4; ++par) {
+    const mt_conv2d_desc e = up2x_parity_desc(d, par, wp, wlo);
+    WsCursor wsp2{(char*)wsp, base};
+    GemmLaunch L{};
+    rc = plan_conv(e, wsp2, true, st, &L);
+    if (rc) return rc;
+    if (L.ep.D != e.y) return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: output layout");
+    rc = dispatch(L, st);
+    if (rc) return rc;
+  }
+  return MT_OK;
 }
 
 }  // namespace mt

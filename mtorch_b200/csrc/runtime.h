@@ -58,6 +58,8 @@ int launch_pack2d(void* out, float* lo, const void* in, int dtype, int64_t batch
                   int64_t sr, int64_t sc, int64_t sb, int64_t out_pitch, cudaStream_t st);
 int launch_conv_pack_weight(void* out, float* lo, const void* w, int dtype, int64_t K, int64_t C, int64_t R,
                             int64_t S, int64_t Cp, cudaStream_t st);
+int launch_conv_up2x_pack_weight(void* out, float* lo, const void* w, int dtype, int64_t K, int64_t C, int64_t Cp,
+                                 cudaStream_t st);
 int launch_im2col(void* col, float* lo, const void* x, int dtype, const mt_conv2d_desc& d, int64_t Cp, int64_t Kp,
                   cudaStream_t st);
 
@@ -76,6 +78,9 @@ size_t gemm_workspace(const mt_gemm_desc& d);
 int run_gemm(const mt_gemm_desc& d, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t conv_workspace(const mt_conv2d_desc& d);
 int run_conv2d(const mt_conv2d_desc& d, void* ws, size_t ws_bytes, cudaStream_t st);
+int64_t conv_up2x_packed_elems(int64_t K, int64_t C, int dtype);
+size_t conv_up2x_workspace(const mt_conv2d_desc& d);
+int run_conv2d_up2x(const mt_conv2d_desc& d, void* ws, size_t ws_bytes, cudaStream_t st);
 int64_t conv_packed_channels(int64_t C, int64_t R, int64_t S, int dtype);
 
 // attention.cu

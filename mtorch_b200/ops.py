@@ -283,6 +283,68 @@ def pack_conv_weight(w: Tensor):
     return wp, lo
 
 
+def conv2d_up2x_supported(x: Tensor, w: Tensor) -> bool:
+    """Whether `conv2d_up2x` takes this input: a 3x3 weight and channels filling whole 128-byte
+    chunks (64 for bf16/f16, 32 for fp32)."""
+    per = 128 // x.dtype.itemsize
+    return (x.dim() == 4 and w.dim() == 4 and tuple(w._shape[2:]) == (3, 3) and x._shape[1] % per == 0
+            and x.dtype is w.dtype)
+
+
+def conv2d_up2x(x: Tensor, w: Tensor, bias: Tensor | None = None, *, packed=None) -> Tensor:
+    """conv2d(interpolate(x, scale_factor=2, mode="nearest"), w, bias, stride=1, padding=1) for a
+    3x3 weight, without forming the upsampled tensor (the SD UNet up-block pair,
+    tensor.cpp:10897 + 26490-27528): four 2x2 convolutions of the source, one per output parity,
+    with the 3x3 taps summed per parity.  Output [N, K, 2H, 2W] channels-last.  `packed`: the
+    result of `pack_conv_up2x_weight(w)`."""
+    _require_cuda(x, w, bias)
+    _same_dtype(x, w, what="conv2d")
+    if not conv2d_up2x_supported(x, w):
+        raise NotImplementedError("conv2d_up2x: needs a 3x3 weight and channels filling 128-byte chunks")
+    N, Cin, H, W = x._shape
+    K = w._shape[0]
+    if w._shape[1] != Cin:
+        raise RuntimeError(f"conv2d_up2x: weight expects {w._shape[1]} input channels, got {Cin}")
+    y = _new((N, K, 2 * H, 2 * W), x.dtype, x.device, channels_last=True)
+    d = L.Conv2dDesc()
+    d.N, d.C, d.H, d.W, d.K, d.R, d.S, d.P, d.Q = N, Cin, H, W, K, 3, 3, 2 * H, 2 * W
+    d.stride_h, d.stride_w, d.pad_h, d.pad_w, d.dil_h, d.dil_w, d.groups = 1, 1, 1, 1, 1, 1, 1
+    d.dtype = d.out_dtype = x.dtype.code
+    d.x = x.data_ptr()
+    d.x_strides[:] = list(x._strides)
+    if packed is not None:
+        d.w, d.w_packed = packed[0].data_ptr(), 1
+        d.w_lo = packed[1].data_ptr() if packed[1] is not None else None
+    else:
+        wc = w.contiguous()
+        d.w, d.w_packed = wc.data_ptr(), 0
+    if bias is not None:
+        bias = bias.contiguous()
+        d.bias, d.bias_dtype, d.bias_batch_stride = bias.data_ptr(), bias.dtype.code, 0
+    d.y = y.data_ptr()
+    d.y_strides[:] = list(y._strides)
+    d.epilogue = int(L.EPI_NONE)
+    lib = _lib()
+    need = lib.mt_cuda_conv2d_up2x_workspace_size(C.byref(d))
+    ws, wsb = workspace(need, x._idx())
+    L.check(lib.mt_cuda_conv2d_up2x(C.byref(d), ws, wsb, x._stream()), "conv2d_up2x")
+    return y
+
+
+def pack_conv_up2x_weight(w: Tensor):
+    """[K, C, 3, 3] -> (per-parity 2x2 weights [4, K, 2, 2, Cp], tf32 low part or None)."""
+    _require_cuda(w)
+    K, Cin = w._shape[0], w._shape[1]
+    n = _lib().mt_cuda_conv2d_up2x_packed_elems(K, Cin, w.dtype.code)
+    wp = _new((n,), w.dtype, w.device)
+    lo = _new((n,), float32, w.device) if w.dtype is float32 else None
+    wc = w.contiguous()
+    L.check(_lib().mt_cuda_conv2d_up2x_pack_weight(wp.data_ptr(), lo.data_ptr() if lo is not None else None,
+                                                   wc.data_ptr(), w.dtype.code, K, Cin, w._stream()),
+            "pack up2x weight")
+    return wp, lo
+
+
 # ---------------------------------------------------------------------------------------------
 # attention (tensor.cpp:30930-31324)
 

@@ -162,11 +162,26 @@ class Downsample(Module):
 
 
 class Upsample(Module):
+    """Nearest-2x upsample + 3x3 conv (SD's up-block tail).  On the device the pair runs as one
+    fused operation (`ops.conv2d_up2x`: four 2x2 convolutions of the source, no upsampled tensor);
+    inputs it does not take go through the explicit upsample and convolution."""
+
     def __init__(self, c, device=None, dtype=None):
         super().__init__()
         self.conv = Conv2d(c, c, 3, padding=1, device=device, dtype=dtype)
+        self._packed_up = None
+
+    def packed_up2x_weight(self):
+        w = self.conv.weight
+        key = (id(w), w._version, w.dtype.name, str(w.device))
+        if self._packed_up is None or self._packed_up[0] != key:
+            self._packed_up = (key, ops.pack_conv_up2x_weight(w))
+        return self._packed_up[1]
 
     def forward(self, x):
+        w = self.conv.weight
+        if x.device.type == "cuda" and ops.conv2d_up2x_supported(x, w):
+            return ops.conv2d_up2x(x, w, self.conv.bias, packed=self.packed_up2x_weight())
         return self.conv(ops.interpolate_nearest2x(x))
 
 

@@ -271,6 +271,44 @@ def test_conv2d_bf16(shape, K, k, stride, pad):
     check(conv(xl).numpy(), ref, BF16_RTOL)
 
 
+def _up2(a):
+    return a.repeat(2, 2).repeat(2, 3)
+
+
+@pytest.mark.parametrize("shape,K", [((2, 320, 8, 8), 320), ((1, 640, 5, 7), 64), ((2, 1280, 4, 4), 1280),
+                                     ((1, 64, 3, 9), 128)])
+def test_conv2d_up2x_bf16(shape, K):
+    """Fused nearest-2x upsample + 3x3 conv (four 2x2 parity convolutions of the source) against
+    the oracle's conv of the explicitly upsampled input, and against the device's explicit pair."""
+    from mtorch_b200 import ops
+    x, w, b = rnd(*shape), rnd(K, shape[1], 3, 3, seed=1, scale=0.05), rnd(K, seed=2)
+    ref = oracle.conv2d_f32(_up2(bf16_round(x)), bf16_round(w), bf16_round(b), 1, 1)
+    xd = cu(x, "bfloat16").contiguous(memory_format=mt.channels_last)
+    wd, bd = cu(w, "bfloat16"), cu(b, "bfloat16")
+    got = ops.conv2d_up2x(xd, wd, bd)
+    assert got.shape == (shape[0], K, 2 * shape[2], 2 * shape[3]) and got.is_contiguous(mt.channels_last)
+    check(got.numpy(), ref, BF16_RTOL)
+    check(ops.conv2d_up2x(xd, wd, bd, packed=ops.pack_conv_up2x_weight(wd)).numpy(), ref, BF16_RTOL)
+    explicit = mt.conv2d(ops.interpolate_nearest2x(xd), wd, bd, 1, 1).numpy()
+    check(got.numpy(), explicit, BF16_RTOL)
+
+
+def test_conv2d_up2x_fp32_and_module():
+    """fp32 (3xTF32) at the fp32 tolerance, NCHW input, and the UNet's Upsample module using it."""
+    from mtorch_b200 import ops
+    from mtorch_b200 import unet as U
+    x, w, b = rnd(2, 64, 6, 5), rnd(32, 64, 3, 3, seed=1, scale=0.1), rnd(32, seed=2)
+    ref = oracle.conv2d_f32(_up2(x), w, b, 1, 1)
+    check(ops.conv2d_up2x(cu(x), cu(w), cu(b)).numpy(), ref, FP32_RTOL)
+    up = U.Upsample(64, device="cuda")
+    up.conv.weight.copy_(cu(rnd(64, 64, 3, 3, seed=3, scale=0.05), "float32"))
+    up.conv.bias.copy_(cu(rnd(64, seed=4)))
+    xm = cu(x).contiguous(memory_format=mt.channels_last)
+    ref_m = oracle.conv2d_f32(_up2(x), up.conv.weight.numpy(), up.conv.bias.numpy(), 1, 1)
+    check(up(xm).numpy(), ref_m, FP32_RTOL)
+    check(up(xm).numpy(), ref_m, FP32_RTOL)  # second call: cached packed weights
+
+
 def test_conv2d_bf16_resnet_epilogue():
     """Per-image bias (conv bias + time embedding) and the residual add fused in the epilogue."""
     N, C, H = 2, 320, 16
