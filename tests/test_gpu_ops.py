@@ -204,6 +204,15 @@ def test_linear_bf16_fused_epilogues():
     check(got, ref, BF16_RTOL)
     got = linear(cu(x, "bfloat16"), cu(w[:F], "bfloat16"), None, epilogue=_lib.EPI_SILU).numpy()
     check(got, oracle.silu_f32(oracle.linear_f32(xb, wb[:F])), BF16_RTOL)
+    # GELU epilogue over pre-activations spread across about +-8 (the 16-bit epilogue evaluates the
+    # normal CDF as a clamped polynomial; fp32 keeps the erf of the reference at 1e-4)
+    ws = rnd(F, K, seed=4, scale=0.15)
+    pre = oracle.linear_f32(xb, bf16_round(ws))
+    assert np.abs(pre).max() > 6
+    got = linear(cu(x, "bfloat16"), cu(ws, "bfloat16"), None, epilogue=_lib.EPI_GELU).numpy()
+    check(got, oracle.gelu_f32(pre), BF16_RTOL)
+    got32 = linear(cu(x), cu(ws), None, epilogue=_lib.EPI_GELU).numpy()
+    check(got32, oracle.gelu_f32(oracle.linear_f32(x, ws)), FP32_RTOL)
 
 
 def test_bmm_bf16_attention_shapes():
