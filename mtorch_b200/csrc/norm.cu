@@ -170,61 +170,54 @@ __device__ __forceinline__ void load8_f32(const void* p, int dtype, int c0, floa
   }
 }
 
-// bf16 rows of cols = 8*k <= 8*32*VPL elements: RPW rows per warp (their loads all in flight before
-// any reduction), 16-byte loads, rows held in registers (VPL vectors per lane and row), two-pass
-// mean / variance, 16-byte stores, affine parameters loaded 8 at a time.
-template <int VPL, int RPW>
-__global__ void __launch_bounds__(256) layer_norm_bf16_warp_kernel(__nv_bfloat16* y, const __nv_bfloat16* x,
-                                                                   const void* w, const void* b, int wbd,
-                                                                   int64_t rows, int cols, float eps) {
-  const int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW;
+// bf16 rows of cols = 8*k elements, LPR lanes per row (16 or 32; 32 / LPR rows per warp), VPL
+// 16-byte vectors per lane with VPL = ceil(cols / 8 / LPR), so few lanes idle (320 columns: 16
+// lanes x 3 vectors).  Rows held in registers, two-pass mean / variance reduced within the row's
+// lane group, affine parameters loaded 8 at a time, 16-byte stores.
+template <int VPL, int LPR>
+__global__ void __launch_bounds__(256) layer_norm_bf16_sub_kernel(__nv_bfloat16* y, const __nv_bfloat16* x,
+                                                                  const void* w, const void* b, int wbd, int64_t rows,
+                                                                  int cols, float eps) {
+  constexpr int RPW = 32 / LPR;
   const int lane = threadIdx.x & 31;
-  if (row0 >= rows) return;
+  const int sub = lane / LPR, l = lane % LPR;
+  const int64_t row = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW + sub;
+  const bool live = row < rows;
   const int nv = cols / 8;
-  float v[RPW][VPL][8];
-  float s[RPW];
+  const uint4* src = reinterpret_cast<const uint4*>(x + (live ? row : 0) * cols);
+  float v[VPL][8];
+  float s = 0.f;
 #pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    s[r] = 0.f;
-    const bool live = row0 + r < rows;
-    const uint4* src = reinterpret_cast<const uint4*>(x + (row0 + r) * cols);
+  for (int k = 0; k < VPL; ++k) {
+    const int vi = l + LPR * k;
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (live && vi < nv) u = src[vi];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-    for (int k = 0; k < VPL; ++k) {
-      const int vi = lane + 32 * k;
-      uint4 u = make_uint4(0u, 0u, 0u, 0u);
-      if (live && vi < nv) u = src[vi];
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        v[r][k][2 * j] = f.x;
-        v[r][k][2 * j + 1] = f.y;
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[k][2 * j] = f.x;
+      v[k][2 * j + 1] = f.y;
+      s += f.x + f.y;
     }
   }
 #pragma unroll
-  for (int r = 0; r < RPW; ++r)
+  for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / (float)cols;
+  float q = 0.f;
 #pragma unroll
-    for (int k = 0; k < VPL; ++k)
+  for (int k = 0; k < VPL; ++k)
+    if (l + LPR * k < nv)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s[r] += v[r][k][j];
-  float mean[RPW], inv[RPW], q[RPW];
+      for (int j = 0; j < 8; ++j) q += (v[k][j] - mean) * (v[k][j] - mean);
 #pragma unroll
-  for (int r = 0; r < RPW; ++r) mean[r] = warp_sum(s[r]) / (float)cols;
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    q[r] = 0.f;
-#pragma unroll
-    for (int k = 0; k < VPL; ++k)
-      if (lane + 32 * k < nv)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) q[r] += (v[r][k][j] - mean[r]) * (v[r][k][j] - mean[r]);
-  }
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) inv[r] = rsqrtf(warp_sum(q[r]) / (float)cols + eps);
+  for (int o = LPR / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float inv = rsqrtf(q / (float)cols + eps);
+  if (!live) return;
+  uint4* dst = reinterpret_cast<uint4*>(y + row * cols);
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
-    const int vi = lane + 32 * k;
+    const int vi = l + LPR * k;
     if (vi >= nv) continue;
     float gw[8], gb[8];
     if (w) {
@@ -239,16 +232,12 @@ __global__ void __launch_bounds__(256) layer_norm_bf16_warp_kernel(__nv_bfloat16
 #pragma unroll
       for (int j = 0; j < 8; ++j) gb[j] = 0.f;
     }
+    uint32_t o[4];
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      if (row0 + r >= rows) break;
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        o[j] = pack_bf16x2((v[r][k][2 * j] - mean[r]) * inv[r] * gw[2 * j] + gb[2 * j],
-                           (v[r][k][2 * j + 1] - mean[r]) * inv[r] * gw[2 * j + 1] + gb[2 * j + 1]);
-      reinterpret_cast<uint4*>(y + (row0 + r) * cols)[vi] = make_uint4(o[0], o[1], o[2], o[3]);
-    }
+    for (int j = 0; j < 4; ++j)
+      o[j] = pack_bf16x2((v[k][2 * j] - mean) * inv * gw[2 * j] + gb[2 * j],
+                         (v[k][2 * j + 1] - mean) * inv * gw[2 * j + 1] + gb[2 * j + 1]);
+    dst[vi] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -258,17 +247,24 @@ int launch_layer_norm(void* y, int yd, const void* x, int xd, const void* w, con
   if (rows > 0x7fffffffLL) return fail(MT_ERR_UNSUPPORTED, "layer_norm: too many rows");
   if (xd == MT_BF16 && yd == MT_BF16 && cols % 8 == 0 && cols <= 8 * 32 * 8 && (uintptr_t)x % 16 == 0 &&
       (uintptr_t)y % 16 == 0 && rows / 8 < 0x7fffffffLL) {
-    const int vpl = (int)((cols / 8 + 31) / 32);
-    const unsigned grid2 = (unsigned)((rows + 15) / 16), grid1 = (unsigned)((rows + 7) / 8);
-    if (vpl <= 2)
-      layer_norm_bf16_warp_kernel<2, 2><<<grid2, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd,
-                                                               rows, (int)cols, (float)eps);
-    else if (vpl <= 4)
-      layer_norm_bf16_warp_kernel<4, 2><<<grid2, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd,
-                                                               rows, (int)cols, (float)eps);
+    const int nv = (int)(cols / 8);
+    const unsigned g32 = (unsigned)((rows + 7) / 8), g16 = (unsigned)((rows + 15) / 16);
+    auto* yy = (__nv_bfloat16*)y;
+    auto* xx = (const __nv_bfloat16*)x;
+    if (nv <= 16)
+      layer_norm_bf16_sub_kernel<1, 16><<<g16, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+    else if (nv <= 32)
+      layer_norm_bf16_sub_kernel<2, 16><<<g16, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+    else if (nv <= 48)
+      layer_norm_bf16_sub_kernel<3, 16><<<g16, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+    else if (nv <= 96)
+      layer_norm_bf16_sub_kernel<3, 32><<<g32, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+    else if (nv <= 128)
+      layer_norm_bf16_sub_kernel<4, 32><<<g32, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+    else if (nv <= 160)
+      layer_norm_bf16_sub_kernel<5, 32><<<g32, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
     else
-      layer_norm_bf16_warp_kernel<8, 1><<<grid1, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)x, w, b, wbd,
-                                                               rows, (int)cols, (float)eps);
+      layer_norm_bf16_sub_kernel<8, 32><<<g32, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
     return check_launch("layer_norm_bf16_warp");
   }
   if (cols <= 512)
