@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_cl_kernel(const void* x
 // Channels-last bf16 partial sums, 8 channels (16 bytes) per load: V = C/8 vectors per pixel,
 // thread t owns vector t % V of pixel lane t / V; one (lane, channel) slot per thread and
 // channel in shared memory keeps the reduction order fixed.
-__global__ void __launch_bounds__(kGnThreads, 6) gn_partial_cl_bf16x8_kernel(const __nv_bfloat16* x, int64_t sn,
+__global__ void __launch_bounds__(kGnThreads, 5) gn_partial_cl_bf16x8_kernel(const __nv_bfloat16* x, int64_t sn,
                                                                           int64_t C, int64_t HW, int64_t G,
                                                                           int chunks, double* part) {
   extern __shared__ float gn_sh[];  // [2][lanes * C]
@@ -349,16 +349,26 @@ __global__ void __launch_bounds__(kGnThreads, 6) gn_partial_cl_bf16x8_kernel(con
     float s[8], q[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j] = q[j] = 0.f;
-    for (int64_t p = p0 + lane; p < p1; p += lanes) {
-      uint4 u = *reinterpret_cast<const uint4*>(xb + p * C + v * 8);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    // four pixels' 16-byte loads in flight per thread (those past the chunk read as zero)
+    const __nv_bfloat16* xv = xb + v * 8;
+    for (int p = (int)(p0 + lane); p < p1; p += 4 * (int)lanes) {
+      uint4 u[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        s[2 * j] += f.x;
-        q[2 * j] += f.x * f.x;
-        s[2 * j + 1] += f.y;
-        q[2 * j + 1] += f.y * f.y;
+      for (int k = 0; k < 4; ++k) {
+        const int pp = p + k * (int)lanes;
+        u[k] = pp < p1 ? *reinterpret_cast<const uint4*>(xv + (int64_t)pp * C) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[k]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          s[2 * j] += f.x;
+          q[2 * j] += f.x * f.x;
+          s[2 * j + 1] += f.y;
+          q[2 * j + 1] += f.y * f.y;
+        }
       }
     }
 #pragma unroll
