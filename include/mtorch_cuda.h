@@ -73,8 +73,10 @@ int mt_cuda_fill(void* dst, int dtype, int64_t n, double value, void* stream);
 
 /* ---- elementwise ------------------------------------------------------------------------- */
 typedef enum { MT_UNARY_SILU = 0, MT_UNARY_GELU = 1, MT_UNARY_GELU_TANH = 2, MT_UNARY_NEG = 3,
-               MT_UNARY_EXP = 4, MT_UNARY_SIGMOID = 5, MT_UNARY_RELU = 6 } mt_unary_op;
-/* Replaces `silu` (tensor.cpp:16480-16600) and `gelu` (tensor.cpp:17207-17290).  Contiguous,
+               MT_UNARY_EXP = 4, MT_UNARY_SIGMOID = 5, MT_UNARY_RELU = 6,
+               MT_UNARY_QUICK_GELU = 7 } mt_unary_op;
+/* Replaces `silu` (tensor.cpp:16480-16600) and `gelu` (tensor.cpp:17207-17290); QUICK_GELU is
+ * CLIP's x * sigmoid(1.702 x) (the reference composes it, tests/compat/benchmarking.py:7714).  Contiguous,
  * n elements; x and y may alias; dtypes may differ (compute in fp32). */
 int mt_cuda_unary(int op, void* y, int y_dtype, const void* x, int x_dtype, int64_t n, void* stream);
 
@@ -96,6 +98,36 @@ int mt_cuda_axpby(void* out, int out_dtype, const void* x, int x_dtype, double a
  * out = sqrt(a_prev) x0 + sqrt(1-a_prev) eps'.  out may alias x. */
 int mt_cuda_ddim_step(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n, double alpha_t,
                       double alpha_prev, int clip, void* stream);
+
+/* The same DDIM update with the timestep read from device memory, so that one captured CUDA graph
+ * serves every step of the loop, and with classifier-free guidance folded in
+ * (tests/compat/benchmarking.py:5847-5850 for the guidance, 6148-6168 for the step):
+ *   t = *timestep (clamped to [0, num_train_steps)), t_prev = max(t - interval, 0),
+ *   a_t = alphas_cumprod[t], a_prev = alphas_cumprod[t_prev] (fp64 table on the device);
+ *   cfg != 0: eps holds 2n values [uncond; text] and the noise used is
+ *   uncond + (text - uncond) * guidance_scale (fp32, in that order); cfg == 0: eps holds n values.
+ * The result is written to out[c*n + i] for c < out_copies (1 or 2): with 2 the next step's
+ * batch-doubled model input [x; x] is produced in the same pass.  out may alias x. */
+int mt_cuda_ddim_step_indexed(void* out, int64_t out_copies, const void* x, const void* eps, int dtype, int eps_dtype,
+                              int64_t n, const double* alphas_cumprod, int64_t num_train_steps,
+                              const int64_t* timestep, int64_t interval, int cfg, double guidance_scale, int clip,
+                              void* stream);
+/* Sinusoidal timestep embedding [n, dim] of the reference's scenario
+ * (tests/compat/benchmarking.py:6011-6036): freq_j = exp((-ln(max_period) * j) / (dim/2)),
+ * arg = t * freq_j, row = [cos | sin] (flip_sin_to_cos != 0, SD's layout) or [sin | cos]; fp32
+ * math.  Row r reads timesteps[r * t_stride] (f32, f64, f16, bf16 or i64; stride 0 broadcasts one
+ * device scalar).  dim must be even. */
+int mt_cuda_timestep_embedding(void* out, int out_dtype, const void* timesteps, int t_dtype, int64_t t_stride,
+                               int64_t n, int64_t dim, double max_period, int flip_sin_to_cos, void* stream);
+
+/* Replaces `embedding` (tensor.cpp:31748-31800) for a contiguous [rows, dim] table and n int64 ids:
+ * out[r, :] = weight[ids[r], :], negative ids counted from the end.  With `add` (a second table
+ * [add_rows, dim] and its ids, e.g. CLIP's position embedding) the two rows are summed in fp32 and
+ * rounded once.  An out-of-range id writes a zero row and increments *invalid_count (device int,
+ * may be NULL): the caller raises the reference's IndexError when it is non-zero. */
+int mt_cuda_embedding(void* out, int out_dtype, const void* weight, int w_dtype, int64_t rows, int64_t dim,
+                      const int64_t* ids, int64_t n, const void* add, int add_dtype, int64_t add_rows,
+                      const int64_t* add_ids, int* invalid_count, void* stream);
 
 /* ---- normalisation / softmax ------------------------------------------------------------- */
 /* Replaces `softmax` (tensor.cpp:15145-15213, fp32 kernel 7508-7742) along the innermost,
@@ -136,7 +168,8 @@ typedef enum {
   MT_EPI_NONE = 0,
   MT_EPI_GELU = 1,  /* y = gelu(acc + bias)                                                       */
   MT_EPI_SILU = 2,  /* y = silu(acc + bias)                                                       */
-  MT_EPI_GEGLU = 3  /* B columns come in (64 value, 64 gate) groups: y[:, j] = v_j * gelu(g_j), N/2 */
+  MT_EPI_GEGLU = 3, /* B columns come in (64 value, 64 gate) groups: y[:, j] = v_j * gelu(g_j), N/2 */
+  MT_EPI_QUICK_GELU = 4 /* y = z * sigmoid(1.702 z), z = acc + bias (CLIP's MLP activation)           */
 } mt_epilogue;
 
 /*

@@ -13,9 +13,9 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmtorch_cuda.so"
 
 MT_F32, MT_BF16, MT_F16, MT_F64, MT_I32, MT_I64, MT_BOOL = range(7)
 MT_OK, MT_ERR_INVALID, MT_ERR_UNSUPPORTED, MT_ERR_LAUNCH, MT_ERR_TIMEOUT, MT_ERR_WORKSPACE = range(6)
-UNARY = {"silu": 0, "gelu": 1, "gelu_tanh": 2, "neg": 3, "exp": 4, "sigmoid": 5, "relu": 6}
+UNARY = {"silu": 0, "gelu": 1, "gelu_tanh": 2, "neg": 3, "exp": 4, "sigmoid": 5, "relu": 6, "quick_gelu": 7}
 BINARY = {"add": 0, "sub": 1, "mul": 2, "div": 3}
-EPI_NONE, EPI_GELU, EPI_SILU, EPI_GEGLU = range(4)
+EPI_NONE, EPI_GELU, EPI_SILU, EPI_GEGLU, EPI_QUICK_GELU = range(5)
 
 I64 = C.c_int64
 I64_4 = I64 * 4
@@ -92,6 +92,10 @@ SIGNATURES = {
     "mt_cuda_axpby": (C.c_int, [VP, C.c_int, VP, C.c_int, C.c_double, VP, C.c_int, C.c_double, VP, C.c_int,
                                 C.c_double, I64, VP]),
     "mt_cuda_ddim_step": (C.c_int, [VP, VP, VP, C.c_int, C.c_int, I64, C.c_double, C.c_double, C.c_int, VP]),
+    "mt_cuda_ddim_step_indexed": (C.c_int, [VP, I64, VP, VP, C.c_int, C.c_int, I64, VP, I64, VP, I64, C.c_int,
+                                            C.c_double, C.c_int, VP]),
+    "mt_cuda_timestep_embedding": (C.c_int, [VP, C.c_int, VP, C.c_int, I64, I64, I64, C.c_double, C.c_int, VP]),
+    "mt_cuda_embedding": (C.c_int, [VP, C.c_int, VP, C.c_int, I64, I64, VP, I64, VP, C.c_int, I64, VP, VP, VP]),
     "mt_cuda_softmax":(C.c_int, [VP, C.c_int, VP, C.c_int, I64, I64, I64, C.c_int, VP]),
     "mt_cuda_layer_norm": (C.c_int, [VP, C.c_int, VP, C.c_int, VP, VP, C.c_int, I64, I64, C.c_double, VP]),
     "mt_cuda_group_norm_workspace_size": (C.c_size_t, [I64, I64, I64, I64]),

@@ -172,7 +172,7 @@ int mt_cuda_fill(void* dst, int dtype, int64_t n, double value, void* stream) {
 }
 
 int mt_cuda_unary(int op, void* y, int y_dtype, const void* x, int x_dtype, int64_t n, void* stream) {
-  if (op < MT_UNARY_SILU || op > MT_UNARY_RELU) return fail(MT_ERR_UNSUPPORTED, "unary: op %d", op);
+  if (op < MT_UNARY_SILU || op > MT_UNARY_QUICK_GELU) return fail(MT_ERR_UNSUPPORTED, "unary: op %d", op);
   return launch_unary(op, y, y_dtype, x, x_dtype, n, S(stream));
 }
 
@@ -194,6 +194,44 @@ int mt_cuda_ddim_step(void* out, const void* x, const void* eps, int dtype, int 
   if (!(alpha_t > 0.0 && alpha_t < 1.0) || !(alpha_prev > 0.0 && alpha_prev <= 1.0))
     return fail(MT_ERR_INVALID, "ddim_step: alphas must lie in (0, 1)");
   return launch_ddim_step(out, x, eps, dtype, eps_dtype, n, alpha_t, alpha_prev, clip, S(stream));
+}
+
+int mt_cuda_ddim_step_indexed(void* out, int64_t out_copies, const void* x, const void* eps, int dtype, int eps_dtype,
+                              int64_t n, const double* alphas_cumprod, int64_t num_train_steps,
+                              const int64_t* timestep, int64_t interval, int cfg, double guidance_scale, int clip,
+                              void* stream) {
+  if (!out || !x || !eps || !alphas_cumprod || !timestep) return fail(MT_ERR_INVALID, "ddim_step_indexed: null pointer");
+  if (out_copies < 1 || out_copies > 2) return fail(MT_ERR_INVALID, "ddim_step_indexed: out_copies must be 1 or 2");
+  if (num_train_steps < 1 || interval < 0) return fail(MT_ERR_INVALID, "ddim_step_indexed: bad schedule");
+  if (dtype != MT_F32 && dtype != MT_BF16 && dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "ddim_step_indexed: dtype %d", dtype);
+  return launch_ddim_indexed(out, out_copies, x, eps, dtype, eps_dtype, n, alphas_cumprod, num_train_steps, timestep,
+                             interval, cfg ? 1 : 0, guidance_scale, clip, S(stream));
+}
+
+int mt_cuda_timestep_embedding(void* out, int out_dtype, const void* timesteps, int t_dtype, int64_t t_stride,
+                               int64_t n, int64_t dim, double max_period, int flip_sin_to_cos, void* stream) {
+  if (!out || !timesteps) return fail(MT_ERR_INVALID, "timestep_embedding: null pointer");
+  if (dim % 2 != 0) return fail(MT_ERR_UNSUPPORTED, "timestep_embedding: odd dim %lld", (long long)dim);
+  if (!(max_period > 1.0)) return fail(MT_ERR_INVALID, "timestep_embedding: max_period must exceed 1");
+  if (t_dtype != MT_F32 && t_dtype != MT_I64 && t_dtype != MT_F64 && t_dtype != MT_BF16 && t_dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "timestep_embedding: timestep dtype %d", t_dtype);
+  if (out_dtype != MT_F32 && out_dtype != MT_BF16 && out_dtype != MT_F16)
+    return fail(MT_ERR_UNSUPPORTED, "timestep_embedding: dtype %d", out_dtype);
+  return launch_timestep_embedding(out, out_dtype, timesteps, t_dtype, t_stride, n, dim, max_period, flip_sin_to_cos,
+                                   S(stream));
+}
+
+int mt_cuda_embedding(void* out, int out_dtype, const void* weight, int w_dtype, int64_t rows, int64_t dim,
+                      const int64_t* ids, int64_t n, const void* add, int add_dtype, int64_t add_rows,
+                      const int64_t* add_ids, int* invalid_count, void* stream) {
+  if (n > 0 && dim > 0 && (!out || !weight || !ids)) return fail(MT_ERR_INVALID, "embedding: null pointer");
+  if (add && !add_ids) return fail(MT_ERR_INVALID, "embedding: add table without ids");
+  if (rows < 0 || dim < 0) return fail(MT_ERR_INVALID, "embedding: negative size");
+  auto ok = [](int d) { return d == MT_F32 || d == MT_BF16 || d == MT_F16 || d == MT_F64; };
+  if (!ok(out_dtype) || !ok(w_dtype) || (add && !ok(add_dtype))) return fail(MT_ERR_UNSUPPORTED, "embedding: dtype");
+  return launch_embedding(out, out_dtype, weight, w_dtype, rows, dim, ids, n, add, add_dtype, add_rows, add_ids,
+                          invalid_count, S(stream));
 }
 
 int mt_cuda_softmax(void* y, int y_dtype, const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ld,

@@ -49,6 +49,16 @@ __global__ void copy_strided_kernel(void* dst, int dd, const void* src, int sd, 
   }
 }
 
+// Same-type strided copy of integer / bool elements (bit patterns moved, no conversion).
+template <typename T>
+__global__ void copy_strided_raw_kernel(T* dst, const T* src, StridedND nd, int64_t n) {
+  MT_GRID_STRIDE(i, n) {
+    int64_t od, os, unused;
+    nd_offsets(nd, i, od, os, unused);
+    dst[od] = src[os];
+  }
+}
+
 // Same-dtype strided copy in 16-byte units (offsets of `nd` are in 16-byte units).
 __global__ void copy_rows16_kernel(uint4* dst, const uint4* src, StridedND nd, int64_t n16) {
   const int64_t inner = nd.sizes[nd.ndim - 1];
@@ -126,6 +136,7 @@ __device__ __forceinline__ float apply_unary(int op, float x) {
     case MT_UNARY_EXP: return expf(x);
     case MT_UNARY_SIGMOID: return 1.0f / (1.0f + expf(-x));
     case MT_UNARY_RELU: return x > 0.f ? x : 0.f;
+    case MT_UNARY_QUICK_GELU: return x * (1.0f / (1.0f + expf(-__fmul_rn(x, 1.702f))));
     default: return x;
   }
 }
@@ -345,8 +356,9 @@ int launch_copy_strided(void* dst, int dd, const int64_t* dst_st, const void* sr
   int64_t n = 1;
   for (int d = 0; d < ndim; ++d) n *= sizes[d];
   if (n == 0) return MT_OK;
-  if (dtype_size(dd) == 0 || dtype_size(sd) == 0 || dd > MT_F64 || sd > MT_F64)
-    return fail(MT_ERR_UNSUPPORTED, "copy_strided: dtype");
+  if (dtype_size(dd) == 0 || dtype_size(sd) == 0) return fail(MT_ERR_UNSUPPORTED, "copy_strided: dtype");
+  const bool raw = dd > MT_F64 || sd > MT_F64;  // integer / bool: same-type copies only, no casts
+  if (raw && dd != sd) return fail(MT_ERR_UNSUPPORTED, "copy_strided: integer dtype casts");
   const bool dc = is_contig(dst_st, sizes, ndim), sc = is_contig(src_st, sizes, ndim);
   if (dc && sc) {
     if (dd == sd) {
@@ -426,6 +438,15 @@ int launch_copy_strided(void* dst, int dd, const int64_t* dst_st, const void* sr
       copy_rows16_kernel<<<grid_for(n16, 256), 256, 0, st>>>((uint4*)dst, (const uint4*)src, rows, n16);
       return check_launch("copy_rows16");
     }
+  }
+  if (raw) {
+    switch (es) {
+      case 1: copy_strided_raw_kernel<<<grid_for(n, 256), 256, 0, st>>>((uint8_t*)dst, (const uint8_t*)src, nd, n); break;
+      case 4: copy_strided_raw_kernel<<<grid_for(n, 256), 256, 0, st>>>((uint32_t*)dst, (const uint32_t*)src, nd, n); break;
+      case 8: copy_strided_raw_kernel<<<grid_for(n, 256), 256, 0, st>>>((uint64_t*)dst, (const uint64_t*)src, nd, n); break;
+      default: return fail(MT_ERR_UNSUPPORTED, "copy_strided: element size %d", es);
+    }
+    return check_launch("copy_strided_raw");
   }
   copy_strided_kernel<<<grid_for(n, 256), 256, 0, st>>>(dst, dd, src, sd, nd, n);
   return check_launch("copy_strided");
@@ -507,15 +528,79 @@ int launch_axpby(void* out, int od, const void* x, int xd, double a, const void*
   return check_launch("axpby");
 }
 
+// One DDIM update in fp32 (sa = sqrt(a_t), sb = sqrt(1 - a_t), sap / sbp the same for a_prev).
+__device__ __forceinline__ float ddim_update(float xv, float ev, float sa, float sb, float sap, float sbp, int clip) {
+  float x0 = (xv - sb * ev) / sa;
+  if (clip) x0 = fminf(fmaxf(x0, -1.0f), 1.0f);
+  const float e2 = (xv - sa * x0) / sb;
+  return sap * x0 + sbp * e2;
+}
+
 __global__ void ddim_step_kernel(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n,
                                  float sa, float sb, float sap, float sbp, int clip) {
   MT_GRID_STRIDE(i, n) {
     const float xv = load_as_f32(x, i, dtype), ev = load_as_f32(eps, i, eps_dtype);
-    float x0 = (xv - sb * ev) / sa;
-    if (clip) x0 = fminf(fmaxf(x0, -1.0f), 1.0f);
-    const float e2 = (xv - sa * x0) / sb;
-    store_from_f32(out, i, dtype, sap * x0 + sbp * e2);
+    store_from_f32(out, i, dtype, ddim_update(xv, ev, sa, sb, sap, sbp, clip));
   }
+}
+
+// DDIM update whose timestep is read from device memory (so one captured graph serves every step)
+// with optional classifier-free guidance folded in: eps holds [uncond; text] (2n values) and the
+// guided noise is uncond + (text - uncond) * g, evaluated in that order with no FMA contraction
+// (tests/compat/benchmarking.py:5847-5850).  The result goes to out[c*n + i] for c < copies, so the
+// next step's doubled model input is written in the same pass.
+__global__ void ddim_indexed_kernel(void* out, int64_t copies, const void* x, const void* eps, int dtype,
+                                    int eps_dtype, int64_t n, const double* ac, int64_t len, const int64_t* tstep,
+                                    int64_t interval, int cfg, float g, int clip) {
+  int64_t t = *tstep;
+  t = t < 0 ? 0 : (t >= len ? len - 1 : t);
+  const int64_t tp = t - interval > 0 ? t - interval : 0;
+  const double a_t = ac[t], a_p = ac[tp];
+  const float sa = (float)sqrt(a_t), sb = (float)sqrt(1.0 - a_t), sap = (float)sqrt(a_p),
+              sbp = (float)sqrt(1.0 - a_p);
+  MT_GRID_STRIDE(i, n) {
+    const float xv = load_as_f32(x, i, dtype);
+    float ev = load_as_f32(eps, i, eps_dtype);
+    if (cfg) ev = __fadd_rn(ev, __fmul_rn(__fsub_rn(load_as_f32(eps, n + i, eps_dtype), ev), g));
+    const float v = ddim_update(xv, ev, sa, sb, sap, sbp, clip);
+    for (int64_t c = 0; c < copies; ++c) store_from_f32(out, c * n + i, dtype, v);
+  }
+}
+
+int launch_ddim_indexed(void* out, int64_t copies, const void* x, const void* eps, int dtype, int eps_dtype,
+                        int64_t n, const double* ac, int64_t len, const int64_t* tstep, int64_t interval, int cfg,
+                        double g, int clip, cudaStream_t st) {
+  if (n <= 0) return MT_OK;
+  ddim_indexed_kernel<<<grid_for(n, 256), 256, 0, st>>>(out, copies, x, eps, dtype, eps_dtype, n, ac, len, tstep,
+                                                        interval, cfg, (float)g, clip);
+  return check_launch("ddim_step_indexed");
+}
+
+// Sinusoidal timestep embedding in fp32, as the reference's scenario builds it
+// (tests/compat/benchmarking.py:6016-6021, 6035-6036): freq_j = exp((-ln(max_period) * j) / half),
+// arg = t * freq_j, row = [cos(arg) | sin(arg)] (flip != 0) or [sin | cos]; accurate expf / cosf /
+// sinf (the library is built without fast-math), so large arguments (t up to 999) keep full range
+// reduction.  Timestep k of row r is t[r * t_stride] (stride 0 broadcasts one device scalar).
+__global__ void timestep_embedding_kernel(void* out, int od, const void* t, int td, int64_t t_stride, int64_t n,
+                                          int64_t half, float neg_log_period, int flip) {
+  MT_GRID_STRIDE(i, n * 2 * half) {
+    const int64_t r = i / (2 * half), c = i - r * 2 * half;
+    const int64_t j = c < half ? c : c - half;
+    const float tv = td == MT_I64 ? (float)static_cast<const int64_t*>(t)[r * t_stride]
+                                  : load_as_f32(t, r * t_stride, td);
+    const float freq = expf(__fdiv_rn(__fmul_rn(neg_log_period, (float)j), (float)half));
+    const float arg = __fmul_rn(tv, freq);
+    const bool first = c < half;
+    store_from_f32(out, i, od, (first == (flip != 0)) ? cosf(arg) : sinf(arg));
+  }
+}
+
+int launch_timestep_embedding(void* out, int od, const void* t, int td, int64_t t_stride, int64_t n, int64_t dim,
+                              double max_period, int flip, cudaStream_t st) {
+  if (n <= 0 || dim <= 0) return MT_OK;
+  timestep_embedding_kernel<<<grid_for(n * dim, 256), 256, 0, st>>>(out, od, t, td, t_stride, n, dim / 2,
+                                                                    -logf((float)max_period), flip);
+  return check_launch("timestep_embedding");
 }
 
 int launch_ddim_step(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n, double a_t,
@@ -525,6 +610,49 @@ int launch_ddim_step(void* out, const void* x, const void* eps, int dtype, int e
                                                      (float)sqrt(1.0 - a_t), (float)sqrt(a_prev),
                                                      (float)sqrt(1.0 - a_prev), clip);
   return check_launch("ddim_step");
+}
+
+// Embedding row gather (tensor.cpp:31748-31800): out[r, :] = weight[ids[r], :] (+ add[add_ids[r], :]),
+// negative ids counted from the end as the reference's normalized_dim_index does.  An id outside
+// [-rows, rows) writes a zero row and increments *invalid (when given) so the caller can raise the
+// reference's IndexError.  Each warp copies one row; the optional add is done in fp32 and rounded
+// once to the output type (for 16-bit tables this equals the reference's separate add).
+__device__ __forceinline__ int64_t embed_row(const int64_t* ids, int64_t r, int64_t rows, int* invalid, bool* ok) {
+  int64_t id = ids[r];
+  if (id < 0) id += rows;
+  *ok = id >= 0 && id < rows;
+  if (!*ok && invalid && (threadIdx.x & 31) == 0) atomicAdd(invalid, 1);
+  return *ok ? id : 0;
+}
+
+__global__ void embedding_kernel(void* out, int od, const void* w, int wd, int64_t rows, int64_t dim,
+                                 const int64_t* ids, int64_t n, const void* add, int ad, int64_t add_rows,
+                                 const int64_t* add_ids, int* invalid) {
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
+    bool ok, ok2 = true;
+    const int64_t id = embed_row(ids, r, rows, invalid, &ok);
+    const int64_t id2 = add ? embed_row(add_ids, r, add_rows, invalid, &ok2) : 0;
+    for (int64_t c = lane; c < dim; c += 32) {
+      float v = 0.f;
+      if (ok && ok2) {
+        v = load_as_f32(w, id * dim + c, wd);
+        if (add) v += load_as_f32(add, id2 * dim + c, ad);
+      }
+      store_from_f32(out, r * dim + c, od, v);
+    }
+  }
+}
+
+int launch_embedding(void* out, int od, const void* w, int wd, int64_t rows, int64_t dim, const int64_t* ids,
+                     int64_t n, const void* add, int ad, int64_t add_rows, const int64_t* add_ids, int* invalid,
+                     cudaStream_t st) {
+  if (n <= 0 || dim <= 0) return MT_OK;
+  const int64_t blocks = (n + 7) / 8;
+  embedding_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(out, od, w, wd, rows, dim, ids, n, add,
+                                                                              ad, add_rows, add_ids, invalid);
+  return check_launch("embedding");
 }
 
 int launch_pack2d(void* out, float* lo, const void* in, int dtype, int64_t batch, int64_t rows, int64_t cols,

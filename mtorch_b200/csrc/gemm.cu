@@ -463,6 +463,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             } else if (ep.act == MT_EPI_SILU) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+            } else if (ep.act == MT_EPI_QUICK_GELU) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = v[j] * (1.0f / (1.0f + expf(-__fmul_rn(v[j], 1.702f))));
             }
             if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
             row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
@@ -751,7 +754,7 @@ static int validate_gemm(const mt_gemm_desc& d) {
     return fail(MT_ERR_UNSUPPORTED, "gemm: input dtype %d", d.dtype);
   if (d.out_dtype != MT_F32 && d.out_dtype != MT_BF16 && d.out_dtype != MT_F16)
     return fail(MT_ERR_UNSUPPORTED, "gemm: output dtype %d", d.out_dtype);
-  if (d.epilogue < MT_EPI_NONE || d.epilogue > MT_EPI_GEGLU) return fail(MT_ERR_UNSUPPORTED, "gemm: epilogue");
+  if (d.epilogue < MT_EPI_NONE || d.epilogue > MT_EPI_QUICK_GELU) return fail(MT_ERR_UNSUPPORTED, "gemm: epilogue");
   if (d.epilogue == MT_EPI_GEGLU && d.N % 128 != 0)
     return fail(MT_ERR_INVALID, "gemm: GEGLU needs N %% 128 == 0 (interleaved 64-column groups)");
   if (d.M > 0 && d.N > 0 && d.K == 0) return fail(MT_ERR_UNSUPPORTED, "gemm: K == 0 (caller fills)");

@@ -54,6 +54,14 @@ int launch_axpby(void* out, int od, const void* x, int xd, double a, const void*
                  int zd, double c, int64_t n, cudaStream_t st);
 int launch_ddim_step(void* out, const void* x, const void* eps, int dtype, int eps_dtype, int64_t n, double a_t,
                      double a_prev, int clip, cudaStream_t st);
+int launch_ddim_indexed(void* out, int64_t copies, const void* x, const void* eps, int dtype, int eps_dtype,
+                        int64_t n, const double* ac, int64_t len, const int64_t* tstep, int64_t interval, int cfg,
+                        double g, int clip, cudaStream_t st);
+int launch_timestep_embedding(void* out, int od, const void* t, int td, int64_t t_stride, int64_t n, int64_t dim,
+                              double max_period, int flip, cudaStream_t st);
+int launch_embedding(void* out, int od, const void* w, int wd, int64_t rows, int64_t dim, const int64_t* ids,
+                     int64_t n, const void* add, int ad, int64_t add_rows, const int64_t* add_ids, int* invalid,
+                     cudaStream_t st);
 int launch_pack2d(void* out, float* lo, const void* in, int dtype, int64_t batch, int64_t rows, int64_t cols,
                   int64_t sr, int64_t sc, int64_t sb, int64_t out_pitch, cudaStream_t st);
 int launch_conv_pack_weight(void* out, float* lo, const void* w, int dtype, int64_t K, int64_t C, int64_t R,

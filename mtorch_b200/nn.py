@@ -359,6 +359,7 @@ class _Functional:
     gelu = staticmethod(ops.gelu)
     relu = staticmethod(ops.relu)
     sigmoid = staticmethod(ops.sigmoid)
+    embedding = staticmethod(ops.embedding)
 
     @staticmethod
     def interpolate(x, size=None, scale_factor=None, mode="nearest", align_corners=None):

@@ -10,9 +10,11 @@ from __future__ import annotations
 import ctypes as C
 import math
 
+import numpy as np
+
 from . import _lib as L
-from .tensor import (Tensor, _new, _require_cuda, _broadcast_shape, bfloat16, float16, float32, to_dtype, workspace,
-                     _contig_strides)
+from .tensor import (Tensor, _new, _require_cuda, _broadcast_shape, bfloat16, float16, float32, float64, int32, int64,
+                     tensor, to_dtype, workspace, zeros, _contig_strides)
 
 
 def _lib():
@@ -546,6 +548,120 @@ def relu(x):
 
 def exp(x):
     return _unary(x, "exp")
+
+
+def quick_gelu(x):
+    """CLIP's x * sigmoid(1.702 x) in one pass (the reference composes it from mul and sigmoid,
+    tests/compat/benchmarking.py:7714)."""
+    return _unary(x, "quick_gelu")
+
+
+def _ids_on_device(ids: Tensor, rows: int, dev) -> Tensor:
+    """int64 ids on `dev`.  Host ids are range-checked on the host (the reference's
+    normalized_dim_index raises std::out_of_range -> IndexError) before the copy."""
+    if ids.dtype not in (int32, int64):
+        raise ValueError("embedding indices must have integer dtype")
+    if ids.device.type != "cpu" and ids.dtype is int64:
+        return ids.contiguous()
+    a = ids.numpy().astype(np.int64)  # host ids, or device int32 ids widened on the host
+    if a.size and (a.min() < -rows or a.max() >= rows):
+        raise IndexError("index out of range in embedding")
+    return tensor(a).to(dev)
+
+
+def embedding(input: Tensor, weight: Tensor, padding_idx=None, max_norm=None, norm_type=2.0,
+              scale_grad_by_freq=False, sparse=False, *, add_weight: Tensor | None = None,
+              add_input: Tensor | None = None) -> Tensor:
+    """`embedding` (tensor.cpp:31748-31800): rows of `weight` [rows, dim] selected by `input`.
+    `add_weight` / `add_input` (keyword-only, an extension) add a second gathered table in the same
+    pass — CLIP's token + position embedding.  Ids may live on the host (checked there) or on the
+    device (an out-of-range id is counted by the kernel and raises IndexError after a sync)."""
+    _require_cuda(weight)
+    if weight.dim() != 2:
+        raise ValueError("embedding weight must be 2-D")
+    if max_norm is not None:
+        raise NotImplementedError("embedding max_norm renormalisation is not implemented on the cuda device")
+    rows, dim = weight._shape
+    if padding_idx is not None:
+        p = padding_idx + rows if padding_idx < 0 else padding_idx
+        if not 0 <= p < rows:
+            raise IndexError("embedding padding_idx is out of bounds")
+    dev = weight.device
+    ids = _ids_on_device(input, rows, dev)
+    w = weight.contiguous()
+    out = _new(tuple(input._shape) + (dim,), weight.dtype, dev)
+    add = add_ids = None
+    add_rows = 0
+    if add_weight is not None:
+        _require_cuda(add_weight)
+        if add_weight.dim() != 2 or add_weight._shape[1] != dim:
+            raise ValueError("embedding: add_weight must be [rows, dim] with the same dim")
+        if add_input is None or tuple(add_input.shape) != tuple(input.shape):
+            raise ValueError("embedding: add_input must have the shape of input")
+        add = add_weight.contiguous()
+        add_rows = add._shape[0]
+        add_ids = _ids_on_device(add_input, add_rows, dev)
+    device_ids = (input.device.type != "cpu" and input.dtype is int64) or (
+        add_input is not None and add_input.device.type != "cpu" and add_input.dtype is int64)
+    counter = zeros(1, dtype=int32, device=dev) if device_ids else None
+    L.check(_lib().mt_cuda_embedding(out.data_ptr(), out.dtype.code, w.data_ptr(), w.dtype.code, rows, dim,
+                                     ids.data_ptr(), ids.numel(), add.data_ptr() if add is not None else None,
+                                     add.dtype.code if add is not None else 0, add_rows,
+                                     add_ids.data_ptr() if add_ids is not None else None,
+                                     counter.data_ptr() if counter is not None else None, weight._stream()),
+            "embedding")
+    if counter is not None and int(counter.item()) != 0:
+        raise IndexError("index out of range in embedding")
+    return out
+
+
+def timestep_embedding(timesteps: Tensor, dim: int, dtype=None, flip_sin_to_cos=True, max_period=10000.0,
+                       batch: int | None = None) -> Tensor:
+    """Sinusoidal timestep embedding [n, dim] on the device, fp32 math in the reference's order
+    (tests/compat/benchmarking.py:6011-6036): freq_j = exp(-ln(max_period) * j / (dim/2)),
+    [cos(t freq) | sin(t freq)].  `timesteps` is a device tensor of n values, or one value
+    broadcast over `batch` rows (so a captured graph can read the step's timestep from memory)."""
+    _require_cuda(timesteps)
+    t = timesteps.contiguous()
+    if batch is None:
+        n, stride = t.numel(), 1
+    else:
+        if t.numel() != 1:
+            raise ValueError("timestep_embedding: batch= needs a single timestep")
+        n, stride = int(batch), 0
+    out = _new((n, dim), to_dtype(dtype) if dtype is not None else float32, t.device)
+    L.check(_lib().mt_cuda_timestep_embedding(out.data_ptr(), out.dtype.code, t.data_ptr(), t.dtype.code, stride, n,
+                                              dim, float(max_period), 1 if flip_sin_to_cos else 0, t._stream()),
+            "timestep_embedding")
+    return out
+
+
+def ddim_step_indexed(x: Tensor, eps: Tensor, alphas_cumprod: Tensor, timestep: Tensor, interval: int, clip=True,
+                      guidance_scale: float | None = None, out: Tensor | None = None, out_copies: int = 1) -> Tensor:
+    """DDIM update reading the timestep from device memory (one graph serves every step), with
+    classifier-free guidance folded in when `guidance_scale` is given: `eps` is then the model
+    output for the doubled batch [uncond; text] (tests/compat/benchmarking.py:5847-5850,
+    6148-6168).  `out` receives `out_copies` (1 or 2) stacked copies of the updated latents; 2
+    writes the next step's doubled model input directly.  `out` may alias `x`'s storage."""
+    _require_cuda(x, eps, alphas_cumprod, timestep)
+    if alphas_cumprod.dtype is not float64 or timestep.dtype is not int64:
+        raise ValueError("ddim_step_indexed: alphas_cumprod must be float64 and timestep int64")
+    n = x.numel()
+    cfg = guidance_scale is not None
+    if eps.numel() != (2 * n if cfg else n):
+        raise ValueError(f"ddim_step_indexed: eps has {eps.numel()} values, expected {(2 if cfg else 1) * n}")
+    if x.is_contiguous() is False or eps.is_contiguous() is False:
+        raise ValueError("ddim_step_indexed: x and eps must be contiguous")
+    if out is None:
+        out = _new((out_copies * x._shape[0],) + tuple(x._shape[1:]), x.dtype, x.device)
+    if out.numel() != out_copies * n or not out.is_contiguous():
+        raise ValueError("ddim_step_indexed: out must be contiguous with out_copies * x.numel() values")
+    L.check(_lib().mt_cuda_ddim_step_indexed(out.data_ptr(), out_copies, x.data_ptr(), eps.data_ptr(), x.dtype.code,
+                                             eps.dtype.code, n, alphas_cumprod.data_ptr(), alphas_cumprod.numel(),
+                                             timestep.data_ptr(), int(interval), 1 if cfg else 0,
+                                             float(guidance_scale) if cfg else 0.0, 1 if clip else 0, x._stream()),
+            "ddim_step_indexed")
+    return out
 
 
 # ---------------------------------------------------------------------------------------------

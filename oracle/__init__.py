@@ -163,6 +163,45 @@ def gelu_f32(x, approximate="none"):
     return out
 
 
+def quick_gelu_f32(x):
+    x = _f(x)
+    out = np.empty_like(x)
+    _lib().oracle_quick_gelu_f32(_p(x), _p(out), I(x.size))
+    return out
+
+
+def timestep_embedding_f32(t, dim, max_period=10000.0, flip=True):
+    t = _f(t).reshape(-1)
+    out = np.empty((t.size, dim), np.float32)
+    _lib().oracle_timestep_embedding_f32(_p(t), _p(out), I(t.size), I(dim), C.c_double(max_period),
+                                         C.c_int(1 if flip else 0))
+    return out
+
+
+def embedding_f32(w, ids, add=None, add_ids=None):
+    """Returns (rows [*ids.shape, dim], number of out-of-range ids)."""
+    w = _f(w)
+    ids = np.ascontiguousarray(ids, np.int64)
+    dim = w.shape[1]
+    out = np.empty(ids.shape + (dim,), np.float32)
+    a = _f(add) if add is not None else None
+    ai = np.ascontiguousarray(add_ids, np.int64) if add_ids is not None else None
+    f = _lib().oracle_embedding_f32
+    f.restype = C.c_int64
+    bad = f(_p(w), I(w.shape[0]), I(dim), _p(ids), I(ids.size), _p(a), I(a.shape[0] if a is not None else 0), _p(ai),
+            _p(out))
+    return out, int(bad)
+
+
+def cfg_ddim_f32(x, eps, g, a_t, a_prev, clip=True):
+    """eps = [uncond; text] stacked on the first axis (2n rows for n latents)."""
+    x, eps = _f(x), _f(eps)
+    out = np.empty_like(x)
+    _lib().oracle_cfg_ddim_f32(_p(x), _p(eps), _p(out), I(x.size), C.c_double(g), C.c_double(a_t),
+                               C.c_double(a_prev), C.c_int(1 if clip else 0))
+    return out
+
+
 def ref():
     """The reference mtorch module (built CPU implementation) or None when not built here."""
     from . import build_ref

@@ -87,6 +87,35 @@ rec("silu", x=x, y=F.silu(x))
 rec("gelu", x=x, y=F.gelu(x))
 rec("gelu_tanh", x=x, y=F.gelu(x, approximate="tanh"))
 
+# Scheduler / text-encoder ops around the UNet (appended after the cases above so their seeded
+# inputs are unchanged).  Each follows the reference's own scenario code in
+# tests/compat/benchmarking.py, written against the public API.
+t = mtorch.tensor([999.0, 500.0, 1.0, 0.0], dtype=mtorch.float32)
+exponent = -mtorch.log(mtorch.tensor(10000.0, dtype=mtorch.float32)) * mtorch.arange(0, 160, dtype=mtorch.float32) / 160
+args = t.reshape(-1, 1) * mtorch.exp(exponent).reshape(1, -1)  # 6016-6021, 6035
+rec("tsemb", t=t, y=mtorch.cat([mtorch.cos(args), mtorch.sin(args)], dim=-1))  # 6036
+
+mtorch.manual_seed(40)
+x = mtorch.randn(300) * 3.0
+rec("quick_gelu", x=x, y=x * mtorch.sigmoid(x * 1.702))  # 7714
+
+mtorch.manual_seed(41)
+w, pw = mtorch.randn(11, 6), mtorch.randn(4, 6)
+ids = mtorch.tensor([[0, 3, -1, 10], [5, 5, 2, -11]], dtype=mtorch.long)
+pos = mtorch.tensor([[0, 1, 2, 3], [0, 1, 2, 3]], dtype=mtorch.long)
+rec("embedding", w=w, pw=pw, ids=ids, pos=pos, y=F.embedding(ids, w) + F.embedding(pos, pw))  # 5235-5236
+
+mtorch.manual_seed(42)
+uncond, text, cur = mtorch.randn(2, 4, 3, 3), mtorch.randn(2, 4, 3, 3), mtorch.randn(2, 4, 3, 3)
+noise = uncond + (text - uncond) * 7.5  # 5847-5850
+betas = mtorch.linspace(0.00085 ** 0.5, 0.012 ** 0.5, 16, dtype=mtorch.float32) ** 2  # 6138-6141
+alphas_cumprod = mtorch.cumprod(1.0 - betas, dim=0)
+a_t, a_prev = alphas_cumprod[10], alphas_cumprod[6]
+pred_original = ((cur - (1.0 - a_t).sqrt() * noise) / a_t.sqrt()).clamp(-1.0, 1.0)  # 6158-6164
+pred_epsilon = (cur - a_t.sqrt() * pred_original) / (1.0 - a_t).sqrt()
+step = a_prev.sqrt() * pred_original + (1.0 - a_prev).sqrt() * pred_epsilon
+rec("cfg_ddim", x=cur, eps=mtorch.cat([uncond, text], dim=0), a=mtorch.stack([a_t, a_prev]), y=step)
+
 path = Path(__file__).resolve().parent / "reference_ops.npz"
 np.savez_compressed(path, **out)
 print(f"wrote {path} ({len(out)} arrays)")

@@ -56,6 +56,19 @@ def test_norms_and_activations(golden):
     close(oracle.gelu_f32(golden["gelu_tanh.x"], "tanh"), golden["gelu_tanh.y"], 1e-6, 1e-7)
 
 
+def test_pipeline_ops(golden):
+    """Timestep embedding, quick GELU, embedding gather + add, and guidance + DDIM step."""
+    close(oracle.timestep_embedding_f32(golden["tsemb.t"], 320), golden["tsemb.y"], 0, 2e-6)
+    close(oracle.quick_gelu_f32(golden["quick_gelu.x"]), golden["quick_gelu.y"], 1e-6, 1e-7)
+    y, bad = oracle.embedding_f32(golden["embedding.w"], golden["embedding.ids"], golden["embedding.pw"],
+                                  golden["embedding.pos"])
+    assert bad == 0
+    close(y, golden["embedding.y"], 0, 0)
+    a_t, a_prev = (float(v) for v in golden["cfg_ddim.a"])
+    close(oracle.cfg_ddim_f32(golden["cfg_ddim.x"], golden["cfg_ddim.eps"], 7.5, a_t, a_prev), golden["cfg_ddim.y"],
+          1e-6, 1e-6)
+
+
 def test_reference_live_if_built():
     """When the reference is built here, the oracle matches it on a fresh case too."""
     m = oracle.ref()
