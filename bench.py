@@ -7,6 +7,7 @@ weights are replicated, and the output latents are all-gathered once over NCCL a
 timed region.  `value` = steps/s of the whole 64-sample job.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --workload sampler|vae|text [--batch B]   (the workloads around the UNet)
 
 `--impl reference` times the reference mtorch's own CPU implementation (built from its sources
 into oracle/_ref; the restated C oracle when that is absent) on the host cores, on a bounded
@@ -416,6 +417,68 @@ def run_kernel(args):
                       "frac_of_bf16_peak": tflops / tf_burst, "peak_kind": kind}))
 
 
+def run_workload(args):
+    """The §8(f) workloads around the UNet, one GPU, device-timed (CUDA events on torch's current
+    stream, after `warmup` untimed runs), each as one JSON line with its FLOP rate against the
+    measured bf16 peak:
+      sampler  guided denoising (classifier-free guidance 7.5) of `batch` latents: the UNet on the
+               doubled batch, device timestep embedding and the fused guidance + DDIM kernel, one
+               CUDA graph per step; unit = denoise steps/s of the whole batch
+      vae      SD-1.5 VAE decode of `batch` latents 64x64 -> 512x512 images; unit = images/s
+      text     SD-1.5 CLIP text encoder on `batch` sequences of 77 tokens; unit = sequences/s"""
+    import torch
+
+    import mtorch_b200 as mt
+
+    stream = torch.cuda.current_stream()
+    nb = args.batch
+    mt.manual_seed(0)
+    if args.workload == "sampler":
+        from mtorch_b200.unet import DDIM, Sampler, UNet, unet_flops_per_sample
+
+        unet = UNet(device="cuda", dtype="bfloat16")
+        mt.manual_seed(1)
+        lat = mt.randn(nb, 4, H, W).to("bfloat16").cuda()
+        ctx = mt.randn(nb, CTX, 768).to("bfloat16").cuda()
+        unc = mt.randn(nb, CTX, 768).to("bfloat16").cuda()
+        sampler = Sampler(unet, DDIM(steps=50), ctx, uncond_ctx=unc, guidance_scale=7.5, graph=True)
+        fn = lambda: sampler(lat, steps=1)  # noqa: E731
+        flops, unit = unet_flops_per_sample() * 2 * nb, "denoise steps/s"
+        name = f"guided denoise step, {nb} latents (UNet batch {2 * nb}), CUDA graph"
+    elif args.workload == "vae":
+        from mtorch_b200.vae import VAEDecoder, vae_decoder_flops
+
+        dec = VAEDecoder(device="cuda", dtype="bfloat16")
+        z = mt.randn(nb, 4, H, W).to("bfloat16").cuda()
+        fn = lambda: dec(z)  # noqa: E731
+        flops, unit = vae_decoder_flops(H, W) * nb, "images/s"
+        name = f"SD-1.5 VAE decode, {nb} latents 64x64 -> 512x512"
+    else:
+        from mtorch_b200.text_encoder import CLIPTextEncoder, clip_text_flops
+
+        enc = CLIPTextEncoder(device="cuda", dtype="bfloat16")
+        ids = mt.tensor((np.arange(nb * CTX).reshape(nb, CTX) * 7919) % 49408)
+        fn = lambda: enc(ids)  # noqa: E731
+        flops, unit = clip_text_flops() * nb, "sequences/s"
+        name = f"SD-1.5 CLIP text encoder, {nb} x 77 tokens"
+    for _ in range(max(args.warmup, 1)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    _, tf_burst, tf_sust, kind = peaks()
+    tflops = flops / (ms * 1e-3) / 1e12
+    per = 1 if args.workload == "sampler" else nb
+    print(json.dumps({"workload": name, "value": 1000.0 * per / ms, "unit": unit, "ms_per_run": ms,
+                      "batch": nb, "dtype": "bf16", "data": "synthetic, random-init weights", "tflops": tflops,
+                      "frac_of_bf16_peak": tflops / tf_burst, "peak_kind": f"{kind} bf16 burst"}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -425,9 +488,13 @@ def main():
     ap.add_argument("--eager", action="store_true", help="launch the UNet op by op instead of replaying a CUDA graph")
     ap.add_argument("--kernel", choices=["conv", "attn", "geglu"], default=None,
                     help="time one hot kernel alone at its UNet shape (for profiling), not the UNet")
-    ap.add_argument("--batch", type=int, default=BATCH, help="samples for --kernel runs")
+    ap.add_argument("--batch", type=int, default=BATCH, help="samples for --kernel / --workload runs")
+    ap.add_argument("--workload", choices=["sampler", "vae", "text"], default=None,
+                    help="time one of the workloads around the UNet instead of the UNet step")
     args = ap.parse_args()
-    if args.kernel:
+    if args.workload:
+        run_workload(args)
+    elif args.kernel:
         run_kernel(args)
     elif args.impl == "reference":
         run_reference(args)

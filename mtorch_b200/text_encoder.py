@@ -90,3 +90,10 @@ class CLIPTextEncoder(Module):
         for layer in self.layers:
             h = layer(h, n, s)
         return self.final_norm(h).reshape(n, s, self.width)
+
+
+def clip_text_flops(seq=77, width=768, layers=12, mlp=3072) -> float:
+    """FLOPs (2 per MAC) of one sequence: the four projections per layer and the attention
+    products counted over the full S x S (the causal half is still computed)."""
+    per_layer = 2.0 * seq * width * (3 * width + width + 2 * mlp) + 4.0 * seq * seq * width
+    return layers * per_layer

@@ -370,7 +370,8 @@ def denoise(unet: UNet, latents: Tensor, ctx: Tensor, sched: DDIM, steps: int | 
     x = latents.contiguous()
     ts = sched.timesteps if steps is None else sched.timesteps[:steps]
     for t in ts:
-        temb = tensor(timestep_embedding(np.full(n, float(t))), dtype=latents.dtype, device=latents.device)
+        temb = tensor(timestep_embedding(np.full(n, float(t)), unet.chans[0]), dtype=latents.dtype,
+                      device=latents.device)
         eps = unet(x, temb, ctx)
         x = sched.step(x, eps, t)
     return x

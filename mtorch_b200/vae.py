@@ -103,3 +103,27 @@ class VAEDecoder(Module):
         h = self.norm_out(h, fuse_silu=True)
         return ops.conv2d(h, self.conv_out.weight, self.conv_out.bias, 1, 1, packed=self.conv_out.packed_weight(),
                           out_channels_last=False)
+
+
+def vae_decoder_flops(h=64, w=64, chans=(128, 256, 512, 512), layers=2, latent_ch=4, out_ch=3) -> float:
+    """Multiply-add FLOPs (2 per MAC) of one decode of a [h, w] latent: convolutions, the mid
+    attention's projections and its two S x S products."""
+    def conv(cin, cout, k, hh, ww):
+        return 2.0 * hh * ww * cin * cout * k * k
+
+    def resnet(cin, cout, hh, ww):
+        return conv(cin, cout, 3, hh, ww) + conv(cout, cout, 3, hh, ww) + (conv(cin, cout, 1, hh, ww) if cin != cout
+                                                                           else 0.0)
+    top = chans[-1]
+    s = h * w
+    fl = conv(latent_ch, latent_ch, 1, h, w) + conv(latent_ch, top, 3, h, w)
+    fl += 2 * resnet(top, top, h, w) + 2.0 * s * top * 4 * top + 4.0 * s * s * top
+    c, hh, ww = top, h, w
+    for lvl, co in enumerate(reversed(chans)):
+        for _ in range(layers + 1):
+            fl += resnet(c, co, hh, ww)
+            c = co
+        if lvl != len(chans) - 1:
+            hh, ww = 2 * hh, 2 * ww
+            fl += conv(c, c, 3, hh, ww)
+    return fl + conv(c, out_ch, 3, hh, ww)
