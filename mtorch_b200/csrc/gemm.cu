@@ -33,6 +33,7 @@ struct TileParams {
   int c_chunks, R, S, pad_h, pad_w, dil_h, dil_w, stride_h, stride_w;
   int bk;  // elements per 128-byte K chunk
   int a_stages;  // B-resident variant: A-only stages behind the resident B tile
+  int m_pairs;   // CTA-pair variant: row-tile pairs, ceil(num_m_tiles / 2)
 };
 
 struct EpiParams {
@@ -217,12 +218,14 @@ __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b,
 constexpr int kResBytes = 200 * 1024;
 constexpr int kMaxResStages = 8;
 
-template <int BN, bool TF32>
+template <int BN, bool TF32, bool PAIR = false>
 struct GemmCfg {
   static constexpr int A_BYTES = kBM * 128;
   static constexpr int B_BYTES = BN * 128;
+  // CTA pair: each CTA stages half of the B columns
+  static constexpr int B_STAGE_BYTES = PAIR ? B_BYTES / 2 : B_BYTES;
   static constexpr int OPS = TF32 ? 2 : 1;
-  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * OPS;
+  static constexpr int STAGE_BYTES = (A_BYTES + B_STAGE_BYTES) * OPS;
   static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
   static constexpr int TMEM_COLS = (2 * BN <= 32)    ? 32
@@ -239,13 +242,19 @@ struct GemmCfg {
 // the number of column tiles), so the whole [BN x K] B tile is loaded into shared memory once and
 // only A streams through the stage ring; for the short-K projections this removes the re-reads
 // of B from L2 that otherwise cost more than the A traffic.
-template <int BN, bool TF32, bool CONV, bool BRES>
+//
+// PAIR (CTA pairs, cluster of 2): the pair computes a 256 x BN tile with tcgen05 cta_group::2 MMAs
+// issued by the even CTA; each CTA loads its own 128 rows of A and BN/2 rows of B (its half of
+// the columns), so every SM streams half as many B bytes per MMA as a single-CTA tile of the same
+// width.  Each CTA's TMEM holds its 128 rows of D and its epilogue stores them.
+template <int BN, bool TF32, bool CONV, bool BRES, bool PAIR = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmAlo, const __grid_constant__ CUtensorMap tmBlo,
                       const TileParams tp, const EpiParams ep, const uint32_t idesc) {
-  using Cfg = GemmCfg<BN, TF32>;
+  using Cfg = GemmCfg<BN, TF32, PAIR>;
   static_assert(!BRES || (!TF32 && !CONV), "B-resident variant: 16-bit GEMMs only");
+  static_assert(!PAIR || (!TF32 && !BRES), "CTA-pair variant: 16-bit streaming GEMMs only");
   const int STAGES = BRES ? tp.a_stages : Cfg::STAGES;
   // stage s: A at stage_base + s * STAGE_BYTES; B (not BRES) right after it
   constexpr int STAGE_BYTES = BRES ? Cfg::A_BYTES : Cfg::STAGE_BYTES;
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 256);
+      mbar_init(&tempty[b], PAIR ? 512 : 256);  // pair: both CTAs' epilogue threads
     }
     mbar_init(b_full, 1);
     *abort_flag = 0;
@@ -284,14 +293,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int total_tiles = tp.num_m_tiles * tp.num_n_tiles * tp.batch;
+  // PAIR: tiles are row-tile pairs; CTA `crank` of the pair takes row tile 2 * pair + crank.
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0;
+  const int total_tiles = (PAIR ? tp.m_pairs : tp.num_m_tiles) * tp.num_n_tiles * tp.batch;
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  auto decode = [&](int t, int& b, int& mt, int& nt) {
+    nt = t % tp.num_n_tiles;
+    const int rest = t / tp.num_n_tiles;
+    const int mcount = PAIR ? tp.m_pairs : tp.num_m_tiles;
+    mt = rest % mcount;
+    b = rest / mcount;
+    if (PAIR) mt = 2 * mt + (int)crank;
+  };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -305,10 +332,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kk = 0; kk < tp.k_iters; ++kk)
           tma_load_3d(sbres + kk * Cfg::B_BYTES, &tmB, b_full, kk * tp.bk, nt * BN, 0);
       }
-      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+      for (int t = tile0; t < total_tiles && !*abort_flag; t += tstep) {
         int b, mt, nt;
-        decode_tile(tp, t, b, mt, nt);
-        const int n0 = nt * BN;
+        decode(t, b, mt, nt);
+        const int n0 = nt * BN + (int)crank * (BN / 2);  // PAIR: this CTA's half of the columns
         int q0 = 0, p0 = 0, i0 = 0;
         if (CONV) {
           q0 = (mt % tp.tiles_q) * tp.tw;
@@ -317,7 +344,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int kk = 0; kk < tp.k_iters; ++kk) {
           if (!mbar_wait(&empty[stage], phase ^ 1, 1, abort_flag)) break;
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          // PAIR: the even CTA's barrier counts both CTAs' bytes
+          if (crank == 0) mbar_arrive_expect_tx(&full[stage], PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
           uint8_t* sa = stage_base + stage * STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
           uint8_t* salo = sb + Cfg::B_BYTES;
@@ -327,16 +355,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int r = rs / tp.S, s = rs - r * tp.S;
             const int cx = cc * tp.bk, wx = q0 * tp.stride_w + s * tp.dil_w - tp.pad_w,
                       hy = p0 * tp.stride_h + r * tp.dil_h - tp.pad_h;
-            tma_load_4d(sa, &tmA, &full[stage], cx, wx, hy, i0);
-            tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, 0);
+            if (PAIR) {
+              const uint32_t fb = mapa_rank(&full[stage], 0);
+              tma_load_4d_pair(sa, &tmA, fb, cx, wx, hy, i0);
+              tma_load_3d_pair(sb, &tmB, fb, kk * tp.bk, n0, 0);
+            } else {
+              tma_load_4d(sa, &tmA, &full[stage], cx, wx, hy, i0);
+              tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, 0);
+            }
             if (TF32) {
               tma_load_4d(salo, &tmAlo, &full[stage], cx, wx, hy, i0);
               tma_load_3d(sblo, &tmBlo, &full[stage], kk * tp.bk, n0, 0);
             }
           } else {
             const int ab = tp.a_batched ? b : 0, bb = tp.b_batched ? b : 0;
-            tma_load_3d(sa, &tmA, &full[stage], kk * tp.bk, mt * kBM, ab);
-            if (!BRES) tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, bb);
+            if (PAIR) {
+              const uint32_t fb = mapa_rank(&full[stage], 0);
+              tma_load_3d_pair(sa, &tmA, fb, kk * tp.bk, mt * kBM, ab);
+              tma_load_3d_pair(sb, &tmB, fb, kk * tp.bk, n0, bb);
+            } else {
+              tma_load_3d(sa, &tmA, &full[stage], kk * tp.bk, mt * kBM, ab);
+              if (!BRES) tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, bb);
+            }
             if (TF32) {
               tma_load_3d(salo, &tmAlo, &full[stage], kk * tp.bk, mt * kBM, ab);
               tma_load_3d(sblo, &tmBlo, &full[stage], kk * tp.bk, n0, bb);
@@ -350,13 +390,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (PAIR: the even CTA only) ----------------
+    if (lane == 0 && crank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       if (BRES && blockIdx.x < total_tiles && !mbar_wait(b_full, 0, 4, abort_flag)) local = -1;
-      for (int t = blockIdx.x; local >= 0 && t < total_tiles && !*abort_flag; t += gridDim.x, ++local) {
+      for (int t = tile0; local >= 0 && t < total_tiles && !*abort_flag; t += tstep, ++local) {
         const int buf = local & 1;
         const uint32_t tph = (local >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1, 2, abort_flag)) break;
@@ -373,7 +413,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = sdesc_sw128(a_addr + k * 32), bd = sdesc_sw128(b_addr + k * 32);
             const uint32_t acc = (kk > 0 || k > 0) ? 1u : 0u;
-            if (TF32) {
+            if (PAIR) {
+              umma_f16_pair(d_tmem, ad, bd, idesc, acc);
+            } else if (TF32) {
               umma_tf32(d_tmem, ad, bd, idesc, acc);
               umma_tf32(d_tmem, ad, sdesc_sw128(blo_addr + k * 32), idesc, 1u);
               umma_tf32(d_tmem, sdesc_sw128(alo_addr + k * 32), bd, idesc, 1u);
@@ -381,13 +423,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               umma_f16(d_tmem, ad, bd, idesc, acc);
             }
           }
-          umma_commit(&empty[stage]);
+          if (PAIR)
+            umma_commit_pair_both(&empty[stage]);
+          else
+            umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        umma_commit(&tfull[buf]);
+        if (PAIR)
+          umma_commit_pair_both(&tfull[buf]);
+        else
+          umma_commit(&tfull[buf]);
       }
     }
   } else {
@@ -400,13 +448,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool geglu = ep.act == MT_EPI_GEGLU;
     const int64_t n_out = geglu ? ep.N / 2 : ep.N;
     int local = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+    for (int t = tile0; t < total_tiles; t += tstep, ++local) {
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
       if (!mbar_wait(&tfull[buf], tph, 4, abort_flag)) break;
       tc_fence_after();
       int b, mt, nt;
-      decode_tile(tp, t, b, mt, nt);
+      decode(t, b, mt, nt);
       // Map this thread's accumulator row to output coordinates (i0, i1, i2).
       int64_t i0 = 0, i1 = 0, i2 = 0;
       bool valid;
@@ -506,13 +554,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[buf]);
+      if (PAIR)
+        mbar_arrive_cluster(mapa_rank(&tempty[buf], 0));
+      else
+        mbar_arrive(&tempty[buf]);
     }
   }
   __syncthreads();
+  if (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal its barriers
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -526,13 +581,18 @@ struct GemmLaunch {
   int kind;  // MT_BF16 / MT_F16 / MT_F32 (tf32 x3)
   int bn;
   bool conv;
+  // B operand as mapped (K-major), kept so the CTA-pair variant can re-map it with half-width boxes
+  const void* b_ptr; int64_t b_K, b_rows, b_batch, b_pitch, b_bstride;
 };
 
-template <int BN, bool TF32, bool CONV, bool BRES = false>
+static int map_kmajor(CUtensorMap* m, int dtype, const void* base, int64_t K, int64_t rows, int64_t batch,
+                      int64_t pitch, int64_t bstride, int box_rows);
+
+template <int BN, bool TF32, bool CONV, bool BRES = false, bool PAIR = false>
 static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
-  using Cfg = GemmCfg<BN, TF32>;
+  using Cfg = GemmCfg<BN, TF32, PAIR>;
   constexpr int smem = BRES ? Cfg::RES_SMEM_BYTES : Cfg::SMEM_BYTES;
-  auto kern = gemm_sm100_kernel<BN, TF32, CONV, BRES>;
+  auto kern = gemm_sm100_kernel<BN, TF32, CONV, BRES, PAIR>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -547,6 +607,29 @@ static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
   int grid = (int)std::min<int64_t>(tiles, num_sms());
   if (BRES) grid = num_sms() / L.tp.num_n_tiles * L.tp.num_n_tiles;  // one column tile per CTA
   const int fmt = L.kind == MT_BF16 ? 1 : L.kind == MT_F16 ? 0 : 2;
+  if (PAIR) {
+    // clusters of two CTAs, one pair per two SMs; the MMA spans 256 rows
+    const int64_t pairs = (int64_t)L.tp.m_pairs * L.tp.num_n_tiles * L.tp.batch;
+    GemmLaunch P = L;
+    int rc = map_kmajor(&P.b, L.kind, L.b_ptr, L.b_K, L.b_rows, L.b_batch, L.b_pitch, L.b_bstride, BN / 2);
+    if (rc) return rc;
+    const uint32_t idesc = make_idesc(fmt, 2 * kBM, BN);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(pairs, num_sms() / 2)));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P.a, P.b, P.alo, P.b, P.tp, P.ep, idesc);
+    if (e != cudaSuccess) return fail(MT_ERR_LAUNCH, "gemm_sm100 (CTA pairs): %s", cudaGetErrorString(e));
+    return check_launch("gemm_sm100_pair");
+  }
   const uint32_t idesc = make_idesc(fmt, kBM, BN);
   kern<<<grid, kGemmThreads, smem, st>>>(L.a, L.b, L.alo, L.blo, L.tp, L.ep, idesc);
   return check_launch("gemm_sm100");
@@ -570,11 +653,41 @@ static bool use_bres(GemmLaunch& L) {
   return true;
 }
 
+// Whether the CTA-pair variant is used: 16-bit, column tiles of 128 / 160 / 256 (half-width B
+// boxes of whole 8-row swizzle atoms), at least two row tiles.  MT_GEMM_PAIR=0 turns it off.
+static bool use_pair(GemmLaunch& L) {
+  static const bool off = [] {
+    const char* e = getenv("MT_GEMM_PAIR");
+    return e && e[0] == '0';
+  }();
+  if (off || L.kind == MT_F32 || !L.b_ptr) return false;
+  if (L.bn != 128 && L.bn != 160 && L.bn != 256) return false;
+  if (L.tp.num_m_tiles < 2) return false;
+  L.tp.m_pairs = (L.tp.num_m_tiles + 1) / 2;
+  return true;
+}
+
 static int dispatch(GemmLaunch& L, cudaStream_t st) {
   if (L.kind == MT_F32) {
     if (L.conv) return launch_variant<128, true, true>(L, st);
     if (L.bn == 64) return launch_variant<64, true, false>(L, st);
     return launch_variant<128, true, false>(L, st);
+  }
+  if (use_pair(L)) {
+    if (L.conv) {
+      switch (L.bn) {
+        case 128: return launch_variant<128, false, true, false, true>(L, st);
+        case 160: return launch_variant<160, false, true, false, true>(L, st);
+        default: return launch_variant<256, false, true, false, true>(L, st);
+      }
+    }
+    if (!use_bres(L)) {
+      switch (L.bn) {
+        case 128: return launch_variant<128, false, false, false, true>(L, st);
+        case 160: return launch_variant<160, false, false, false, true>(L, st);
+        default: return launch_variant<256, false, false, false, true>(L, st);
+      }
+    }
   }
   if (L.conv) {
     switch (L.bn) {
@@ -791,6 +904,7 @@ int run_gemm(const mt_gemm_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st)
   const int64_t a_b = p.a_batched ? d.batch : 1, b_b = p.b_batched ? d.batch : 1;
   rc = map_kmajor(&L.a, d.dtype, p.A, d.K, d.M, a_b, p.lda, p.sa, kBM);
   if (!rc) rc = map_kmajor(&L.b, d.dtype, p.B, d.K, d.N, b_b, p.ldb, p.sb, L.bn);
+  L.b_ptr = p.B; L.b_K = d.K; L.b_rows = d.N; L.b_batch = b_b; L.b_pitch = p.ldb; L.b_bstride = p.sb;
   if (!rc && d.dtype == MT_F32) {
     rc = map_kmajor(&L.alo, MT_F32, p.Alo, d.K, d.M, a_b, p.Kp, d.M * p.Kp, kBM);
     if (!rc) rc = map_kmajor(&L.blo, MT_F32, p.Blo, d.K, d.N, b_b, p.Kp, d.N * p.Kp, L.bn);
@@ -980,6 +1094,7 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   if (!tf32) L->bn = narrow_bn(L->bn, d.K, tp.num_m_tiles, false);
   tp.num_n_tiles = (int)((d.K + L->bn - 1) / L->bn);
   if (!rc) rc = map_kmajor(&L->b, d.dtype, wp, Kg, d.K, 1, Kg, 0, L->bn);
+  L->b_ptr = wp; L->b_K = Kg; L->b_rows = d.K; L->b_batch = 1; L->b_pitch = Kg; L->b_bstride = 0;
   if (!rc && tf32) rc = map_kmajor(&L->blo, MT_F32, wlo, Kg, d.K, 1, Kg, 0, L->bn);
   if (rc) return rc;
   if (!tf32) {
