@@ -654,11 +654,11 @@ static bool use_bres(GemmLaunch& L) {
 }
 
 // Whether the CTA-pair variant is used: 16-bit, column tiles of 128 / 160 / 256 (half-width B
-// boxes of whole 8-row swizzle atoms), at least two row tiles.  MT_GEMM_PAIR=0 turns it off.
+// boxes of whole 8-row swizzle atoms), at least two row tiles.  MT_GEMM_PAIR=1 turns it on.
 static bool use_pair(GemmLaunch& L) {
   static const bool off = [] {
     const char* e = getenv("MT_GEMM_PAIR");
-    return e && e[0] == '0';
+    return !(e && e[0] == '1');
   }();
   if (off || L.kind == MT_F32 || !L.b_ptr) return false;
   if (L.bn != 128 && L.bn != 160 && L.bn != 256) return false;
