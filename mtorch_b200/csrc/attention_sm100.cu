@@ -423,14 +423,8 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
 // for its previous PV product — only for the S tile it consumes.
 constexpr float kLazyThreshold = 8.0f;  // log2 of the largest p allowed before rescaling
 
-// SPLIT: two softmax threads per query row, each owning 64 of the 128 key columns of a score
-// tile (16 softmax warps instead of 8).  The exponential unit is the bound; twice as many
-// independent warps keep it fed across the max pass and the barrier waits of the other warps.
-// The two halves exchange their row maxima through shared memory behind an mbarrier per tile
-// parity (bounded waits, like every other wait here); the half with columns 0..63 rescales O
-// and writes the output.
-template <int DP, int DVP, bool F16, bool SUMCOL, bool SPLIT = false>
-__global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
+template <int DP, int DVP, bool F16, bool SUMCOL>
+__global__ void __launch_bounds__(320, 1)
     fa_lazy_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const FaParams p) {
   constexpr int NQ = 2;
@@ -469,11 +463,8 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
   // consumes tile j, so one barrier per tile could complete two phases ahead of its waiter.
   uint64_t* p_full = s_empty + 2;              // [2 tiles][2 buffers]
   uint64_t* p_free = p_full + 4;               // [2 tiles][2 buffers]
-  uint64_t* x_bar = p_free + 4;                // SPLIT: [2 tiles][2 parities] max exchange
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_bar + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_free + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* xch = reinterpret_cast<float*>(bars + 64);  // SPLIT: [2 tiles][2 parities][2 halves][128 rows]
-  constexpr int kSoftmaxThreads = SPLIT ? 256 : 128;  // per query tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
@@ -492,12 +483,11 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kSoftmaxThreads);
+      mbar_init(&s_empty[i], 128);
     }
     for (int i = 0; i < 4; ++i) {
-      mbar_init(&p_full[i], kSoftmaxThreads);
+      mbar_init(&p_full[i], 128);
       mbar_init(&p_free[i], 1);
-      mbar_init(&x_bar[i], kSoftmaxThreads);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -610,13 +600,7 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
       }
     }
   } else {
-    // softmax warps: group g of four warps (one per TMEM lane quarter) = query tile x, columns
-    // [hc * NCOL, (hc + 1) * NCOL) of each score tile
-    const int g = (warp - 2) >> 2;
-    const int x = SPLIT ? (g & 1) : g;
-    const int hc = SPLIT ? (g >> 1) : 0;
-    constexpr int NCOL = SPLIT ? kFaBN / 2 : kFaBN;
-    const int col_lo = hc * NCOL;
+    const int x = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -626,17 +610,6 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
     const float sl = p.scale_log2;
     const uint64_t sl2 = f2_bits(sl, sl);
     bool ok = true;
-    // SPLIT: publish v for exchange round e, wait for the partner half's value and return it
-    auto exchange = [&](float v, int e, bool& good) -> float {
-      float* slot = xch + ((x * 2 + (e & 1)) * 2) * kFaBM;
-      slot[hc * kFaBM + row] = v;
-      mbar_arrive(&x_bar[x * 2 + (e & 1)]);
-      if (!mbar_wait(&x_bar[x * 2 + (e & 1)], (e >> 1) & 1, 31, abort_flag)) {
-        good = false;
-        return v;
-      }
-      return slot[(hc ^ 1) * kFaBM + row];
-    };
     for (int j = 0; j < n_tiles && ok; ++j) {
       if (!mbar_wait(&s_full[x], j & 1, 26, abort_flag)) {
         ok = false;
@@ -647,7 +620,7 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
       const bool full = kvalid == kFaBN;
       float mx = -INFINITY;
 #pragma unroll 1
-      for (int c0 = col_lo; c0 < col_lo + NCOL; c0 += 64) {
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
         uint32_t r[64];
         tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
@@ -660,10 +633,6 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
             if (c0 + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
         }
       }
-      if (SPLIT) {
-        mx = fmaxf(mx, exchange(mx, j, ok));
-        if (!ok) break;
-      }
       const float mt = mx * sl;
       if (j == 0) {
         m_used = mt;
@@ -671,10 +640,8 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
         const bool need = mt > m_used + kLazyThreshold;
         if (__any_sync(0xffffffffu, need)) {
           // O holds the sum over the previous tiles: wait for the last PV, then rescale in TMEM
-          // (SPLIT: the half with the low columns rescales; both keep the same m_used / l_run)
           const float m_new = need ? mt : m_used;
           const float corr = ex2(m_used - m_new);
-          if (hc == 0) {
           // PV_{j-1} released P buffer (j-1)&1 (its use number (j-1)>>1); commits complete in issue
           // order, so this also covers every earlier PV.  Phases of p_free are consumed in order,
           // which keeps the parity test unambiguous.
@@ -693,7 +660,6 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
             tmem_st16(t_o + c0, r);
           }
           tmem_st_wait();
-          }
           l_run *= corr;
           m_used = m_new;
         }
@@ -707,12 +673,12 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
       const uint64_t negm2 = f2_bits(-m_used, -m_used);
       uint64_t sum2 = f2_bits(0.f, 0.f);
 #pragma unroll 1
-      for (int c0 = col_lo; c0 < col_lo + NCOL; c0 += 64) {
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
         uint32_t r[64];
         tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
-        if (c0 == col_lo + NCOL - 64) {  // the last read of S: the next QK^T may overwrite it
+        if (c0 == kFaBN - 64) {  // the last read of S: the next QK^T may overwrite it
           tc_fence_before();
           mbar_arrive(&s_empty[x]);
         }
@@ -746,11 +712,8 @@ __global__ void __launch_bounds__(SPLIT ? 576 : 320, 1)
       f2_unpack(sum2, s0, s1);
       l_run += s0 + s1;
     }
-    // SPLIT without the ones column: the row sum is the sum of both halves' partial sums
-    if (SPLIT && !SUMCOL && ok) l_run += exchange(l_run, n_tiles, ok);
     // final: O (all PV products accumulated) / l
-    if (ok && hc == 0 &&
-        mbar_wait(&p_free[x * 2 + ((n_tiles - 1) & 1)], ((n_tiles - 1) >> 1) & 1, 29, abort_flag)) {
+    if (ok && mbar_wait(&p_free[x * 2 + ((n_tiles - 1) & 1)], ((n_tiles - 1) >> 1) & 1, 29, abort_flag)) {
       tc_fence_after();
       float o[DVP];
 #pragma unroll
@@ -854,20 +817,18 @@ static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
 }
 
 // Launch of the lazy-rescale variant; returns false (not launched) when two KV stages do not fit.
-template <int DP, int DVP, bool F16, bool SUMCOL, bool SPLIT>
-static int fa_lazy_launch_t(const mt_sdpa_desc& d, cudaStream_t st, bool* launched) {
+template <int DP, int DVP, bool F16, bool SUMCOL>
+static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched) {
   constexpr int FIXED = 2 * (kFaBM * DP * 2 + 2 * kFaBM * kFaBN * 2);
   constexpr int K_BYTES = kFaBN * DP * 2, V_BYTES = kFaBN * DVP * 2;
   constexpr int SMEM_MAX = 224 * 1024;
   const int stages_v = 2;
-  int stages_k = (SMEM_MAX - 2048 - FIXED - stages_v * V_BYTES - (SPLIT ? 4096 : 0)) / K_BYTES;
+  int stages_k = (SMEM_MAX - 2048 - FIXED - stages_v * V_BYTES) / K_BYTES;
   if (stages_k > kFaMaxStages) stages_k = kFaMaxStages;
   *launched = false;
   if (stages_k < 2) return MT_OK;
-  // barriers in the first 512 bytes after the V ring, then (SPLIT) the 4 KB max-exchange area
-  const int smem = FIXED + stages_k * K_BYTES + stages_v * V_BYTES + 2048 + 1024 + (SPLIT ? 4096 : 0);
-  if (smem > 227 * 1024) return MT_OK;
-  auto kern = fa_lazy_sm100_kernel<DP, DVP, F16, SUMCOL, SPLIT>;
+  const int smem = FIXED + stages_k * K_BYTES + stages_v * V_BYTES + 2048 + 1024;
+  auto kern = fa_lazy_sm100_kernel<DP, DVP, F16, SUMCOL>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -892,20 +853,9 @@ static int fa_lazy_launch_t(const mt_sdpa_desc& d, cudaStream_t st, bool* launch
   p.stages = stages_k;
   p.stages_v = stages_v;
   dim3 grid((unsigned)((d.Sq + 2 * kFaBM - 1) / (2 * kFaBM)), (unsigned)(d.B * d.H));
-  kern<<<grid, SPLIT ? 576 : 320, smem, st>>>(mq, mk, mv, p);
+  kern<<<grid, 320, smem, st>>>(mq, mk, mv, p);
   *launched = true;
   return check_launch("flash_attention_lazy_sm100");
-}
-
-// MT_FA_SPLIT=1 selects the column-split softmax (two threads per query row).
-template <int DP, int DVP, bool F16, bool SUMCOL>
-static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched) {
-  static const bool split = [] {
-    const char* e = getenv("MT_FA_SPLIT");
-    return e && e[0] == '1';
-  }();
-  if (split) return fa_lazy_launch_t<DP, DVP, F16, SUMCOL, true>(d, st, launched);
-  return fa_lazy_launch_t<DP, DVP, F16, SUMCOL, false>(d, st, launched);
 }
 
 size_t sdpa_tc_workspace(const mt_sdpa_desc&) { return 0; }
