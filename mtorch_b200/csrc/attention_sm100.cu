@@ -36,6 +36,7 @@ struct FaParams {
   int out_dtype;
   int stages;    // KV stages (K and V tiles together); the lazy kernel: K stages
   int stages_v;  // lazy kernel: V stages
+  int causal;    // fa_sm100_kernel: key j of query i is masked when j > i (top-left aligned)
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -289,7 +290,10 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
       }
       tc_fence_after();
       const uint32_t ts = tmem + slot * 128 + lane_off;
-      const int kvalid = min(kFaBN, p.Sk - j * kFaBN);
+      // keys of this tile the row may see; causal rows see keys 0..qi (tile 0 always holds key 0,
+      // so the running max is finite after the first tile)
+      int kvalid = min(kFaBN, p.Sk - j * kFaBN);
+      if (p.causal) kvalid = max(0, min(kvalid, qbase + x * kFaBM + row - j * kFaBN + 1));
       const bool full = kvalid == kFaBN;
       // TMEM reads are issued 64 columns at a time before one tcgen05.wait::ld, so the load
       // latency is paid twice per pass rather than once per 16 columns.
@@ -811,6 +815,7 @@ static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
   p.Dv = (int)d.Dv;
   p.out_dtype = d.dtype;
   p.stages = stages;
+  p.causal = d.causal ? 1 : 0;
   dim3 grid((unsigned)((d.Sq + kFaBM * NQ - 1) / (kFaBM * NQ)), (unsigned)(d.B * d.H));
   kern<<<grid, 64 + 128 * NQ, smem, st>>>(mq, mk, mv, p);
   return check_launch("flash_attention_sm100");
@@ -867,7 +872,7 @@ static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, cudaStream_t st, bool*
   // two query tiles per CTA when there are enough queries to fill them
   const bool two = d.Sq > kFaBM;
   *handled = true;
-  if (two && Dp == 48 && d.scale > 0 && !getenv("MT_FA_NO_LAZY")) {
+  if (two && Dp == 48 && d.scale > 0 && !d.causal && !getenv("MT_FA_NO_LAZY")) {
     bool launched = false;
     const int rc = d.Dv <= 40 ? fa_lazy_launch<48, 48, F16, true>(d, st, &launched)
                               : fa_lazy_launch<48, 48, F16, false>(d, st, &launched);
@@ -886,7 +891,7 @@ static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, cudaStream_t st, bool*
 int run_sdpa_tc(const mt_sdpa_desc& d, void*, size_t, cudaStream_t st, bool* handled) {
   *handled = false;
   if (d.dtype != MT_BF16 && d.dtype != MT_F16) return MT_OK;
-  if (d.mask_kind != 0 || d.causal) return MT_OK;
+  if (d.mask_kind != 0) return MT_OK;
   if (d.D != d.Dv || d.D % 8 != 0) return MT_OK;
   if (d.Sq > INT32_MAX || d.Sk > INT32_MAX || d.B * d.H > 65535) return MT_OK;
   if (!aligned16p(d.q) || !aligned16p(d.k) || !aligned16p(d.v)) return MT_OK;

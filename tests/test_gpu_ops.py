@@ -357,6 +357,18 @@ def test_sdpa_bf16(B, H, Sq, Sk, D):
     check(got, ref, BF16_RTOL)
 
 
+@pytest.mark.parametrize("B,H,Sq,Sk,D", [(2, 12, 77, 77, 64), (1, 4, 300, 300, 64), (1, 4, 200, 330, 40),
+                                         (1, 4, 330, 200, 80), (2, 2, 129, 129, 64)])
+def test_sdpa_bf16_causal(B, H, Sq, Sk, D):
+    """Causal attention on the tensor-core kernel (key j of query i hidden when j > i, the top-left
+    alignment of the reference), with ragged query and key tiles and Sq != Sk both ways."""
+    q, k, v = rnd(B, H, Sq, D), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
+    ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v), causal=True)
+    got = mt.scaled_dot_product_attention(cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16"),
+                                          is_causal=True).numpy()
+    check(got, ref, BF16_RTOL)
+
+
 def test_sdpa_bf16_growing_scores_rescale():
     """Later key tiles score much higher than earlier ones, so the running maximum grows by far more
     than the lazy-rescale threshold several times within a row."""
