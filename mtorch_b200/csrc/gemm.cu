@@ -216,9 +216,40 @@ __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b,
 
 // Shared memory of the B-resident variant's operand region (B tile + A stages).
 constexpr int kResBytes = 200 * 1024;
+// TMA-store epilogue: each epilogue warp stages its 32 x 32 output chunk in one of two private
+// 2 KB shared-memory buffers (64-byte swizzle) and stores it with one bulk tensor store.
+constexpr int kStoreBytes = 8 * 2 * 2048;
+
+__device__ __forceinline__ void gemm_fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Stage 32 output values of this lane's row (bf16 / f16) into the warp's 32 x 64-byte buffer with
+// the 64-byte swizzle the store's tensor map uses (16-byte chunk k of row r at k ^ ((r >> 1) & 3)),
+// which keeps the warp's shared-memory writes free of bank conflicts.
+__device__ __forceinline__ void stage_row32(uint8_t* buf, int lane, int dtype, const float (&v)[32]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = dtype == MT_BF16 ? pack_bf16x2(v[8 * k + 2 * j], v[8 * k + 2 * j + 1])
+                              : pack_f16x2(v[8 * k + 2 * j], v[8 * k + 2 * j + 1]);
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
 constexpr int kMaxResStages = 8;
 
-template <int BN, bool TF32, bool PAIR = false>
+template <int BN, bool TF32, bool PAIR = false, bool TST = false>
 struct GemmCfg {
   static constexpr int A_BYTES = kBM * 128;
   static constexpr int B_BYTES = BN * 128;
@@ -226,14 +257,16 @@ struct GemmCfg {
   static constexpr int B_STAGE_BYTES = PAIR ? B_BYTES / 2 : B_BYTES;
   static constexpr int OPS = TF32 ? 2 : 1;
   static constexpr int STAGE_BYTES = (A_BYTES + B_STAGE_BYTES) * OPS;
-  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int ST_BYTES = TST ? kStoreBytes : 0;
+  // TST: the staging buffers come on top of the usual ring where the 227 KB limit allows
+  static constexpr int STAGES_RAW = TST ? (226 * 1024 - ST_BYTES) / STAGE_BYTES : (200 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
   static constexpr int TMEM_COLS = (2 * BN <= 32)    ? 32
                                    : (2 * BN <= 64)  ? 64
                                    : (2 * BN <= 128) ? 128
                                    : (2 * BN <= 256) ? 256
                                                      : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + ST_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   // B-resident variant: [B tile, all K chunks][A stages] within kResBytes, barriers after it.
   static constexpr int RES_SMEM_BYTES = kResBytes + 1024 + 256;
 };
@@ -247,12 +280,17 @@ struct GemmCfg {
 // issued by the even CTA; each CTA loads its own 128 rows of A and BN/2 rows of B (its half of
 // the columns), so every SM streams half as many B bytes per MMA as a single-CTA tile of the same
 // width.  Each CTA's TMEM holds its 128 rows of D and its epilogue stores them.
-template <int BN, bool TF32, bool CONV, bool BRES, bool PAIR = false>
+//
+// TST (TMA-store epilogue, plain GEMMs with 16-bit output): output chunks go through per-warp
+// shared-memory buffers and bulk tensor stores (tmD) instead of per-row global stores.
+template <int BN, bool TF32, bool CONV, bool BRES, bool PAIR = false, bool TST = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmAlo, const __grid_constant__ CUtensorMap tmBlo,
-                      const TileParams tp, const EpiParams ep, const uint32_t idesc) {
-  using Cfg = GemmCfg<BN, TF32, PAIR>;
+                      const __grid_constant__ CUtensorMap tmD, const TileParams tp, const EpiParams ep,
+                      const uint32_t idesc) {
+  using Cfg = GemmCfg<BN, TF32, PAIR, TST>;
+  static_assert(!TST || (!TF32 && !CONV && !PAIR), "TMA-store epilogue: plain 16-bit GEMMs");
   static_assert(!BRES || (!TF32 && !CONV), "B-resident variant: 16-bit GEMMs only");
   static_assert(!PAIR || (!TF32 && !BRES), "CTA-pair variant: 16-bit streaming GEMMs only");
   const int STAGES = BRES ? tp.a_stages : Cfg::STAGES;
@@ -262,7 +300,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sbres = smem;  // BRES: k_iters chunks of B_BYTES
   uint8_t* stage_base = BRES ? smem + tp.k_iters * Cfg::B_BYTES : smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (BRES ? kResBytes : Cfg::STAGES * Cfg::STAGE_BYTES));
+  // TST staging: after the ring, or (BRES) the last kStoreBytes of the resident region (the host
+  // sizes the B tile + A stages to leave it free)
+  uint8_t* sstore = BRES ? smem + kResBytes - Cfg::ST_BYTES : smem + Cfg::STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(smem + (BRES ? kResBytes : Cfg::STAGES * Cfg::STAGE_BYTES + Cfg::ST_BYTES));
   uint64_t* empty = full + (BRES ? kMaxResStages : Cfg::STAGES);
   uint64_t* tfull = empty + (BRES ? kMaxResStages : Cfg::STAGES);
   uint64_t* tempty = tfull + 2;
@@ -448,6 +490,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool geglu = ep.act == MT_EPI_GEGLU;
     const int64_t n_out = geglu ? ep.N / 2 : ep.N;
     int local = 0;
+    int sbuf = 0;  // TST: which of this warp's two staging buffers is next
+    // TST: the warp's 32 output rows x 32 columns via shared memory and one bulk tensor store
+    auto store_chunk = [&](const float (&v)[32], int64_t col0, int mt, int b) {
+      uint8_t* sb = sstore + ((warp - 2) * 2 + sbuf) * 2048;
+      if (lane == 0) bulk_wait_read1();  // the store that last read this buffer has read it
+      __syncwarp();
+      stage_row32(sb, lane, ep.out_dtype, v);
+      gemm_fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&tmD, sb, (int)col0, mt * kBM + (warp & 3) * 32, b);
+        bulk_commit();
+      }
+      sbuf ^= 1;
+    };
     for (int t = tile0; t < total_tiles; t += tstep, ++local) {
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
@@ -493,13 +550,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int64_t col0 = (int64_t)nt * BN + c0;
           const int64_t remain = n_out - col0;
           const int nvalid = remain < 32 ? (int)remain : 32;
-          if (valid && nvalid > 0) {
+          // TST: every lane of the warp takes part in the store (rows past M are clipped by TMA)
+          if ((valid || TST) && nvalid > 0) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
             if (ep.bias)
               row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, ep.bias_vec != 0, 1.f, v);
-            if (ep.C) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
+            if (ep.C && valid) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
             if (ep.act == MT_EPI_GELU) {
               if (TF32) {
 #pragma unroll
@@ -515,8 +573,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = v[j] * (1.0f / (1.0f + expf(-__fmul_rn(v[j], 1.702f))));
             }
-            if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
-            row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
+            if (ep.res && valid) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
+            if (TST)
+              store_chunk(v, col0, mt, b);
+            else
+              row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
           }
         }
       } else {
@@ -534,7 +595,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int64_t col0 = (int64_t)nt * (BN / 2) + g * 64 + h;
             const int64_t remain = n_out - col0;
             const int nvalid = remain < 32 ? (int)remain : 32;
-            if (valid && nvalid > 0) {
+            if ((valid || TST) && nvalid > 0) {
               float v[32], gt[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
@@ -547,8 +608,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              gt);
               }
               epi_gelu32<TF32>(v, gt);
-              if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
-              row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
+              if (ep.res && valid) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
+              if (TST)
+                store_chunk(v, col0, mt, b);
+              else
+                row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
             }
           }
         }
@@ -559,6 +623,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       else
         mbar_arrive(&tempty[buf]);
     }
+    if (TST && lane == 0) bulk_wait_all();  // this warp's stores are done before the CTA exits
   }
   __syncthreads();
   if (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal its barriers
@@ -583,16 +648,19 @@ struct GemmLaunch {
   bool conv;
   // B operand as mapped (K-major), kept so the CTA-pair variant can re-map it with half-width boxes
   const void* b_ptr; int64_t b_K, b_rows, b_batch, b_pitch, b_bstride;
+  // TMA-store epilogue: output map (32 x 32 boxes, 64-byte swizzle) when `tst`
+  CUtensorMap d;
+  bool tst;
 };
 
 static int map_kmajor(CUtensorMap* m, int dtype, const void* base, int64_t K, int64_t rows, int64_t batch,
                       int64_t pitch, int64_t bstride, int box_rows);
 
-template <int BN, bool TF32, bool CONV, bool BRES = false, bool PAIR = false>
+template <int BN, bool TF32, bool CONV, bool BRES = false, bool PAIR = false, bool TST = false>
 static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
-  using Cfg = GemmCfg<BN, TF32, PAIR>;
+  using Cfg = GemmCfg<BN, TF32, PAIR, TST>;
   constexpr int smem = BRES ? Cfg::RES_SMEM_BYTES : Cfg::SMEM_BYTES;
-  auto kern = gemm_sm100_kernel<BN, TF32, CONV, BRES, PAIR>;
+  auto kern = gemm_sm100_kernel<BN, TF32, CONV, BRES, PAIR, TST>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -626,12 +694,12 @@ static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P.a, P.b, P.alo, P.b, P.tp, P.ep, idesc);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P.a, P.b, P.alo, P.b, P.a, P.tp, P.ep, idesc);
     if (e != cudaSuccess) return fail(MT_ERR_LAUNCH, "gemm_sm100 (CTA pairs): %s", cudaGetErrorString(e));
     return check_launch("gemm_sm100_pair");
   }
   const uint32_t idesc = make_idesc(fmt, kBM, BN);
-  kern<<<grid, kGemmThreads, smem, st>>>(L.a, L.b, L.alo, L.blo, L.tp, L.ep, idesc);
+  kern<<<grid, kGemmThreads, smem, st>>>(L.a, L.b, L.alo, L.blo, TST ? L.d : L.a, L.tp, L.ep, idesc);
   return check_launch("gemm_sm100");
 }
 
@@ -642,7 +710,7 @@ static bool use_bres(GemmLaunch& L) {
   static const bool off = getenv("MT_GEMM_NO_BRES") != nullptr;
   if (off || L.kind == MT_F32 || L.conv || L.tp.batch != 1) return false;
   const int b_bytes = L.bn * 128 * L.tp.k_iters;
-  const int stages = std::min(kMaxResStages, (kResBytes - b_bytes) / (kBM * 128));
+  const int stages = std::min(kMaxResStages, (kResBytes - (L.tst ? kStoreBytes : 0) - b_bytes) / (kBM * 128));
   if (stages < 3) return false;
   const int sms = num_sms(), nn = L.tp.num_n_tiles;
   if (nn > sms) return false;
@@ -695,6 +763,22 @@ static int dispatch(GemmLaunch& L, cudaStream_t st) {
       case 128: return launch_variant<128, false, true>(L, st);
       case 160: return launch_variant<160, false, true>(L, st);
       default: return launch_variant<256, false, true>(L, st);
+    }
+  }
+  if (L.tst) {
+    if (use_bres(L)) {
+      switch (L.bn) {
+        case 64: return launch_variant<64, false, false, true, false, true>(L, st);
+        case 128: return launch_variant<128, false, false, true, false, true>(L, st);
+        case 160: return launch_variant<160, false, false, true, false, true>(L, st);
+        default: return launch_variant<256, false, false, true, false, true>(L, st);
+      }
+    }
+    switch (L.bn) {
+      case 64: return launch_variant<64, false, false, false, false, true>(L, st);
+      case 128: return launch_variant<128, false, false, false, false, true>(L, st);
+      case 160: return launch_variant<160, false, false, false, false, true>(L, st);
+      default: return launch_variant<256, false, false, false, false, true>(L, st);
     }
   }
   if (use_bres(L)) {
@@ -937,6 +1021,20 @@ int run_gemm(const mt_gemm_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st)
     vec = vec && aligned16(d.residual) && (d.ldr * oes) % 16 == 0 && (d.batch == 1 || (d.stride_r * oes) % 16 == 0);
   ep.vec_ok = vec;
   ep.bias_vec = bias_vec_ok(d.bias, d.bias_dtype, d.bias_batch_stride);
+  // TMA-store epilogue for 16-bit outputs with 16-byte aligned rows (MT_GEMM_TSTORE=0 turns it off)
+  static const bool tst_off = [] {
+    const char* e = getenv("MT_GEMM_TSTORE");
+    return e && e[0] == '0';
+  }();
+  L.tst = false;
+  if (!tst_off && d.dtype != MT_F32 && (d.out_dtype == MT_BF16 || d.out_dtype == MT_F16) && vec &&
+      d.M <= INT32_MAX && d.N <= INT32_MAX) {
+    const int64_t n_out = geglu ? d.N / 2 : d.N;
+    uint64_t dims[3] = {(uint64_t)n_out, (uint64_t)d.M, (uint64_t)d.batch};
+    uint64_t strides[2] = {(uint64_t)(d.ldd * oes), (uint64_t)((d.batch > 1 ? d.stride_d : d.M * d.ldd) * oes)};
+    uint32_t box[3] = {32, 32, 1};
+    L.tst = make_tensor_map(&L.d, d.out_dtype, 3, d.D, dims, strides, box, 64) == MT_OK;
+  }
   return dispatch(L, st);
 }
 
