@@ -10,8 +10,9 @@ timed region.  `value` = steps/s of the whole 64-sample job.
     python bench.py --workload sampler|vae|text [--batch B]   (the workloads around the UNet)
 
 `--impl reference` times the reference mtorch's own CPU implementation (built from its sources
-into oracle/_ref; the restated C oracle when that is absent) on the host cores, on a bounded
-sample of the same workload, and reports the extrapolated steps/s.
+into oracle/_ref; the restated C oracle when that is absent) on all host cores: each step runs
+every op of one sample's UNet forward at full widths on 1/R of its output rows (oracle/cpu_bench.py),
+and `value` is the C5 steps/s that implies (one C5 step = 64 * R sampled steps).
 """
 from __future__ import annotations
 
@@ -51,15 +52,40 @@ def peaks():
 # clocks
 
 
+def smi_index(local: int):
+    """nvidia-smi's index of torch device `local` (matched by UUID; CUDA_VISIBLE_DEVICES as the
+    fallback), so that each rank samples only the GPU it runs on."""
+    try:
+        import torch
+
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+        out = subprocess.run(["nvidia-smi", "--query-gpu=index,uuid", "--format=csv,noheader"], capture_output=True,
+                             text=True, timeout=30).stdout
+        for line in out.splitlines():
+            idx, u = [x.strip() for x in line.split(",")[:2]]
+            if u.lower().removeprefix("gpu-") == uuid.lower().removeprefix("gpu-"):
+                return int(idx)
+    except Exception:  # noqa: BLE001
+        pass
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    parts = [v.strip() for v in vis.split(",") if v.strip()]
+    if local < len(parts) and parts[local].isdigit():
+        return int(parts[local])
+    return local
+
+
 class ClockSampler:
-    def __init__(self, path: Path):
-        self.path = path
+    """nvidia-smi sampling (200 ms) of ONE GPU during the timed region."""
+
+    def __init__(self, path: Path, gpu_index: int):
+        self.path, self.gpu_index = path, gpu_index
         self.proc = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                ["nvidia-smi", "-i", str(self.gpu_index),
+                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
                  "--format=csv,noheader,nounits", "-lms", "200"],
@@ -74,123 +100,87 @@ class ClockSampler:
             self.proc.terminate()
             self.proc.wait()
 
-    def summary(self, gpu_index=None):
-        if not self.path.exists():
-            return None
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
+
+def clock_summary(paths):
+    """Median SM clock, max clock and the throttle reasons seen, over the samples of the GPUs the
+    ranks ran on (one file per rank, each holding only its own GPU's samples)."""
+    sm, mx, reasons, gpus = [], None, set(), set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for path in paths:
+        if not Path(path).exists():
+            continue
+        for line in Path(path).read_text().splitlines():
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
-                continue
-            if gpu_index is not None and f[0] != str(gpu_index):
                 continue
             try:
                 sm.append(float(f[1]))
                 mx = float(f[2])
             except ValueError:
                 continue
+            gpus.add(f[0])
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+    if not sm:
+        return None
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+            "gpus": sorted(gpus, key=int)}
 
 
 # ---------------------------------------------------------------------------------------------
 # CPU baseline (reference mtorch on the host cores)
 
 
-def _ref_sample_worker(seconds_hint: float = 0.0):
-    """One bounded sample of the workload on the reference CPU implementation: the UNet's level-0
-    3x3 conv 320->320 on a 16x16 patch of one sample, a 320-wide linear over 512 tokens and a
-    self-attention of 8 heads x 256 tokens x 40 (the three op classes that carry 99% of the UNet's
-    FLOPs).  Returns (seconds per class, flops per class, kind)."""
-    import oracle
+def cpu_sampled_steps(processes: int, warmup: int, steps: int):
+    """Times the reference's CPU path on every op of the UNet (oracle/cpu_bench.py: all ops of one
+    sample's forward at full widths on 1/R of their output rows, spread over `processes` single-
+    threaded processes).  Returns (seconds per sampled step [list], sampler)."""
+    from oracle import cpu_bench
 
-    m = oracle.ref()
-    kind = "reference" if m is not None else "port"
-    rng = np.random.default_rng(0)
-    x = rng.standard_normal((1, 320, 16, 16)).astype(np.float32)
-    w = (rng.standard_normal((320, 320, 3, 3)) * 0.02).astype(np.float32)
-    t = rng.standard_normal((512, 320)).astype(np.float32)
-    lw = (rng.standard_normal((320, 320)) * 0.05).astype(np.float32)
-    q = rng.standard_normal((1, 8, 256, 40)).astype(np.float32)
-    flops = {"conv": 2.0 * 320 * 320 * 9 * 256, "linear": 2.0 * 512 * 320 * 320, "attn": 4.0 * 8 * 256 * 256 * 40}
-    secs = {}
-    if m is not None:
-        F = m.nn.functional
-        mx, mw = m.tensor(x.tolist()), m.tensor(w.tolist())
-        mt_, ml = m.tensor(t.tolist()), m.tensor(lw.tolist())
-        mq = m.tensor(q.tolist())
-        t0 = time.perf_counter(); F.conv2d(mx, mw, None, padding=1); secs["conv"] = time.perf_counter() - t0
-        t0 = time.perf_counter(); F.linear(mt_, ml); secs["linear"] = time.perf_counter() - t0
-        t0 = time.perf_counter(); F.scaled_dot_product_attention(mq, mq, mq); secs["attn"] = time.perf_counter() - t0
-    else:
-        t0 = time.perf_counter(); oracle.conv2d_f32(x, w, None, 1, 1); secs["conv"] = time.perf_counter() - t0
-        t0 = time.perf_counter(); oracle.linear_f32(t, lw); secs["linear"] = time.perf_counter() - t0
-        t0 = time.perf_counter(); oracle.sdpa_f32(q, q, q); secs["attn"] = time.perf_counter() - t0
-    return secs, flops, kind
+    r = cpu_bench.default_r(processes)
+    s = cpu_bench.SampledUNet(processes, r, size=H)
+    try:
+        for _ in range(warmup):
+            s.step()
+        times = [s.step() for _ in range(steps)]
+    finally:
+        s.close()
+    return times, s
 
 
-def _step_flop_split():
-    """FLOPs of one C5 step (64 samples) split into conv / linear / attention classes."""
-    from mtorch_b200.unet import unet_flops_per_sample
-
-    cls: dict = {}
-    total = unet_flops_per_sample(classes=cls) * BATCH
-    return {k: v * BATCH for k, v in cls.items()}, total
-
-
-def cpu_baseline(processes: int = 1):
-    """Extrapolated reference-CPU steps/s from one bounded sample per process."""
-    if processes <= 1:
-        secs, flops, kind = _ref_sample_worker()
-        rates = [{k: flops[k] / secs[k] for k in secs}]
-    else:
-        import multiprocessing as mp
-
-        with mp.get_context("spawn").Pool(processes) as pool:
-            res = pool.map(_ref_sample_worker, [0.0] * processes)
-        kind = res[0][2]
-        rates = [{k: r[1][k] / r[0][k] for k in r[0]} for r in res]
-    split, total = _step_flop_split()
-    # aggregate rate of P independent single-threaded processes
-    agg = {k: sum(r[k] for r in rates) for k in rates[0]}
-    sec_per_step = sum(split[k] / agg[k] for k in split)
-    sample = ("reference mtorch portable CPU path: conv2d 1x320x16x16 3x3 (0.47 GFLOP), linear 512x320x320 "
-              "(0.10 GFLOP), sdpa 1x8x256x40 (0.08 GFLOP) per process; UNet step time extrapolated by FLOP class "
-              "(conv / linear / attention FLOP classes of the 51.4 TFLOP step)")
-    return {"value": 1.0 / sec_per_step, "unit": "steps/s", "cores": processes, "kind": kind, "sample": sample,
-            "gflops_per_s": {k: v / 1e9 for k, v in agg.items()}}
+def cpu_result(times, s, processes):
+    """steps/s of the 64-sample C5 step from the sampled steps: one C5 step = 64 * R sampled steps."""
+    sec = statistics.median(times)
+    value = 1.0 / (BATCH * s.r * sec)
+    return {"value": value, "unit": "steps/s", "cores": processes, "kind": s.kind,
+            "sample": s.describe() + f"; median {sec:.2f} s per sampled step over {len(times)} steps",
+            "sampled_fraction_of_step": 1.0 / (BATCH * s.r), "seconds_per_sampled_step": sec,
+            "gflops_per_s": s.full_flops / s.r / sec / 1e9}
 
 
 # ---------------------------------------------------------------------------------------------
 
 
 def run_reference(args):
+    """The reference arm: the reference mtorch's own CPU implementation, all host cores, a
+    bounded sample per step (see cpu_sampled_steps).  `ms_per_step` is the measured wall time of
+    one sampled step; `value` is the C5 steps/s it implies (64 * R sampled steps per C5 step)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     procs = os.cpu_count() or 1
-    cfg = {"workload": "C5: SD-1.5 UNet, batch 64 latents [64,4,64,64], context [64,77,768], DDIM step",
-           "global_batch": BATCH, "seq_len": H * W, "parallelism": "host cores (independent processes)",
-           "l2": "n/a (CPU)"}
-    for _ in range(args.warmup if args.warmup < 1 else 1):
-        pass
-    times, vals = [], []
-    base = None
-    for _ in range(max(args.steps, 1)):
-        t0 = time.perf_counter()
-        base = cpu_baseline(processes=procs)
-        times.append(time.perf_counter() - t0)
-        vals.append(base["value"])
-    value = statistics.median(vals)
+    times, s = cpu_sampled_steps(procs, args.warmup, max(args.steps, 1))
+    base = cpu_result(times, s, procs)
+    value = base["value"]
+    cfg = {"workload": "C5: SD-1.5 UNet, batch 64 latents [64,4,64,64], context [64,77,768], 1 UNet eval "
+           "per step (fp32 reference CPU path, row-sampled)", "global_batch": BATCH, "seq_len": H * W,
+           "parallelism": f"{procs} host processes, ops of one sample spread over them", "l2": "n/a (CPU)"}
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
-            "cpu_baseline": {**base, "value": value},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * base["seconds_per_sampled_step"],
+            "ms_per_step_is": "wall time of one sampled step (1/(64*R) of a C5 step)",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": cfg, "cpu_baseline": base,
             "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -249,7 +239,7 @@ def run_ours(args):
 
     # ---- device-timed region ----
     lib = _lib.lib()
-    clocks = ClockSampler(out_dir / f"clocks_rank{rank}.csv")
+    clocks = ClockSampler(out_dir / f"clocks_rank{rank}.csv", smi_index(local))
     with clocks:
         if dist:
             dist.barrier()
@@ -260,8 +250,9 @@ def run_ours(args):
         e0.record(stream)
         for i in range(args.steps):
             x = step(args.warmup + i, x)
-        if dist:
-            parallel.gather_shards(x.contiguous()._buf[:x.numel() * 2])  # output latents, all ranks
+        gathered = None
+        if dist:  # output latents, all ranks
+            gathered = parallel.gather_shards(x.contiguous()._buf[:x.numel() * 2])
         e1.record(stream)
         torch.cuda.synchronize()
         if dist:
@@ -351,19 +342,45 @@ def run_ours(args):
                      "frac": conv_ach / tf_burst, "peak_kind": f"{peak_kind} bf16 burst",
                      "traffic": DRAM_BYTES_PER_SAMPLE["conv"] * nb, "ms_per_launch": conv_ms}
 
+    # ---- N-GPU result vs a 1-GPU run of the whole batch (rank 0, untimed): the sharded latents
+    # after W + K steps must equal, bit for bit, the same steps on all 64 samples on one GPU ----
+    bitwise = None
+    if dist:
+        if rank == 0:
+            del graphed
+            x64 = lat_all.to("bfloat16").to(dev)
+            ctx64 = ctx_all.to("bfloat16").to(dev)
+            temb64 = [mt.tensor(timestep_embedding(np.full(BATCH, float(t))), dtype="bfloat16", device=dev)
+                      for t in sched.timesteps]
+            g64 = Graphed(unet, x64, temb64[0], ctx64) if use_graph else None
+            for i in range(args.warmup + args.steps):
+                te = temb64[i % len(temb64)]
+                eps = g64(x64, te, ctx64) if use_graph else unet(x64, te, ctx64)
+                x64 = sched.step(x64, eps, sched.timesteps[i % len(sched.timesteps)])
+            torch.cuda.synchronize()
+            ref = x64.contiguous()._buf[:x64.numel() * 2]
+            bitwise = bool(torch.equal(ref, gathered))
+        dist.barrier()
+
+    clk = clock_summary([out_dir / f"clocks_rank{r}.csv" for r in range(world)]) if rank == 0 else None
     if rank == 0:
-        clk = clocks.summary(gpu_index=None)
         # the attention kernel is bound by the exponential unit: 16 ex2 per SM per clock (the
         # same for .f32 / .f16x2 / .bf16x2, measured), at the median SM clock of the timed region
-        mhz = (clk or {}).get("sm_mhz") or 1965.0
-        exp_rate = nb * 8 * float(H * W) ** 2 / (attn_ms * 1e-3)
-        exp_peak = 16.0 * 148 * mhz * 1e6
-        roofline["exp_unit"] = {"achieved": exp_rate, "peak": exp_peak, "unit": "exp2/s",
-                                "frac": exp_rate / exp_peak, "sm_mhz": mhz}
-        try:
-            base = cpu_baseline(processes=1)
-        except Exception as e:  # noqa: BLE001
-            base = {"value": None, "unit": "steps/s", "cores": 1, "kind": "unavailable", "sample": str(e)[:200]}
+        # on the GPUs that ran it
+        if clk and clk["samples"] > 0:
+            mhz = clk["sm_mhz"]
+            exp_rate = nb * 8 * float(H * W) ** 2 / (attn_ms * 1e-3)
+            exp_peak = 16.0 * 148 * mhz * 1e6
+            roofline["exp_unit"] = {"achieved": exp_rate, "peak": exp_peak, "unit": "exp2/s",
+                                    "frac": exp_rate / exp_peak, "sm_mhz": mhz}
+        base = None
+        if world == 1:  # the reference CPU path on this box's host cores, bounded sample
+            try:
+                procs = os.cpu_count() or 1
+                times, smp = cpu_sampled_steps(procs, 1, 2)
+                base = cpu_result(times, smp, procs)
+            except Exception as e:  # noqa: BLE001
+                base = {"value": None, "unit": "steps/s", "cores": 0, "kind": "unavailable", "sample": str(e)[:200]}
         line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents/context, random-init "
@@ -372,7 +389,7 @@ def run_ours(args):
                 "global_batch": BATCH, "seq_len": H * W, "parallelism": f"batch-shard dp{world} + NCCL all-gather",
                 "l2": "activations > L2 (126 MB) at batch 64/GPU; no flush"},
                 "gpu_launches": int(launches), "e2e": e2e, "roofline": roofline, "roofline_conv": roofline_conv,
-                "cpu_baseline": base,
+                "cpu_baseline": base, "bitwise_equal_to_1gpu": bitwise,
                 "clocks": clk}
         print(json.dumps(line))
     if dist:

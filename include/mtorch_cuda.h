@@ -52,6 +52,11 @@ int mt_cuda_synchronize(void* stream);
 /* Device-side error word written by bounded waits inside kernels (MT_ERR_TIMEOUT); `clear`
  * resets it.  Returns MT_OK when no kernel reported a problem. */
 int mt_cuda_device_status(int clear);
+/* Failure-detection self test (no counterpart in the reference, which has no device): launches
+ * one kernel whose bounded mbarrier wait can never complete; after `budget_cycles` SM clocks it
+ * gives up, records MT_ERR_TIMEOUT in the device status word and returns, so that the next
+ * mt_cuda_device_status reports the timeout while the context stays usable. */
+int mt_cuda_selftest_wait_timeout(long long budget_cycles, void* stream);
 /* Number of kernels this library has launched in the process (all devices); instrumentation for
  * benchmarks (no counterpart in the reference, which has no device). */
 uint64_t mt_cuda_launch_count(void);
@@ -282,6 +287,15 @@ typedef struct {
 } mt_sdpa_desc;
 size_t mt_cuda_sdpa_workspace_size(const mt_sdpa_desc* desc);
 int mt_cuda_sdpa(const mt_sdpa_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+/* Which kernel mt_cuda_sdpa runs for `desc` (no counterpart in the reference, whose SDPA has one
+ * CPU path): the tcgen05 kernel with the output kept in TMEM (head dims 33-48, more than 128
+ * queries, no mask or causal), the general tcgen05 kernel (16-bit types, head dims that are
+ * multiples of 8 up to 160, padded to 32/48/64/80/128/160; no mask), or the fp32 SIMT kernel
+ * (fp32, masks, other head dims or strides).  Returns 0 for an invalid descriptor. */
+#define MT_SDPA_PATH_TC_LAZY 1
+#define MT_SDPA_PATH_TC 2
+#define MT_SDPA_PATH_SIMT 3
+int mt_cuda_sdpa_path(const mt_sdpa_desc* desc);
 
 /* ---- host random generator: the reference's RandomState (module.cpp:47-183) ------------- */
 /* SplitMix64 + Marsaglia-polar normal with the odd-count "spare" rule, bit-identical to

@@ -16,6 +16,7 @@ MT_OK, MT_ERR_INVALID, MT_ERR_UNSUPPORTED, MT_ERR_LAUNCH, MT_ERR_TIMEOUT, MT_ERR
 UNARY = {"silu": 0, "gelu": 1, "gelu_tanh": 2, "neg": 3, "exp": 4, "sigmoid": 5, "relu": 6, "quick_gelu": 7}
 BINARY = {"add": 0, "sub": 1, "mul": 2, "div": 3}
 EPI_NONE, EPI_GELU, EPI_SILU, EPI_GEGLU, EPI_QUICK_GELU = range(5)
+SDPA_PATH_TC_LAZY, SDPA_PATH_TC, SDPA_PATH_SIMT = 1, 2, 3
 
 I64 = C.c_int64
 I64_4 = I64 * 4
@@ -80,6 +81,7 @@ SIGNATURES = {
     "mt_cuda_set_device": (C.c_int, [C.c_int]),
     "mt_cuda_synchronize": (C.c_int, [VP]),
     "mt_cuda_device_status": (C.c_int, [C.c_int]),
+    "mt_cuda_selftest_wait_timeout": (C.c_int, [C.c_longlong, VP]),
     "mt_cuda_launch_count": (C.c_uint64, []),
     "mt_cuda_memcpy":(C.c_int, [VP, VP, C.c_size_t, C.c_int, VP]),
     "mt_cuda_memset": (C.c_int, [VP, C.c_int, C.c_size_t, VP]),
@@ -115,6 +117,7 @@ SIGNATURES = {
     "mt_cuda_conv2d_up2x_pack_weight": (C.c_int, [VP, VP, VP, C.c_int, I64, I64, VP]),
     "mt_cuda_sdpa_workspace_size": (C.c_size_t, [C.POINTER(SdpaDesc)]),
     "mt_cuda_sdpa": (C.c_int, [C.POINTER(SdpaDesc), VP, C.c_size_t, VP]),
+    "mt_cuda_sdpa_path": (C.c_int, [C.POINTER(SdpaDesc)]),
     "mt_rng_seed": (None, [C.POINTER(RngState), C.c_uint64]),
     "mt_rng_fill_normal": (None, [C.POINTER(RngState), VP, C.c_int, I64, C.c_double, C.c_double]),
     "mt_rng_fill_uniform": (None, [C.POINTER(RngState), VP, C.c_int, I64, C.c_double, C.c_double]),

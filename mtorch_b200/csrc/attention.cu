@@ -195,7 +195,7 @@ static int run_sdpa_simt(const SdpaParams& p, cudaStream_t st) {
 int run_sdpa_tc(const mt_sdpa_desc& d, void* ws, size_t ws_bytes, cudaStream_t st, bool* handled);
 size_t sdpa_tc_workspace(const mt_sdpa_desc& d);
 
-static int validate_sdpa(const mt_sdpa_desc& d) {
+int validate_sdpa_desc(const mt_sdpa_desc& d) {
   if (d.B < 0 || d.H <= 0 || d.Hkv <= 0 || d.Sq < 0 || d.Sk < 0 || d.D <= 0 || d.Dv <= 0)
     return fail(MT_ERR_INVALID, "sdpa: bad sizes");
   if (d.H % d.Hkv != 0)
@@ -208,12 +208,12 @@ static int validate_sdpa(const mt_sdpa_desc& d) {
 }
 
 size_t sdpa_workspace(const mt_sdpa_desc& d) {
-  if (validate_sdpa(d) != MT_OK) return 0;
+  if (validate_sdpa_desc(d) != MT_OK) return 0;
   return sdpa_tc_workspace(d);
 }
 
 int run_sdpa(const mt_sdpa_desc& d, void* ws, size_t ws_bytes, cudaStream_t st) {
-  int rc = validate_sdpa(d);
+  int rc = validate_sdpa_desc(d);
   if (rc) return rc;
   if (d.B == 0 || d.Sq == 0) return MT_OK;
   if (d.Sk == 0) {

@@ -867,39 +867,62 @@ size_t sdpa_tc_workspace(const mt_sdpa_desc&) { return 0; }
 
 static bool aligned16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Padded head dim of the tcgen05 kernels for head dim D (a multiple of 8): the smallest
+// instantiated width >= D (TMA zero-fills the padding columns); 0 when none fits.
+static int64_t tc_head_pad(int64_t D) {
+  if (D % 8 != 0) return 0;
+  for (int64_t w : {32, 48, 64, 80, 128, 160})
+    if (D <= w) return w;
+  return 0;
+}
+
+// Which kernel run_sdpa_tc launches for `d`: MT_SDPA_PATH_TC_LAZY, MT_SDPA_PATH_TC, or
+// MT_SDPA_PATH_SIMT when the tcgen05 kernels do not take it.
+int sdpa_tc_path(const mt_sdpa_desc& d) {
+  if (d.dtype != MT_BF16 && d.dtype != MT_F16) return MT_SDPA_PATH_SIMT;
+  if (d.mask_kind != 0) return MT_SDPA_PATH_SIMT;
+  if (d.D != d.Dv) return MT_SDPA_PATH_SIMT;
+  const int64_t Dp = tc_head_pad(d.D);
+  if (Dp == 0) return MT_SDPA_PATH_SIMT;
+  if (d.Sq > INT32_MAX || d.Sk > INT32_MAX || d.B * d.H > 65535) return MT_SDPA_PATH_SIMT;
+  if (!aligned16p(d.q) || !aligned16p(d.k) || !aligned16p(d.v)) return MT_SDPA_PATH_SIMT;
+  for (int i = 0; i < 3; ++i)
+    if ((d.q_strides[i] * 2) % 16 || (d.k_strides[i] * 2) % 16 || (d.v_strides[i] * 2) % 16)
+      return MT_SDPA_PATH_SIMT;
+  if (d.q_strides[3] != 1 || d.k_strides[3] != 1 || d.v_strides[3] != 1) return MT_SDPA_PATH_SIMT;
+  const bool two = d.Sq > kFaBM;
+  if (two && Dp == 48 && d.scale > 0 && !d.causal && !getenv("MT_FA_NO_LAZY")) return MT_SDPA_PATH_TC_LAZY;
+  return MT_SDPA_PATH_TC;
+}
+
 template <bool F16>
-static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, cudaStream_t st, bool* handled) {
+static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, bool lazy, cudaStream_t st) {
   // two query tiles per CTA when there are enough queries to fill them
   const bool two = d.Sq > kFaBM;
-  *handled = true;
-  if (two && Dp == 48 && d.scale > 0 && !d.causal && !getenv("MT_FA_NO_LAZY")) {
+  if (lazy) {
     bool launched = false;
     const int rc = d.Dv <= 40 ? fa_lazy_launch<48, 48, F16, true>(d, st, &launched)
                               : fa_lazy_launch<48, 48, F16, false>(d, st, &launched);
     if (rc || launched) return rc;
   }
   switch (Dp) {
+    case 32: return two ? fa_launch<32, 32, 2, F16>(d, st) : fa_launch<32, 32, 1, F16>(d, st);
     case 48: return two ? fa_launch<48, 48, 2, F16>(d, st) : fa_launch<48, 48, 1, F16>(d, st);
     case 64: return two ? fa_launch<64, 64, 2, F16>(d, st) : fa_launch<64, 64, 1, F16>(d, st);
     case 80: return two ? fa_launch<80, 80, 2, F16>(d, st) : fa_launch<80, 80, 1, F16>(d, st);
     case 128: return two ? fa_launch<128, 128, 2, F16>(d, st) : fa_launch<128, 128, 1, F16>(d, st);
     case 160: return fa_launch<160, 160, 1, F16>(d, st);
-    default: *handled = false; return MT_OK;
+    default: return fail(MT_ERR_UNSUPPORTED, "sdpa: no tcgen05 kernel for padded head dim %lld", (long long)Dp);
   }
 }
 
 int run_sdpa_tc(const mt_sdpa_desc& d, void*, size_t, cudaStream_t st, bool* handled) {
-  *handled = false;
-  if (d.dtype != MT_BF16 && d.dtype != MT_F16) return MT_OK;
-  if (d.mask_kind != 0) return MT_OK;
-  if (d.D != d.Dv || d.D % 8 != 0) return MT_OK;
-  if (d.Sq > INT32_MAX || d.Sk > INT32_MAX || d.B * d.H > 65535) return MT_OK;
-  if (!aligned16p(d.q) || !aligned16p(d.k) || !aligned16p(d.v)) return MT_OK;
-  for (int i = 0; i < 3; ++i)
-    if ((d.q_strides[i] * 2) % 16 || (d.k_strides[i] * 2) % 16 || (d.v_strides[i] * 2) % 16) return MT_OK;
-  if (d.q_strides[3] != 1 || d.k_strides[3] != 1 || d.v_strides[3] != 1) return MT_OK;
-  const int64_t Dp = (d.D + 15) / 16 * 16;
-  return d.dtype == MT_F16 ? fa_dispatch<true>(d, Dp, st, handled) : fa_dispatch<false>(d, Dp, st, handled);
+  const int path = sdpa_tc_path(d);
+  *handled = path != MT_SDPA_PATH_SIMT;
+  if (!*handled) return MT_OK;
+  const int64_t Dp = tc_head_pad(d.D);
+  const bool lazy = path == MT_SDPA_PATH_TC_LAZY;
+  return d.dtype == MT_F16 ? fa_dispatch<true>(d, Dp, lazy, st) : fa_dispatch<false>(d, Dp, lazy, st);
 }
 
 }  // namespace mt

@@ -144,6 +144,10 @@ int mt_cuda_device_status(int clear) {
   return MT_OK;
 }
 
+int mt_cuda_selftest_wait_timeout(long long budget_cycles, void* stream) {
+  return run_wait_timeout_selftest(budget_cycles, S(stream));
+}
+
 uint64_t mt_cuda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int mt_cuda_memcpy(void* dst, const void* src, size_t bytes, int kind, void* stream) {
@@ -287,6 +291,11 @@ int mt_cuda_conv2d_up2x_pack_weight(void* w_packed, void* w_lo, const void* w, i
   if (!w_packed && !w_lo) return fail(MT_ERR_INVALID, "conv2d_up2x pack: no output");
   return launch_conv_up2x_pack_weight(w_packed, (float*)w_lo, w, dtype, K, C, conv_packed_channels(C, 2, 2, dtype),
                                       S(stream));
+}
+
+int mt_cuda_sdpa_path(const mt_sdpa_desc* desc) {
+  if (!desc || validate_sdpa_desc(*desc) != MT_OK) return 0;
+  return sdpa_tc_path(*desc);
 }
 
 size_t mt_cuda_sdpa_workspace_size(const mt_sdpa_desc* desc) { return desc ? sdpa_workspace(*desc) : 0; }

@@ -136,16 +136,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Waits until the phase with the given parity has completed.  Gives up after
-// kWaitBudgetCycles or when another role raised `abort_flag`, records `site` in the device error
-// word (first timeout only), raises the abort flag and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site, volatile int* abort_flag) {
+// `budget` cycles (kWaitBudgetCycles, about 2 s, unless a caller passes less) or when another role
+// raised `abort_flag`, records `site` in the device error word (first timeout only), raises the
+// abort flag and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site, volatile int* abort_flag,
+                                          long long budget = kWaitBudgetCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - start > kWaitBudgetCycles) {
+    if (clock64() - start > budget) {
       report_device_error(site);
       *abort_flag = 1;
       return false;

@@ -1379,4 +1379,31 @@ int run_conv2d_up2x(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStr
   return MT_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Failure-detection self test: one thread waits, through the same bounded mbar_wait every kernel
+// of this library uses, on an mbarrier that nothing ever arrives on.  The wait gives up after
+// `budget_cycles`, records MT_ERR_TIMEOUT (site kSiteSelftest) in this unit's device status word
+// and the kernel returns; the context stays usable.
+constexpr int kSiteSelftest = 99;
+
+__global__ void wait_timeout_selftest_kernel(long long budget_cycles) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, kSiteSelftest, &abort_flag, budget_cycles);
+}
+
+int run_wait_timeout_selftest(long long budget_cycles, cudaStream_t st) {
+  if (budget_cycles < 0 || budget_cycles > kWaitBudgetCycles)
+    return fail(MT_ERR_INVALID, "wait self test: budget %lld cycles outside [0, %lld]", budget_cycles,
+                kWaitBudgetCycles);
+  wait_timeout_selftest_kernel<<<1, 32, 0, st>>>(budget_cycles);
+  return check_launch("wait_timeout_selftest_kernel");
+}
+
 }  // namespace mt

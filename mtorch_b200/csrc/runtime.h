@@ -94,9 +94,12 @@ int64_t conv_packed_channels(int64_t C, int64_t R, int64_t S, int dtype);
 // attention.cu
 size_t sdpa_workspace(const mt_sdpa_desc& d);
 int run_sdpa(const mt_sdpa_desc& d, void* ws, size_t ws_bytes, cudaStream_t st);
+int validate_sdpa_desc(const mt_sdpa_desc& d);
+int sdpa_tc_path(const mt_sdpa_desc& d);
 
 // Per-translation-unit device status readers (see g_device_error).
 int read_status_gemm(int clear);
+int run_wait_timeout_selftest(long long budget_cycles, cudaStream_t st);
 int read_status_attention(int clear);
 #define MT_STATUS_READER(name)                                                   \
   int name(int clear) {                                                          \

@@ -351,29 +351,11 @@ def pack_conv_up2x_weight(w: Tensor):
 # attention (tensor.cpp:30930-31324)
 
 
-def scaled_dot_product_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None = None, dropout_p=0.0,
-                                 is_causal=False, scale=None, enable_gqa=False, *, out: Tensor | None = None) -> Tensor:
-    """`scaled_dot_product_attention` (tensor.cpp:30930-31324).  `out` (optional) may be any
-    strided view of the right shape, e.g. a heads-merged [B, S, H, D] buffer seen as
-    [B, H, S, D], so the next projection reads it without a copy."""
-    _require_cuda(q, k, v, attn_mask)
-    if q.dtype is not k.dtype or q.dtype is not v.dtype:
-        raise ValueError("scaled_dot_product_attention query, key, and value must have the same dtype")
-    if not (0.0 <= dropout_p <= 1.0):
-        raise ValueError("scaled_dot_product_attention dropout_p must be between 0 and 1")
-    if dropout_p not in (0.0, 1.0):
-        raise ValueError("scaled_dot_product_attention dropout_p is only supported when it is 0 or 1")
-    if q.dim() < 2:
-        raise ValueError("scaled_dot_product_attention expects query with at least 2 dims")
+def _sdpa_desc(q, k, v, out, attn_mask, is_causal, scale, enable_gqa):
+    """The mt_sdpa_desc of an SDPA call (shapes already checked by the caller)."""
     lead = q._shape[:-2]
     Lq, E = q._shape[-2], q._shape[-1]
     Sk, Ev = k._shape[-2], v._shape[-1]
-    if out is None:
-        out = _new(lead + (Lq, Ev), q.dtype, q.device)
-    elif tuple(out.shape) != lead + (Lq, Ev):
-        raise RuntimeError(f"sdpa: out has shape {tuple(out.shape)}, expected {lead + (Lq, Ev)}")
-    if dropout_p == 1.0:
-        return out.zero_()
 
     def as4(t):
         if t.dim() == 4:
@@ -416,6 +398,48 @@ def scaled_dot_product_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Ten
         d.mask_strides[:] = list(me._strides)
     d.causal = 1 if is_causal else 0
     d.scale = float(scale) if scale is not None else 1.0 / math.sqrt(E)
+    return d
+
+
+def sdpa_path(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None = None, is_causal=False, scale=None,
+              enable_gqa=False) -> str:
+    """Which device kernel scaled_dot_product_attention runs for these arguments: "tc_lazy" (the
+    tcgen05 kernel with the output in TMEM), "tc" (the general tcgen05 kernel) or "simt" (the fp32
+    SIMT kernel).  Nothing is launched."""
+    _require_cuda(q, k, v, attn_mask)
+    out = _new(q._shape[:-2] + (q._shape[-2], v._shape[-1]), q.dtype, q.device)
+    d = _sdpa_desc(q, k, v, out, attn_mask, is_causal, scale, enable_gqa)
+    code = _lib().mt_cuda_sdpa_path(C.byref(d))
+    if code == 0:
+        raise ValueError("sdpa_path: invalid arguments")
+    return {L.SDPA_PATH_TC_LAZY: "tc_lazy", L.SDPA_PATH_TC: "tc", L.SDPA_PATH_SIMT: "simt"}[code]
+
+
+def scaled_dot_product_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None = None, dropout_p=0.0,
+                                 is_causal=False, scale=None, enable_gqa=False, *, out: Tensor | None = None) -> Tensor:
+    """`scaled_dot_product_attention` (tensor.cpp:30930-31324).  `out` (optional) may be any
+    strided view of the right shape, e.g. a heads-merged [B, S, H, D] buffer seen as
+    [B, H, S, D], so the next projection reads it without a copy."""
+    _require_cuda(q, k, v, attn_mask)
+    if q.dtype is not k.dtype or q.dtype is not v.dtype:
+        raise ValueError("scaled_dot_product_attention query, key, and value must have the same dtype")
+    if not (0.0 <= dropout_p <= 1.0):
+        raise ValueError("scaled_dot_product_attention dropout_p must be between 0 and 1")
+    if dropout_p not in (0.0, 1.0):
+        raise ValueError("scaled_dot_product_attention dropout_p is only supported when it is 0 or 1")
+    if q.dim() < 2:
+        raise ValueError("scaled_dot_product_attention expects query with at least 2 dims")
+    lead = q._shape[:-2]
+    Lq, E = q._shape[-2], q._shape[-1]
+    Sk, Ev = k._shape[-2], v._shape[-1]
+    if out is None:
+        out = _new(lead + (Lq, Ev), q.dtype, q.device)
+    elif tuple(out.shape) != lead + (Lq, Ev):
+        raise RuntimeError(f"sdpa: out has shape {tuple(out.shape)}, expected {lead + (Lq, Ev)}")
+    if dropout_p == 1.0:
+        return out.zero_()
+
+    d = _sdpa_desc(q, k, v, out, attn_mask, is_causal, scale, enable_gqa)
     lib = _lib()
     need = lib.mt_cuda_sdpa_workspace_size(C.byref(d))
     ws, wsb = workspace(need, q._idx())

@@ -70,6 +70,19 @@ def addmm_f32(inp, A, B, beta=1.0, alpha=1.0):
     return out
 
 
+def baddbmm_f32(inp, A, B, beta=1.0, alpha=1.0):
+    """A [b, M, K] @ B [b, K, N], input broadcast to [b, M, N]."""
+    A, B = _f(A), _f(B)
+    nb, M, K = A.shape
+    N = B.shape[2]
+    inp = _f(np.broadcast_to(inp, (nb, M, N)))
+    out = np.empty((nb, M, N), np.float32)
+    for k in range(nb):
+        _lib().oracle_baddbmm_f32(_p(inp[k]), _p(_f(A[k])), _p(_f(B[k])), _p(out[k]), I(M), I(K), I(N),
+                                  C.c_double(beta), C.c_double(alpha))
+    return out
+
+
 def linear_f32(X, W, b=None):
     X, W = _f(X), _f(W)
     lead = X.shape[:-1]

@@ -46,6 +46,10 @@ mtorch.manual_seed(3)
 i, a, b = mtorch.randn(16, 12), mtorch.randn(16, 40), mtorch.randn(40, 12)
 rec("addmm", i=i, a=a, b=b, y=mtorch.addmm(i, a, b, beta=0.5, alpha=2.0))
 
+mtorch.manual_seed(40)
+i, a, b = mtorch.randn(3, 1, 14), mtorch.randn(3, 18, 33), mtorch.randn(3, 33, 14)
+rec("baddbmm", i=i, a=a, b=b, y=mtorch.baddbmm(i, a, b, beta=-0.75, alpha=1.5))
+
 mtorch.manual_seed(4)
 x, w, bias = mtorch.randn(3, 17, 40), mtorch.randn(24, 40), mtorch.randn(24)
 rec("linear", x=x, w=w, b=bias, y=F.linear(x, w, bias))

@@ -215,6 +215,21 @@ def test_linear_bf16_fused_epilogues():
     check(got32, oracle.gelu_f32(oracle.linear_f32(x, ws)), FP32_RTOL)
 
 
+def test_baddbmm_fp32_golden(golden):
+    """`baddbmm` (tensor.cpp:25557-25694): beta * input (broadcast over rows) + alpha * bmm, the
+    reference's own output."""
+    i, a, b = (cu(golden[f"baddbmm.{n}"]) for n in "iab")
+    check(mt.baddbmm(i, a, b, beta=-0.75, alpha=1.5).numpy(), golden["baddbmm.y"], FP32_RTOL)
+
+
+@pytest.mark.parametrize("B,M,K,N", [(16, 256, 40, 256), (4, 77, 64, 130)])
+def test_baddbmm_bf16(B, M, K, N):
+    i, a, b = rnd(B, M, N, seed=3), rnd(B, M, K, seed=4), rnd(B, K, N, seed=5)
+    ref = oracle.baddbmm_f32(bf16_round(i), bf16_round(a), bf16_round(b), 0.5, 0.25)
+    got = mt.baddbmm(cu(i, "bfloat16"), cu(a, "bfloat16"), cu(b, "bfloat16"), beta=0.5, alpha=0.25).numpy()
+    check(got, ref, BF16_RTOL)
+
+
 def test_bmm_bf16_attention_shapes():
     a, b = rnd(16, 256, 40), rnd(16, 40, 256, seed=1)
     ref = np.stack([oracle.matmul_f32(bf16_round(a[i]), bf16_round(b[i])) for i in range(16)])
@@ -421,3 +436,39 @@ def test_sdpa_fp32_strided_heads():
     xs = x.reshape(B, S, 3, H, D).transpose(2, 0, 3, 1, 4)
     ref = oracle.sdpa_f32(xs[0], xs[1], xs[2])
     check(mt.scaled_dot_product_attention(q, k, v).numpy(), ref, FP32_RTOL)
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk,D", [(2, 2, 256, 256, 32), (2, 4, 100, 77, 32), (1, 2, 300, 129, 16),
+                                         (1, 2, 200, 200, 96), (1, 2, 130, 300, 144), (1, 3, 260, 100, 24)])
+def test_sdpa_bf16_padded_head_dims(B, H, Sq, Sk, D):
+    """Head dims without their own kernel run on the next wider tcgen05 kernel (32, 128, 160), the
+    extra columns zero-filled by TMA."""
+    q, k, v = rnd(B, H, Sq, D), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
+    qd, kd, vd = cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")
+    assert mt.ops.sdpa_path(qd, kd, vd) == "tc"
+    ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
+    check(mt.scaled_dot_product_attention(qd, kd, vd).numpy(), ref, BF16_RTOL)
+
+
+def test_sdpa_path_of_unet_shapes():
+    """The attention shapes of the SD-1.5 UNet (strided head views of the fused projections) run on
+    the tensor-core kernels; fp32 and masked calls report the SIMT kernel."""
+    def heads(t, n, s, h, d):
+        p = t.stride(0)
+        return t._view((n, h, s, d), (s * p, d, p, 1))
+
+    n = 2
+    for c, s in ((320, 4096), (640, 1024), (1280, 256), (1280, 64)):
+        d = c // 8
+        qkv = mt.empty(n * s, 3 * c, dtype="bfloat16", device="cuda")
+        q, k, v = (heads(qkv[:, i * c:(i + 1) * c], n, s, 8, d) for i in range(3))
+        want = "tc_lazy" if d <= 48 and s > 128 else "tc"
+        assert mt.ops.sdpa_path(q, k, v) == want, (c, s)
+        kv = mt.empty(n * 77, 2 * c, dtype="bfloat16", device="cuda")
+        kc, vc = heads(kv[:, 0:c], n, 77, 8, d), heads(kv[:, c:2 * c], n, 77, 8, d)
+        assert mt.ops.sdpa_path(q, kc, vc) == want, (c, s, "cross")
+    q = mt.empty(1, 2, 64, 40, device="cuda")
+    assert mt.ops.sdpa_path(q, q, q) == "simt"
+    qb = q.to("bfloat16")
+    mask = mt.zeros(64, 64, device="cuda")
+    assert mt.ops.sdpa_path(qb, qb, qb, attn_mask=mask) == "simt"

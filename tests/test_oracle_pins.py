@@ -24,6 +24,11 @@ def test_addmm(golden):
           1e-6, 1e-6)
 
 
+def test_baddbmm(golden):
+    i, a, b = golden["baddbmm.i"], golden["baddbmm.a"], golden["baddbmm.b"]
+    close(oracle.baddbmm_f32(i, a, b, -0.75, 1.5), golden["baddbmm.y"], 0, 0)
+
+
 def test_linear(golden):
     close(oracle.linear_f32(golden["linear.x"], golden["linear.w"], golden["linear.b"]), golden["linear.y"], 0, 0)
 
@@ -78,3 +83,28 @@ def test_reference_live_if_built():
     x, w, b = m.randn(1, 5, 6, 6), m.randn(7, 5, 3, 3), m.randn(7)
     y = m.nn.functional.conv2d(x, w, b, padding=1).numpy()
     close(oracle.conv2d_f32(x.numpy(), w.numpy(), b.numpy(), 1, 1), y, 0, 0)
+
+
+def test_oracle_unet_matches_reference_unet():
+    """The whole-UNet oracle composition (oracle/unet.py over the C restatement), with parameters
+    and inputs from mtorch_b200's host generator, reproduces the reference's own UNet forward and
+    DDIM step (tests/golden/reference_unet.npz) bit for bit."""
+    from pathlib import Path
+
+    import mtorch_b200 as mt
+    from oracle import unet as OU
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "reference_unet.npz")
+    cfg = OU.GOLDEN_CFG
+    mt.manual_seed(cfg["param_seed"])
+    P = OU.make_params(cfg, lambda s: mt.randn(*s).numpy(), OU.NumpyOps)
+    assert [n for n, _ in OU.param_spec(cfg)] == list(g["param_names"])
+    ck = np.array([float(np.abs(P[n]).astype(np.float64).sum()) for n in g["param_names"]])
+    np.testing.assert_array_equal(ck, g["param_checksum"])
+    mt.manual_seed(cfg["input_seed"])
+    x, ctx, temb = OU.make_inputs(cfg, lambda s: mt.randn(*s).numpy())
+    for k, v in (("x", x), ("ctx", ctx), ("temb", temb)):
+        np.testing.assert_array_equal(v, g[k])
+    eps = OU.unet_forward(P, x, temb, ctx, cfg, OU.NumpyOps)
+    np.testing.assert_array_equal(eps, g["eps"])
+    np.testing.assert_array_equal(OU.ddim_step(x, eps, cfg["timestep"], OU.NumpyOps), g["x_next"])

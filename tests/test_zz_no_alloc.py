@@ -25,10 +25,16 @@ pytestmark = pytest.mark.gpu
 RTOL = {"float32": 1e-4, "bfloat16": 2e-2}
 
 
-def _reference(x, G, w, b, silu):
+def _out(x, out_cl):
+    N, C, H, W = x.shape
+    fmt = mt.channels_last if out_cl else mt.contiguous_format
+    return mt.empty(N, C, H, W, dtype=x.dtype, device="cuda", memory_format=fmt)
+
+
+def _reference(x, G, w, b, silu, out_cl=True):
     lib = _lib.lib()
     N, C, H, W = x.shape
-    out = mt.empty(N, C, H, W, dtype=x.dtype, device="cuda", memory_format=mt.channels_last)
+    out = _out(x, out_cl)
     need = lib.mt_cuda_group_norm_workspace_size(N, C, H * W, G)
     ws, wsb = workspace(need, 0)
     xs = (x.stride(0), x.stride(1), x.stride(3))
@@ -39,10 +45,10 @@ def _reference(x, G, w, b, silu):
     return out
 
 
-def _no_alloc(x, G, w, b, silu):
+def _no_alloc(x, G, w, b, silu, out_cl=True):
     lib = _lib.lib()
     N, C, H, W = x.shape
-    out = mt.empty(N, C, H, W, dtype=x.dtype, device="cuda", memory_format=mt.channels_last)
+    out = _out(x, out_cl)
     xs = (x.stride(0), x.stride(1), x.stride(3))
     ys = (out.stride(0), out.stride(1), out.stride(3))
     rc = lib.mt_cuda_group_norm_noalloc(out.data_ptr(), out.dtype.code, _lib.arr64(ys), x.data_ptr(), x.dtype.code,
@@ -64,6 +70,25 @@ def test_no_alloc_group_norm_matches_workspace_version_twice(dtype):
         silu = call % 2
         want = _reference(x, G, w, b, silu).numpy()
         got = _no_alloc(x, G, w, b, silu).numpy()
+        np.testing.assert_allclose(got, want, rtol=RTOL[dtype], atol=RTOL[dtype] * np.abs(want).max())
+
+
+@pytest.mark.parametrize("dtype,in_cl,out_cl", [("float32", False, False), ("bfloat16", True, False),
+                                                ("bfloat16", False, True)])
+def test_no_alloc_group_norm_other_layouts_twice(dtype, in_cl, out_cl):
+    """NCHW input (the per-channel-plane statistics pass) and NCHW output (the generic apply pass)
+    through the fixed scratch, two calls in a row on different data."""
+    rng = np.random.default_rng(12)
+    G = 32
+    for call, shape in enumerate([(3, 64, 20, 12), (2, 320, 16, 16)]):
+        x = mt.tensor(rng.standard_normal(shape).astype(np.float32) * (2 - call) - call, dtype=dtype).cuda()
+        if in_cl:
+            x = x.contiguous(memory_format=mt.channels_last)
+        w = mt.tensor(rng.standard_normal(shape[1]).astype(np.float32)).cuda()
+        b = mt.tensor(rng.standard_normal(shape[1]).astype(np.float32)).cuda()
+        silu = 1 - call % 2
+        want = _reference(x, G, w, b, silu, out_cl).numpy()
+        got = _no_alloc(x, G, w, b, silu, out_cl).numpy()
         np.testing.assert_allclose(got, want, rtol=RTOL[dtype], atol=RTOL[dtype] * np.abs(want).max())
 
 
