@@ -201,7 +201,8 @@ def run_ours(args):
     dist = None
     if world > 1:
         dist = parallel.init("nccl", device_id=torch.device(f"cuda:{local}"))
-    lo, hi = parallel.shard(BATCH, world, rank)
+    gb = args.global_batch
+    lo, hi = parallel.shard(gb, world, rank)
     nb = hi - lo
     dev = f"cuda:{local}"
     out_dir = ROOT / "gpurun_out"
@@ -211,8 +212,8 @@ def run_ours(args):
     mt.manual_seed(0)
     unet = UNet(device=dev, dtype="bfloat16")
     mt.manual_seed(1)
-    lat_all = mt.randn(BATCH, 4, H, W)
-    ctx_all = mt.randn(BATCH, CTX, 768)
+    lat_all = mt.randn(gb, 4, H, W)
+    ctx_all = mt.randn(gb, CTX, 768)
     lat_h = lat_all[lo:hi].to("bfloat16")
     ctx_h = ctx_all[lo:hi].to("bfloat16")
     sched = DDIM(steps=50)
@@ -350,7 +351,7 @@ def run_ours(args):
             del graphed
             x64 = lat_all.to("bfloat16").to(dev)
             ctx64 = ctx_all.to("bfloat16").to(dev)
-            temb64 = [mt.tensor(timestep_embedding(np.full(BATCH, float(t))), dtype="bfloat16", device=dev)
+            temb64 = [mt.tensor(timestep_embedding(np.full(gb, float(t))), dtype="bfloat16", device=dev)
                       for t in sched.timesteps]
             g64 = Graphed(unet, x64, temb64[0], ctx64) if use_graph else None
             for i in range(args.warmup + args.steps):
@@ -374,7 +375,7 @@ def run_ours(args):
             roofline["exp_unit"] = {"achieved": exp_rate, "peak": exp_peak, "unit": "exp2/s",
                                     "frac": exp_rate / exp_peak, "sm_mhz": mhz}
         base = None
-        if world == 1:  # the reference CPU path on this box's host cores, bounded sample
+        if world == 1 and gb == BATCH:  # the reference CPU path on this box's host cores, bounded sample
             try:
                 procs = os.cpu_count() or 1
                 times, smp = cpu_sampled_steps(procs, 1, 2)
@@ -384,9 +385,9 @@ def run_ours(args):
         line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents/context, random-init "
-                "weights)", "config": {"workload": "C5: SD-1.5 UNet bf16, batch 64 latents [64,4,64,64], context "
-                "[64,77,768], 1 UNet eval + DDIM update per step", "model": "SD-1.5-shaped UNet (859.5M params)",
-                "global_batch": BATCH, "seq_len": H * W, "parallelism": f"batch-shard dp{world} + NCCL all-gather",
+                "weights)", "config": {"workload": f"C5: SD-1.5 UNet bf16, batch {gb} latents [{gb},4,64,64], "
+                f"context [{gb},77,768], 1 UNet eval + DDIM update per step", "model": "SD-1.5-shaped UNet (859.5M params)",
+                "global_batch": gb, "seq_len": H * W, "parallelism": f"batch-shard dp{world} + NCCL all-gather",
                 "l2": "activations > L2 (126 MB) at batch 64/GPU; no flush"},
                 "gpu_launches": int(launches), "e2e": e2e, "roofline": roofline, "roofline_conv": roofline_conv,
                 "cpu_baseline": base, "bitwise_equal_to_1gpu": bitwise,
@@ -449,7 +450,9 @@ def run_workload(args):
                doubled batch, device timestep embedding and the fused guidance + DDIM kernel, one
                CUDA graph per step; unit = denoise steps/s of the whole batch
       vae      SD-1.5 VAE decode of `batch` latents 64x64 -> 512x512 images; unit = images/s
-      text     SD-1.5 CLIP text encoder on `batch` sequences of 77 tokens; unit = sequences/s"""
+      text     SD-1.5 CLIP text encoder on `batch` sequences of 77 tokens; unit = sequences/s
+      c4       BASELINE config C4: the fp32 UNet on one latent, one UNet eval + DDIM update (CUDA
+               graph); unit = steps/s, beside the reference CPU path on the same per-sample work"""
     import torch
 
     import mtorch_b200 as mt
@@ -457,7 +460,29 @@ def run_workload(args):
     stream = torch.cuda.current_stream()
     nb = args.batch
     mt.manual_seed(0)
-    if args.workload == "sampler":
+    base = None
+    if args.workload == "c4":
+        from mtorch_b200.graphs import Graphed
+        from mtorch_b200.unet import DDIM, UNet, timestep_embedding, unet_flops_per_sample
+
+        nb = 1
+        unet = UNet(device="cuda", dtype="float32")
+        mt.manual_seed(1)
+        lat = mt.randn(1, 4, H, W).cuda()
+        ctx = mt.randn(1, CTX, 768).cuda()
+        temb = mt.tensor(timestep_embedding(np.array([999.0]))).cuda()
+        sched = DDIM(steps=50)
+        g = Graphed(unet, lat, temb, ctx)
+        fn = lambda: sched.step(lat, g(lat, temb, ctx), 999)  # noqa: E731
+        flops, unit = unet_flops_per_sample(), "steps/s"
+        name = "C4: SD-1.5 UNet fp32 (3xTF32 GEMM/conv, fp32 SIMT attention), batch 1, one UNet eval + DDIM update"
+        if not args.no_cpu_baseline:
+            procs = os.cpu_count() or 1
+            times, smp = cpu_sampled_steps(procs, 1, 2)
+            base = cpu_result(times, smp, procs)
+            base["value"] *= BATCH  # one sample per C4 step
+            base["sample"] += "; C4 step = R sampled steps"
+    elif args.workload == "sampler":
         from mtorch_b200.unet import DDIM, Sampler, UNet, unet_flops_per_sample
 
         unet = UNet(device="cuda", dtype="bfloat16")
@@ -497,10 +522,16 @@ def run_workload(args):
     ms = e0.elapsed_time(e1) / args.steps
     _, tf_burst, tf_sust, kind = peaks()
     tflops = flops / (ms * 1e-3) / 1e12
-    per = 1 if args.workload == "sampler" else nb
-    print(json.dumps({"workload": name, "value": 1000.0 * per / ms, "unit": unit, "ms_per_run": ms,
-                      "batch": nb, "dtype": "bf16", "data": "synthetic, random-init weights", "tflops": tflops,
-                      "frac_of_bf16_peak": tflops / tf_burst, "peak_kind": f"{kind} bf16 burst"}))
+    per = 1 if args.workload in ("sampler", "c4") else nb
+    line = {"workload": name, "value": 1000.0 * per / ms, "unit": unit, "ms_per_run": ms, "batch": nb,
+            "dtype": "f32" if args.workload == "c4" else "bf16", "data": "synthetic, random-init weights",
+            "tflops": tflops, "frac_of_bf16_peak": tflops / tf_burst, "peak_kind": f"{kind} bf16 burst"}
+    if args.workload == "c4":
+        line["note"] = ("fp32 throughput is bounded by 3xTF32 (three tf32 MMAs per product) and fp32 SIMT attention; "
+                        "frac is against the bf16 peak for reference only")
+    if base is not None:
+        line["cpu_baseline"] = base
+    print(json.dumps(line))
 
 
 def main():
@@ -513,7 +544,10 @@ def main():
     ap.add_argument("--kernel", choices=["conv", "attn", "geglu"], default=None,
                     help="time one hot kernel alone at its UNet shape (for profiling), not the UNet")
     ap.add_argument("--batch", type=int, default=BATCH, help="samples for --kernel / --workload runs")
-    ap.add_argument("--workload", choices=["sampler", "vae", "text"], default=None,
+    ap.add_argument("--global-batch", type=int, default=BATCH,
+                    help="UNet bench: samples of the whole job (64 = config C5; smaller for profiling)")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the reference CPU timing of --workload c4")
+    ap.add_argument("--workload", choices=["sampler", "vae", "text", "c4"], default=None,
                     help="time one of the workloads around the UNet instead of the UNet step")
     args = ap.parse_args()
     if args.workload:

@@ -114,3 +114,45 @@ def test_fp16_device_path():
     q, k, v = (rng.standard_normal((2, 4, 200, 40)).astype(np.float32) for _ in range(3))
     got = mt.scaled_dot_product_attention(*(mt.tensor(t, dtype="float16").cuda() for t in (q, k, v))).float().numpy()
     check(got, oracle.sdpa_f32(_f16(q), _f16(k), _f16(v)), BF16_RTOL)
+
+
+F16_RTOL = 5e-3  # fp16 keeps 11 significant bits: one output rounding is 2^-11 relative
+
+
+@pytest.mark.parametrize("cl", [False, True])
+def test_fp16_group_norm_silu(cl):
+    """GroupNorm (+ fused SiLU) in fp16, NCHW and channels-last: the reference's own SD dtype
+    (its channels-last fp16 fast path is tensor.cpp:18683-18791)."""
+    rng = np.random.default_rng(8)
+    x = (rng.standard_normal((2, 320, 16, 16)) * 2 + 0.5).astype(np.float32)
+    w, b = rng.standard_normal(320).astype(np.float32), rng.standard_normal(320).astype(np.float32)
+    xd = mt.tensor(x, dtype="float16").cuda()
+    if cl:
+        xd = xd.contiguous(memory_format=mt.channels_last)
+    wd, bd = mt.tensor(w, dtype="float16").cuda(), mt.tensor(b, dtype="float16").cuda()
+    ref = oracle.group_norm_f32(_f16(x), 32, _f16(w), _f16(b))
+    check(mt.group_norm(xd, 32, wd, bd).float().numpy(), ref, F16_RTOL)
+    check(mt.group_norm(xd, 32, wd, bd, fuse_silu=True).float().numpy(), oracle.silu_f32(ref), F16_RTOL)
+
+
+@pytest.mark.parametrize("cols", [320, 640, 1280, 77])
+def test_fp16_layer_norm_softmax(cols):
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal((300, cols)) * 3).astype(np.float32)
+    w, b = rng.standard_normal(cols).astype(np.float32), rng.standard_normal(cols).astype(np.float32)
+    xd = mt.tensor(x, dtype="float16").cuda()
+    got = mt.layer_norm(xd, (cols,), mt.tensor(w, dtype="float16").cuda(), mt.tensor(b, dtype="float16").cuda())
+    check(got.float().numpy(), oracle.layer_norm_f32(_f16(x), _f16(w), _f16(b)), F16_RTOL)
+    check(mt.softmax(xd, -1).float().numpy(), oracle.softmax_f32(_f16(x)), F16_RTOL)
+
+
+def test_fp16_pointwise():
+    rng = np.random.default_rng(10)
+    x = (rng.standard_normal((4, 320, 8, 8)) * 3).astype(np.float32)
+    y = rng.standard_normal((1, 320, 1, 1)).astype(np.float32)
+    xd, yd = mt.tensor(x, dtype="float16").cuda(), mt.tensor(y, dtype="float16").cuda()
+    check(mt.silu(xd).float().numpy(), oracle.silu_f32(_f16(x)), F16_RTOL)
+    check(mt.gelu(xd).float().numpy(), oracle.gelu_f32(_f16(x)), F16_RTOL)
+    check(mt.gelu(xd, approximate="tanh").float().numpy(), oracle.gelu_f32(_f16(x), "tanh"), F16_RTOL)
+    check((xd + yd).float().numpy(), _f16(x) + _f16(y), F16_RTOL)
+    check((xd * yd).float().numpy(), _f16(x) * _f16(y), F16_RTOL)

@@ -3,8 +3,9 @@ head dims 40 and 80) plus one DDIM step, against
 
 * fp32: the REFERENCE mtorch's own output for the same parameters and inputs
   (tests/golden/reference_unet.npz, made by tests/golden/make_golden_unet.py), rtol 1e-4;
-* bf16: the oracle composition (oracle/unet.py, bit-identical to the reference golden in fp32, see
-  test_oracle_pins.py) evaluated in fp32 on the same bf16-rounded parameters and inputs, rtol 2e-2.
+* bf16 and fp16: the oracle composition (oracle/unet.py, bit-identical to the reference golden in
+  fp32, see test_oracle_pins.py) evaluated in fp32 on the same rounded parameters and inputs,
+  rtol 2e-2.
 
 Parameters are drawn from mtorch's seeded generator in the reference's draw order, so the module
 holds exactly the values the reference used.  Errors are measured against the output's scale
@@ -77,14 +78,16 @@ def test_unet_fp32_matches_reference(golden):
     check("fp32 x_next", x_next, golden["x_next"], 1e-4)
 
 
-def test_unet_bf16_matches_oracle(golden):
-    net, P = build_unet("bfloat16")
-    rb = lambda a: mt.tensor(np.asarray(a, np.float32)).to("bfloat16").float().numpy()  # noqa: E731
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_unet_16bit_matches_oracle(golden, dtype):
+    """bf16 (the bench's dtype) and fp16 (the reference's own SD dtype) device UNets."""
+    net, P = build_unet(dtype)
+    rb = lambda a: mt.tensor(np.asarray(a, np.float32)).to(dtype).float().numpy()  # noqa: E731
     Pb = {k: rb(v) for k, v in P.items()}
     x, ctx, temb = rb(golden["x"]), rb(golden["ctx"]), rb(golden["temb"])
     ref_eps = OU.unet_forward(Pb, x, temb, ctx, CFG, OU.NumpyOps)
     ref_next = OU.ddim_step(x, ref_eps, CFG["timestep"], OU.NumpyOps)
-    eps, x_next = run_device(net, x, temb, ctx, "bfloat16")
-    check("bf16 eps", eps, ref_eps, 2e-2)
-    check("bf16 x_next", x_next, ref_next, 2e-2)
+    eps, x_next = run_device(net, x, temb, ctx, dtype)
+    check(f"{dtype} eps", eps, ref_eps, 2e-2)
+    check(f"{dtype} x_next", x_next, ref_next, 2e-2)
 
