@@ -343,6 +343,23 @@ def run_ours(args):
                      "frac": conv_ach / tf_burst, "peak_kind": f"{peak_kind} bf16 burst",
                      "traffic": DRAM_BYTES_PER_SAMPLE["conv"] * nb, "ms_per_launch": conv_ms}
 
+    # memory-bound kernels of the step at the 64x64 level (activation [nb*4096, 320] bf16, > L2 at
+    # nb = 64): GroupNorm + SiLU and LayerNorm, one read and one write of the activation each
+    xg = mt.empty(nb, 320, H, W, dtype="bfloat16", device=dev).uniform_(-1, 1).contiguous(
+        memory_format=mt.channels_last)
+    gn = unet.down[0].norm1
+    ln = unet.down[1].block.norm1
+    act_bytes = 2.0 * nb * H * W * 320 * 2
+    gn_ms = timed(lambda: gn(xg, fuse_silu=True))
+    ln_ms = timed(lambda: ln(xg.permute(0, 2, 3, 1).reshape(nb * H * W, 320)))
+    del xg
+    roofline_hbm = {"bound": "hbm", "unit": "GB/s", "peak": hbm, "peak_kind": f"{peak_kind} copy bandwidth",
+                    "algorithmic_bytes": act_bytes}
+    for key, kms, kname in (("group_norm_silu", gn_ms, "gn_partial + gn_finalize_table + gn_apply_img (L2-grouped)"),
+                            ("layer_norm", ln_ms, "layer_norm_bf16_sub_kernel")):
+        roofline_hbm[key] = {"kernel": kname, "ms_per_call": kms, "achieved": act_bytes / (kms * 1e-3) / 1e9,
+                             "frac": act_bytes / (kms * 1e-3) / 1e9 / hbm}
+
     # ---- N-GPU result vs a 1-GPU run of the whole batch (rank 0, untimed): the sharded latents
     # after W + K steps must equal, bit for bit, the same steps on all 64 samples on one GPU ----
     bitwise = None
@@ -390,6 +407,7 @@ def run_ours(args):
                 "global_batch": gb, "seq_len": H * W, "parallelism": f"batch-shard dp{world} + NCCL all-gather",
                 "l2": "activations > L2 (126 MB) at batch 64/GPU; no flush"},
                 "gpu_launches": int(launches), "e2e": e2e, "roofline": roofline, "roofline_conv": roofline_conv,
+                "roofline_hbm": roofline_hbm,
                 "cpu_baseline": base, "bitwise_equal_to_1gpu": bitwise,
                 "clocks": clk}
         print(json.dumps(line))
@@ -415,6 +433,20 @@ def run_kernel(args):
         fn = lambda: conv(x)  # noqa: E731
         flops = 2.0 * nb * H * W * 320 * 320 * 9
         name = "implicit-GEMM conv 3x3 320->320 at 64x64"
+    elif args.kernel in ("gn", "ln"):
+        x = mt.empty(nb, 320, H, W, dtype="bfloat16", device="cuda").uniform_(-1, 1).contiguous(
+            memory_format=mt.channels_last)
+        if args.kernel == "gn":
+            gn = mt.nn.GroupNorm(32, 320, device="cuda", dtype="bfloat16")
+            fn = lambda: gn(x, fuse_silu=True)  # noqa: E731
+            name = "GroupNorm(32) + SiLU, 320 channels at 64x64, channels-last"
+        else:
+            ln = mt.nn.LayerNorm(320, device="cuda", dtype="bfloat16")
+            t = x.permute(0, 2, 3, 1).reshape(nb * H * W, 320)
+            fn = lambda: ln(t)  # noqa: E731
+            name = "LayerNorm over 320 columns, 64x64 tokens"
+        flops = None
+        nbytes = 2.0 * nb * H * W * 320 * 2  # one read + one write of the activation
     elif args.kernel == "geglu":
         x = mt.empty(nb * H * W, 320, dtype="bfloat16", device="cuda").uniform_(-1, 1)
         w = mt.empty(2560, 320, dtype="bfloat16", device="cuda").uniform_(-0.05, 0.05)
@@ -436,7 +468,12 @@ def run_kernel(args):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    _, tf_burst, _, kind = peaks()
+    hbm, tf_burst, _, kind = peaks()
+    if flops is None:
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"kernel": name, "batch": nb, "ms_per_launch": ms, "GB/s": gbs, "frac_of_hbm": gbs / hbm,
+                          "algorithmic_bytes": nbytes, "peak_kind": kind}))
+        return
     tflops = flops / (ms * 1e-3) / 1e12
     print(json.dumps({"kernel": name, "batch": nb, "ms_per_launch": ms, "tflops": tflops,
                       "frac_of_bf16_peak": tflops / tf_burst, "peak_kind": kind}))
@@ -541,7 +578,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--eager", action="store_true", help="launch the UNet op by op instead of replaying a CUDA graph")
-    ap.add_argument("--kernel", choices=["conv", "attn", "geglu"], default=None,
+    ap.add_argument("--kernel", choices=["conv", "attn", "geglu", "gn", "ln"], default=None,
                     help="time one hot kernel alone at its UNet shape (for profiling), not the UNet")
     ap.add_argument("--batch", type=int, default=BATCH, help="samples for --kernel / --workload runs")
     ap.add_argument("--global-batch", type=int, default=BATCH,

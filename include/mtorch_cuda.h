@@ -152,6 +152,16 @@ int mt_cuda_group_norm(void* y, int y_dtype, const int64_t* y_strides, const voi
                        const int64_t* x_strides, const void* weight, const void* bias, int wb_dtype, int64_t N,
                        int64_t C, int64_t HW, int64_t groups, double eps, int fuse_silu, void* workspace,
                        size_t workspace_bytes, void* stream);
+/* Group norm of the channel concatenation [x1 | x2] without forming it (the SD up-block skip
+ * connection, `cat(dim=1)` tensor.cpp:32141 followed by `group_norm`): the result equals
+ * mt_cuda_group_norm on the concatenated [N, C, HW] input.  bf16 only; x1 ([N, C1, HW]) and x2
+ * ([N, C - C1, HW]) dense channels-last with C1 and C - C1 multiples of 8, y dense channels-last
+ * [N, C, HW]; other layouts return MT_ERR_UNSUPPORTED (concatenate and call mt_cuda_group_norm).
+ * Workspace: mt_cuda_group_norm_workspace_size(N, C, HW, groups). */
+int mt_cuda_group_norm_cat(void* y, int y_dtype, const int64_t* y_strides, const void* x1, const int64_t* x1_strides,
+                           int64_t C1, const void* x2, const int64_t* x2_strides, int x_dtype, const void* weight,
+                           const void* bias, int wb_dtype, int64_t N, int64_t C, int64_t HW, int64_t groups, double eps,
+                           int fuse_silu, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Group norm for callers that cannot hand the library a workspace — for example code running
  * inside a host callback, a custom allocator hook, or an embedding runtime that owns every
@@ -237,6 +247,16 @@ typedef struct {
 } mt_conv2d_desc;
 size_t mt_cuda_conv2d_workspace_size(const mt_conv2d_desc* desc);
 int mt_cuda_conv2d(const mt_conv2d_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+/* Convolution of the channel concatenation [x | x2] without forming it (`cat(dim=1)`
+ * tensor.cpp:32141 followed by `conv2d`; the SD up-block's 1x1 shortcut): desc->x / x_strides
+ * describe the first source with C1 channels, desc->C is the total, x2 / x2_strides the second
+ * source (element strides n, c, h, w).  16-bit implicit-GEMM convolutions only, both sources
+ * dense channels-last and 16-byte aligned, C1 and C - C1 multiples of 64 (bf16/f16); otherwise
+ * MT_ERR_UNSUPPORTED.  Workspace: mt_cuda_conv2d_cat_workspace_size. */
+size_t mt_cuda_conv2d_cat_workspace_size(const mt_conv2d_desc* desc, const void* x2, const int64_t* x2_strides,
+                                         int64_t C1);
+int mt_cuda_conv2d_cat(const mt_conv2d_desc* desc, const void* x2, const int64_t* x2_strides, int64_t C1,
+                       void* workspace, size_t workspace_bytes, void* stream);
 /* Repacks a torch-layout weight [K, C, R, S] into [K, R, S, Cp] (Cp = C rounded up to a 16-byte
  * multiple) and, for MT_F32 with w_lo != NULL, writes the tf32 low part beside it.  Used once
  * per weight version by the module layer. */

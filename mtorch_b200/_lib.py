@@ -101,6 +101,8 @@ SIGNATURES = {
     "mt_cuda_softmax":(C.c_int, [VP, C.c_int, VP, C.c_int, I64, I64, I64, C.c_int, VP]),
     "mt_cuda_layer_norm": (C.c_int, [VP, C.c_int, VP, C.c_int, VP, VP, C.c_int, I64, I64, C.c_double, VP]),
     "mt_cuda_group_norm_workspace_size": (C.c_size_t, [I64, I64, I64, I64]),
+    "mt_cuda_group_norm_cat": (C.c_int, [VP, C.c_int, _P64, VP, _P64, I64, VP, _P64, C.c_int, VP, VP, C.c_int, I64,
+                                         I64, I64, I64, C.c_double, C.c_int, VP, C.c_size_t, VP]),
     "mt_cuda_group_norm": (C.c_int, [VP, C.c_int, _P64, VP, C.c_int, _P64, VP, VP, C.c_int, I64, I64, I64, I64,
                                      C.c_double, C.c_int, VP, C.c_size_t, VP]),
     "mt_cuda_group_norm_noalloc": (C.c_int, [VP, C.c_int, _P64, VP, C.c_int, _P64, VP, VP, C.c_int, I64, I64, I64,
@@ -109,6 +111,8 @@ SIGNATURES = {
     "mt_cuda_gemm": (C.c_int, [C.POINTER(GemmDesc), VP, C.c_size_t, VP]),
     "mt_cuda_conv2d_workspace_size": (C.c_size_t, [C.POINTER(Conv2dDesc)]),
     "mt_cuda_conv2d": (C.c_int, [C.POINTER(Conv2dDesc), VP, C.c_size_t, VP]),
+    "mt_cuda_conv2d_cat_workspace_size": (C.c_size_t, [C.POINTER(Conv2dDesc), VP, _P64, I64]),
+    "mt_cuda_conv2d_cat": (C.c_int, [C.POINTER(Conv2dDesc), VP, _P64, I64, VP, C.c_size_t, VP]),
     "mt_cuda_conv2d_packed_channels": (I64, [I64, I64, I64, C.c_int]),
     "mt_cuda_conv2d_pack_weight": (C.c_int, [VP, VP, VP, C.c_int, I64, I64, I64, I64, VP]),
     "mt_cuda_conv2d_up2x_workspace_size": (C.c_size_t, [C.POINTER(Conv2dDesc)]),

@@ -260,6 +260,14 @@ int mt_cuda_group_norm(void* y, int y_dtype, const int64_t* y_strides, const voi
                            eps, fuse_silu, workspace, workspace_bytes, S(stream));
 }
 
+int mt_cuda_group_norm_cat(void* y, int y_dtype, const int64_t* y_strides, const void* x1, const int64_t* x1_strides,
+                           int64_t C1, const void* x2, const int64_t* x2_strides, int x_dtype, const void* weight,
+                           const void* bias, int wb_dtype, int64_t N, int64_t C, int64_t HW, int64_t groups, double eps,
+                           int fuse_silu, void* workspace, size_t workspace_bytes, void* stream) {
+  return launch_group_norm_cat(y, y_dtype, y_strides, x1, x1_strides, C1, x2, x2_strides, x_dtype, weight, bias,
+                               wb_dtype, N, C, HW, groups, eps, fuse_silu, workspace, workspace_bytes, S(stream));
+}
+
 size_t mt_cuda_gemm_workspace_size(const mt_gemm_desc* desc) { return desc ? gemm_workspace(*desc) : 0; }
 int mt_cuda_gemm(const mt_gemm_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
   if (!desc) return fail(MT_ERR_INVALID, "gemm: null descriptor");
@@ -270,6 +278,15 @@ size_t mt_cuda_conv2d_workspace_size(const mt_conv2d_desc* desc) { return desc ?
 int mt_cuda_conv2d(const mt_conv2d_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
   if (!desc) return fail(MT_ERR_INVALID, "conv2d: null descriptor");
   return run_conv2d(*desc, workspace, workspace_bytes, S(stream));
+}
+size_t mt_cuda_conv2d_cat_workspace_size(const mt_conv2d_desc* desc, const void* x2, const int64_t* x2_strides,
+                                         int64_t C1) {
+  return desc ? conv_cat_workspace(*desc, x2, x2_strides, C1) : 0;
+}
+int mt_cuda_conv2d_cat(const mt_conv2d_desc* desc, const void* x2, const int64_t* x2_strides, int64_t C1,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (!desc) return fail(MT_ERR_INVALID, "conv2d_cat: null descriptor");
+  return run_conv2d_cat(*desc, x2, x2_strides, C1, workspace, workspace_bytes, S(stream));
 }
 int64_t mt_cuda_conv2d_packed_channels(int64_t C, int64_t R, int64_t S_, int dtype) {
   return conv_packed_channels(C, R, S_, dtype);

@@ -34,6 +34,10 @@ struct TileParams {
   int bk;  // elements per 128-byte K chunk
   int a_stages;  // B-resident variant: A-only stages behind the resident B tile
   int m_pairs;   // CTA-pair variant: row-tile pairs, ceil(num_m_tiles / 2)
+  // implicit convolution over the channel concatenation of two sources (16-bit only): channel
+  // chunks [0, c_split) come from tmA, the rest from the second source's map, passed in the tmAlo
+  // slot (unused by 16-bit kernels); 0 = one source
+  int c_split;
 };
 
 struct EpiParams {
@@ -329,7 +333,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (TF32) {
+    if (TF32 || (CONV && tp.c_split > 0)) {
       tma_prefetch_desc(&tmAlo);
       tma_prefetch_desc(&tmBlo);
     }
@@ -401,6 +405,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               const uint32_t fb = mapa_rank(&full[stage], 0);
               tma_load_4d_pair(sa, &tmA, fb, cx, wx, hy, i0);
               tma_load_3d_pair(sb, &tmB, fb, kk * tp.bk, n0, 0);
+            } else if (!TF32 && tp.c_split > 0 && cc >= tp.c_split) {
+              // second source of a channel concatenation: its own channel coordinate
+              tma_load_4d(sa, &tmAlo, &full[stage], (cc - tp.c_split) * tp.bk, wx, hy, i0);
+              tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, 0);
             } else {
               tma_load_4d(sa, &tmA, &full[stage], cx, wx, hy, i0);
               tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, 0);
@@ -728,7 +736,7 @@ static bool use_pair(GemmLaunch& L) {
     const char* e = getenv("MT_GEMM_PAIR");
     return !(e && e[0] == '1');
   }();
-  if (off || L.kind == MT_F32 || !L.b_ptr) return false;
+  if (off || L.kind == MT_F32 || !L.b_ptr || L.tp.c_split > 0) return false;
   if (L.bn != 128 && L.bn != 160 && L.bn != 256) return false;
   if (L.tp.num_m_tiles < 2) return false;
   L.tp.m_pairs = (L.tp.num_m_tiles + 1) / 2;
@@ -1060,10 +1068,20 @@ static bool is_channels_last(const int64_t* s, int64_t C, int64_t H, int64_t W) 
   return s[1] == 1 && s[3] == C && s[2] == W * C && s[0] == H * W * C;
 }
 
-static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream_t st, GemmLaunch* L) {
+// `cat` (optional): the input is the channel concatenation of d.x (cat->c1 channels, strides
+// d.x_strides) and cat->x2 (d.C - c1 channels); only the implicit 16-bit path takes it.
+struct ConvCat {
+  const void* x2;
+  int64_t x2_strides[4];
+  int64_t c1;
+};
+
+static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream_t st, GemmLaunch* L,
+                     const ConvCat* cat = nullptr) {
   const int es = dtype_size(d.dtype);
   const bool tf32 = d.dtype == MT_F32;
   const bool implicit = conv_implicit_ok(d);
+  if (cat && (tf32 || !implicit)) return fail(MT_ERR_UNSUPPORTED, "conv2d_cat: implicit 16-bit convolutions only");
   const int64_t Cp = conv_packed_channels(d.C, d.R, d.S, d.dtype);
   const int64_t Kg = d.R * d.S * Cp;  // GEMM K (16-byte aligned pitch)
   // Weights -> [K, R, S, Cp].
@@ -1115,7 +1133,9 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   const void* a = nullptr;
   const void* alo = nullptr;
   int64_t M = 0;
-  if (implicit) {
+  if (implicit && cat) {
+    a = d.x;
+  } else if (implicit) {
     const bool x_cl = is_channels_last(d.x_strides, d.C, d.H, d.W) && aligned16(d.x);
     a = d.x;
     if (!x_cl) {
@@ -1181,7 +1201,23 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
     // tw, th <= 128, so a stride-2 box (2 tw x 2 th input pixels) stays within TMA's 256 limit
     uint32_t box[4] = {(uint32_t)tp.bk, (uint32_t)(tw * d.stride_w), (uint32_t)(th * d.stride_h), (uint32_t)tn};
     const uint32_t estr[4] = {1, (uint32_t)d.stride_w, (uint32_t)d.stride_h, 1};
-    rc = make_tensor_map(&L->a, d.dtype, 4, a, dims, strides, box, 128, estr);
+    tp.c_split = 0;
+    if (cat) {
+      // two 4-D maps over the two channels-last sources, chunk c of the concatenation from the
+      // first when c < c1 / bk
+      const int64_t c2 = d.C - cat->c1;
+      uint64_t dims1[4] = {(uint64_t)cat->c1, (uint64_t)d.W, (uint64_t)d.H, (uint64_t)d.N};
+      uint64_t str1[3] = {(uint64_t)(d.x_strides[3] * es), (uint64_t)(d.x_strides[2] * es),
+                          (uint64_t)(d.x_strides[0] * es)};
+      uint64_t dims2[4] = {(uint64_t)c2, (uint64_t)d.W, (uint64_t)d.H, (uint64_t)d.N};
+      uint64_t str2[3] = {(uint64_t)(cat->x2_strides[3] * es), (uint64_t)(cat->x2_strides[2] * es),
+                          (uint64_t)(cat->x2_strides[0] * es)};
+      rc = make_tensor_map(&L->a, d.dtype, 4, d.x, dims1, str1, box, 128, estr);
+      if (!rc) rc = make_tensor_map(&L->alo, d.dtype, 4, cat->x2, dims2, str2, box, 128, estr);
+      tp.c_split = (int)(cat->c1 / tp.bk);
+    } else {
+      rc = make_tensor_map(&L->a, d.dtype, 4, a, dims, strides, box, 128, estr);
+    }
     if (!rc && tf32) rc = make_tensor_map(&L->alo, MT_F32, 4, alo, dims, strides, box, 128, estr);
   } else {
     tp.num_m_tiles = (int)((M + kBM - 1) / kBM);
@@ -1196,7 +1232,7 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   if (!rc && tf32) rc = map_kmajor(&L->blo, MT_F32, wlo, Kg, d.K, 1, Kg, 0, L->bn);
   if (rc) return rc;
   if (!tf32) {
-    L->alo = L->a;
+    if (!(cat && implicit)) L->alo = L->a;
     L->blo = L->b;
   }
 
@@ -1251,6 +1287,55 @@ int run_conv2d(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStream_t
   WsCursor ws{(char*)wsp, 0};
   GemmLaunch L{};
   rc = plan_conv(d, ws, true, st, &L);
+  if (rc) return rc;
+  rc = dispatch(L, st);
+  if (rc) return rc;
+  if (L.ep.D != d.y) {
+    int64_t cl[4] = {d.P * d.Q * d.K, 1, d.Q * d.K, d.K};
+    int64_t sizes[4] = {d.N, d.K, d.P, d.Q};
+    rc = launch_copy_strided(d.y, d.out_dtype, d.y_strides, L.ep.D, d.out_dtype, cl, sizes, 4, st);
+  }
+  return rc;
+}
+
+size_t conv_cat_workspace(const mt_conv2d_desc& d, const void* x2, const int64_t* x2_strides, int64_t c1) {
+  if (validate_conv(d) != MT_OK || !x2_strides) return 0;
+  ConvCat cat{};
+  cat.x2 = x2;
+  for (int i = 0; i < 4; ++i) cat.x2_strides[i] = x2_strides[i];
+  cat.c1 = c1;
+  WsCursor ws{nullptr, 0};
+  plan_conv(d, ws, false, nullptr, nullptr, &cat);
+  return ws.off;
+}
+
+// Convolution of the channel concatenation [x1 | x2] (the up-block skip connection) without
+// forming it: d.x / d.x_strides describe x1 with c1 channels, d.C is the total channel count.
+int run_conv2d_cat(const mt_conv2d_desc& d, const void* x2, const int64_t* x2_strides, int64_t c1, void* wsp,
+                   size_t ws_bytes, cudaStream_t st) {
+  int rc = validate_conv(d);
+  if (rc) return rc;
+  if (!x2 || !x2_strides) return fail(MT_ERR_INVALID, "conv2d_cat: null second source");
+  if (d.dtype != MT_BF16 && d.dtype != MT_F16) return fail(MT_ERR_UNSUPPORTED, "conv2d_cat: 16-bit inputs only");
+  const int64_t bk = 128 / dtype_size(d.dtype);
+  const int64_t c2 = d.C - c1;
+  if (c1 <= 0 || c2 <= 0 || c1 % bk || c2 % bk)
+    return fail(MT_ERR_UNSUPPORTED, "conv2d_cat: source channel counts must be multiples of %lld", (long long)bk);
+  if (!conv_implicit_ok(d)) return fail(MT_ERR_UNSUPPORTED, "conv2d_cat: shape needs the im2col path");
+  if (!is_channels_last(d.x_strides, c1, d.H, d.W) || !is_channels_last(x2_strides, c2, d.H, d.W) ||
+      !aligned16(d.x) || !aligned16(x2))
+    return fail(MT_ERR_UNSUPPORTED, "conv2d_cat: sources must be dense channels-last and 16-byte aligned");
+  if (d.N == 0 || d.P <= 0 || d.Q <= 0) return MT_OK;
+  const size_t need = conv_cat_workspace(d, x2, x2_strides, c1);
+  if (need > 0 && (!wsp || ws_bytes < need))
+    return fail(MT_ERR_WORKSPACE, "conv2d_cat: workspace of %zu bytes required", need);
+  ConvCat cat{};
+  cat.x2 = x2;
+  for (int i = 0; i < 4; ++i) cat.x2_strides[i] = x2_strides[i];
+  cat.c1 = c1;
+  WsCursor ws{(char*)wsp, 0};
+  GemmLaunch L{};
+  rc = plan_conv(d, ws, true, st, &L, &cat);
   if (rc) return rc;
   rc = dispatch(L, st);
   if (rc) return rc;

@@ -333,9 +333,15 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_cl_kernel(const void* x
 // Channels-last bf16 partial sums, 8 channels (16 bytes) per load: V = C/8 vectors per pixel,
 // thread t owns vector t % V of pixel lane t / V; one (lane, channel) slot per thread and
 // channel in shared memory keeps the reduction order fixed.
+//
+// TWO: the input is the channel concatenation of x (C1 channels per pixel, image stride sn) and
+// x2 (C - C1 channels, image stride sn2), read in place.
+template <bool TWO = false>
 __global__ void __launch_bounds__(kGnThreads, 5) gn_partial_cl_bf16x8_kernel(const __nv_bfloat16* x, int64_t sn,
                                                                           int64_t C, int64_t HW, int64_t G,
-                                                                          int chunks, double* part) {
+                                                                          int chunks, double* part,
+                                                                          const __nv_bfloat16* x2 = nullptr,
+                                                                          int64_t sn2 = 0, int64_t C1 = 0) {
   extern __shared__ float gn_sh[];  // [2][lanes * C]
   const int n = blockIdx.y, chunk = blockIdx.x;
   const int64_t per = (HW + chunks - 1) / chunks;
@@ -351,12 +357,21 @@ __global__ void __launch_bounds__(kGnThreads, 5) gn_partial_cl_bf16x8_kernel(con
     for (int j = 0; j < 8; ++j) s[j] = q[j] = 0.f;
     // four pixels' 16-byte loads in flight per thread (those past the chunk read as zero)
     const __nv_bfloat16* xv = xb + v * 8;
+    int64_t pitch = C;
+    if (TWO) {
+      if (v * 8 < C1) {
+        pitch = C1;
+      } else {
+        xv = x2 + (int64_t)n * sn2 + (v * 8 - C1);
+        pitch = C - C1;
+      }
+    }
     for (int p = (int)(p0 + lane); p < p1; p += 4 * (int)lanes) {
       uint4 u[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int pp = p + k * (int)lanes;
-        u[k] = pp < p1 ? *reinterpret_cast<const uint4*>(xv + (int64_t)pp * C) : make_uint4(0u, 0u, 0u, 0u);
+        u[k] = pp < p1 ? *reinterpret_cast<const uint4*>(xv + (int64_t)pp * pitch) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -460,19 +475,42 @@ __global__ void gn_finalize_table_kernel(const double* part, const void* w, cons
 // Apply with one grid row per image and a grid stride that is a multiple of C/8: every thread
 // always meets the same 8 channels, so it holds their (a, b) pairs in registers and each 16 bytes
 // of x cost one load and one store.  32-bit indexing inside the image (HW * C / 8 < 2^31).
+// TWO: x is the concatenation of x (C1 = 8 * c1_8 channels per pixel) and x2 (C - C1 channels),
+// both dense channels-last; the thread's fixed channel vector decides which source it reads.
+template <bool TWO = false>
 __global__ void __launch_bounds__(256) gn_apply_img_bf16x8_kernel(__nv_bfloat16* y, const __nv_bfloat16* x,
-                                                                  const float2* tab, int per_img8, int C8, int silu) {
+                                                                  const float2* tab, int per_img8, int C8, int silu,
+                                                                  const __nv_bfloat16* x2 = nullptr, int c1_8 = 0) {
   const int64_t n = blockIdx.y;
-  const uint4* xi = reinterpret_cast<const uint4*>(x) + n * per_img8;
-  uint4* yi = reinterpret_cast<uint4*>(y) + n * per_img8;
   const int i0 = blockIdx.x * blockDim.x + threadIdx.x;
   const int stride = gridDim.x * blockDim.x;
-  const float4* t = reinterpret_cast<const float4*>(tab + n * C8 * 8) + (i0 % C8) * 4;
+  const int c8 = i0 % C8;
+  // source vector of element vector i: pixel i / C8 at channel vector c8 of its source; the stride
+  // is a multiple of C8, so the pixel advances by stride / C8 per iteration
+  const uint4* xi;
+  int src_c8 = C8, src_off = c8;
+  if (TWO) {
+    const int c2_8 = C8 - c1_8;
+    if (c8 < c1_8) {
+      xi = reinterpret_cast<const uint4*>(x) + n * (int64_t)per_img8 / C8 * c1_8;
+      src_c8 = c1_8;
+    } else {
+      xi = reinterpret_cast<const uint4*>(x2) + n * (int64_t)per_img8 / C8 * c2_8;
+      src_c8 = c2_8;
+      src_off = c8 - c1_8;
+    }
+  } else {
+    xi = reinterpret_cast<const uint4*>(x) + n * per_img8;
+  }
+  uint4* yi = reinterpret_cast<uint4*>(y) + n * per_img8;
+  const float4* t = reinterpret_cast<const float4*>(tab + n * C8 * 8) + c8 * 4;
   float4 ab[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) ab[j] = t[j];  // (a0, b0, a1, b1) for channel pairs 2j, 2j+1
-  for (int i = i0; i < per_img8; i += stride) {
-    uint4 v = xi[i];
+  const int pix_step = stride / C8;
+  int pix = i0 / C8;
+  for (int i = i0; i < per_img8; i += stride, pix += pix_step) {
+    uint4 v = TWO ? xi[(int64_t)pix * src_c8 + src_off] : xi[i];
     __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -619,6 +657,16 @@ __global__ void gn_apply_generic_kernel(void* y, int yd, int64_t ys0, int64_t ys
   }
 }
 
+// Bytes of input per image group of the channels-last bf16 path (MT_GN_L2_GROUP_MB overrides the
+// default 24 MB; 0 processes the whole batch at once).
+static int64_t gn_l2_group_bytes() {
+  static const int64_t v = [] {
+    const char* e = getenv("MT_GN_L2_GROUP_MB");
+    return (int64_t)(e ? atof(e) * (1 << 20) : 24.0 * (1 << 20));
+  }();
+  return v;
+}
+
 static int gn_chunks(int64_t C, int64_t HW, int64_t G, bool cl) {
   int64_t chunks = cl ? (HW + 63) / 64 : (C / G * HW + 4095) / 4096;
   if (chunks < 1) chunks = 1;
@@ -633,6 +681,65 @@ static size_t gn_stats_bytes(int64_t N, int64_t G) { return align_up((size_t)N *
 
 size_t group_norm_workspace(int64_t N, int64_t C, int64_t HW, int64_t G) {
   return gn_part_bytes(N, G) + gn_stats_bytes(N, G) + (size_t)N * C * sizeof(float2);
+}
+
+// The channels-last bf16 path (dense [N, HW, C] in and out, C % 8 == 0).  Images are processed in
+// groups of about gn_l2_group_bytes(): statistics, table and apply of one group run back to back,
+// so the apply pass re-reads x from L2 instead of HBM (one HBM read and one write per element).
+// The per-image work does not depend on the grouping, so results are identical for every batch
+// size.  x2 != nullptr: the input is the channel concatenation [x (C1 channels) | x2 (C - C1)].
+static int gn_fast_cl(__nv_bfloat16* y, const __nv_bfloat16* x, int64_t sn, const __nv_bfloat16* x2, int64_t sn2,
+                      int64_t C1, const void* w, const void* b, int wbd, int64_t N, int64_t C, int64_t HW, int64_t G,
+                      double eps, int silu, double* part, float2* tab, int chunks, cudaStream_t st) {
+  const int64_t img_bytes = HW * C * 2;
+  const int64_t group_bytes = gn_l2_group_bytes();
+  const int64_t per = group_bytes > 0 ? std::max<int64_t>(1, group_bytes / img_bytes) : N;
+  const int64_t ngroups = (N + per - 1) / per;
+  const int64_t nc_max = (N + ngroups - 1) / ngroups;  // balanced groups
+  const int64_t V = C / 8;
+  const int64_t slots = (V >= kGnThreads ? 1 : kGnThreads / V) * C;
+  if (2 * slots * sizeof(float) > 48 * 1024) return fail(MT_ERR_UNSUPPORTED, "group_norm: too many channels");
+  const int per_img8 = (int)(HW * C / 8);
+  const int C8 = (int)(C / 8);
+  // blocks per image: a multiple of C8 / gcd(C8, 256), so that the stride is a multiple of C8
+  int g = C8, r = 256;
+  while (r) {
+    const int t = g % r;
+    g = r;
+    r = t;
+  }
+  const int unit = C8 / g;
+  for (int64_t n0 = 0; n0 < N; n0 += nc_max) {
+    const int64_t nc = std::min<int64_t>(nc_max, N - n0);
+    double* part_g = part + n0 * chunks * G * 2;
+    float2* tab_g = tab + n0 * C;
+    const __nv_bfloat16* xg = x + n0 * sn;
+    const __nv_bfloat16* x2g = x2 ? x2 + n0 * sn2 : nullptr;
+    const size_t sh = 2 * slots * sizeof(float);
+    if (x2)
+      gn_partial_cl_bf16x8_kernel<true><<<dim3(chunks, (unsigned)nc), kGnThreads, sh, st>>>(
+          xg, sn, C, HW, G, chunks, part_g, x2g, sn2, C1);
+    else
+      gn_partial_cl_bf16x8_kernel<false><<<dim3(chunks, (unsigned)nc), kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks,
+                                                                                           part_g);
+    int rc = check_launch("group_norm partial");
+    if (rc) return rc;
+    gn_finalize_table_kernel<<<(unsigned)((nc * G * 32 + 255) / 256), 256, 0, st>>>(
+        part_g, w, b, wbd, nc, C, G, chunks, (double)(C / G) * (double)HW, eps, tab_g);
+    rc = check_launch("group_norm finalize");
+    if (rc) return rc;
+    int bx = (int)std::max<int64_t>(1, std::min<int64_t>((per_img8 + 255) / 256, (int64_t)num_sms() * 16 / nc + 1));
+    bx = (bx + unit - 1) / unit * unit;
+    if (x2)
+      gn_apply_img_bf16x8_kernel<true><<<dim3((unsigned)bx, (unsigned)nc), 256, 0, st>>>(
+          y + n0 * HW * C, xg, tab_g, per_img8, C8, silu, x2g, (int)(C1 / 8));
+    else
+      gn_apply_img_bf16x8_kernel<false><<<dim3((unsigned)bx, (unsigned)nc), 256, 0, st>>>(y + n0 * HW * C, xg, tab_g,
+                                                                                        per_img8, C8, silu);
+    rc = check_launch("group_norm apply");
+    if (rc) return rc;
+  }
+  return MT_OK;
 }
 
 int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd, const int64_t* xs, const void* w,
@@ -654,6 +761,12 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
   // 1280; between 16 and 128): long enough CTAs for narrow images, enough CTAs for wide ones
   const int64_t gn_px = std::max<int64_t>(16, std::min<int64_t>(128, 40960 / C));
   const int chunks = vec_in ? (int)std::min<int64_t>(kGnMaxChunks, (HW + gn_px - 1) / gn_px) : gn_chunks(C, HW, G, cl);
+  const bool ycl = (ys[1] == 1 && ys[2] == C && ys[0] == HW * C);
+  const bool fast = vec_in && ycl && xs[0] == HW * C && yd == MT_BF16 && (uintptr_t)y % 16 == 0 &&
+                    HW * C / 8 < (1LL << 31);
+  if (fast)
+    return gn_fast_cl((__nv_bfloat16*)y, (const __nv_bfloat16*)x, xs[0], nullptr, 0, 0, w, b, wbd, N, C, HW, G, eps,
+                      silu, part, tab, chunks, st);
   if (vec_in) {
     const int64_t V = C / 8;
     const int64_t slots = (V >= kGnThreads ? 1 : kGnThreads / V) * C;
@@ -671,29 +784,7 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
   }
   int rc = check_launch("group_norm partial");
   if (rc) return rc;
-  const bool ycl = (ys[1] == 1 && ys[2] == C && ys[0] == HW * C);
   const int64_t total = N * C * HW;
-  if (vec_in && ycl && xs[0] == HW * C && yd == MT_BF16 && (uintptr_t)y % 16 == 0 && HW * C / 8 < (1LL << 31)) {
-    gn_finalize_table_kernel<<<(unsigned)((N * G * 32 + 255) / 256), 256, 0, st>>>(
-        part, w, b, wbd, N, C, G, chunks, (double)(C / G) * (double)HW, eps, tab);
-    rc = check_launch("group_norm finalize");
-    if (rc) return rc;
-    const int per_img8 = (int)(HW * C / 8);
-    const int C8 = (int)(C / 8);
-    // blocks per image: a multiple of C8 / gcd(C8, 256), so that the stride is a multiple of C8
-    int g = C8, r = 256;
-    while (r) {
-      const int t = g % r;
-      g = r;
-      r = t;
-    }
-    const int unit = C8 / g;
-    int bx = (int)std::max<int64_t>(1, std::min<int64_t>((per_img8 + 255) / 256, (int64_t)num_sms() * 16 / N + 1));
-    bx = (bx + unit - 1) / unit * unit;
-    gn_apply_img_bf16x8_kernel<<<dim3((unsigned)bx, (unsigned)N), 256, 0, st>>>(
-        (__nv_bfloat16*)y, (const __nv_bfloat16*)x, tab, per_img8, (int)(C / 8), silu);
-    return check_launch("group_norm apply");
-  }
   gn_finalize_kernel<<<(unsigned)((N * G + 127) / 128), 128, 0, st>>>(part, stats, N, G, chunks,
                                                                       (double)(C / G) * (double)HW, eps);
   rc = check_launch("group_norm finalize");
@@ -711,6 +802,37 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
                                                              stats, w, b, wbd, N, C, HW, G, silu, cl ? 1 : 0);
   }
   return check_launch("group_norm apply");
+}
+
+// Group norm of the channel concatenation [x1 | x2] (the up-block skip connection) without forming
+// it: bf16 dense channels-last sources of C1 and C - C1 channels (multiples of 8), bf16 dense
+// channels-last output of C channels.  Same statistics and chunking as launch_group_norm's
+// channels-last path on the concatenated tensor.
+int launch_group_norm_cat(void* y, int yd, const int64_t* ys, const void* x1, const int64_t* xs1, int64_t C1,
+                          const void* x2, const int64_t* xs2, int xd, const void* w, const void* b, int wbd, int64_t N,
+                          int64_t C, int64_t HW, int64_t G, double eps, int silu, void* ws, size_t ws_bytes,
+                          cudaStream_t st) {
+  if (G <= 0 || C % G != 0)
+    return fail(MT_ERR_INVALID, "group_norm_cat: channels %lld not divisible by groups %lld", (long long)C,
+                (long long)G);
+  if (!x1 || !x2 || !y || !xs1 || !xs2 || !ys) return fail(MT_ERR_INVALID, "group_norm_cat: null argument");
+  const int64_t C2 = C - C1;
+  if (C1 <= 0 || C2 <= 0 || C1 % 8 || C2 % 8)
+    return fail(MT_ERR_UNSUPPORTED, "group_norm_cat: source channel counts must be positive multiples of 8");
+  if (xd != MT_BF16 || yd != MT_BF16) return fail(MT_ERR_UNSUPPORTED, "group_norm_cat: bf16 only");
+  if (N == 0 || HW == 0) return MT_OK;
+  if (N > 65535) return fail(MT_ERR_UNSUPPORTED, "group_norm_cat: batch too large");
+  auto dense_cl = [&](const int64_t* s, int64_t c) { return s[1] == 1 && s[2] == c && s[0] == HW * c; };
+  if (!dense_cl(xs1, C1) || !dense_cl(xs2, C2) || !dense_cl(ys, C) || (uintptr_t)x1 % 16 || (uintptr_t)x2 % 16 ||
+      (uintptr_t)y % 16 || HW * C / 8 >= (1LL << 31))
+    return fail(MT_ERR_UNSUPPORTED, "group_norm_cat: dense 16-byte aligned channels-last tensors only");
+  if (!ws || ws_bytes < group_norm_workspace(N, C, HW, G)) return fail(MT_ERR_WORKSPACE, "group_norm_cat: workspace");
+  double* part = (double*)ws;
+  float2* tab = (float2*)((char*)ws + gn_part_bytes(N, G) + gn_stats_bytes(N, G));
+  const int64_t gn_px = std::max<int64_t>(16, std::min<int64_t>(128, 40960 / C));
+  const int chunks = (int)std::min<int64_t>(kGnMaxChunks, (HW + gn_px - 1) / gn_px);
+  return gn_fast_cl((__nv_bfloat16*)y, (const __nv_bfloat16*)x1, xs1[0], (const __nv_bfloat16*)x2, xs2[0], C1, w, b,
+                    wbd, N, C, HW, G, eps, silu, part, tab, chunks, st);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -82,10 +82,17 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
                       void* ws, size_t ws_bytes, cudaStream_t st);
 
 // gemm.cu
+int launch_group_norm_cat(void* y, int yd, const int64_t* ys, const void* x1, const int64_t* xs1, int64_t C1,
+                          const void* x2, const int64_t* xs2, int xd, const void* w, const void* b, int wbd, int64_t N,
+                          int64_t C, int64_t HW, int64_t G, double eps, int silu, void* ws, size_t ws_bytes,
+                          cudaStream_t st);
 size_t gemm_workspace(const mt_gemm_desc& d);
 int run_gemm(const mt_gemm_desc& d, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t conv_workspace(const mt_conv2d_desc& d);
 int run_conv2d(const mt_conv2d_desc& d, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t conv_cat_workspace(const mt_conv2d_desc& d, const void* x2, const int64_t* x2_strides, int64_t c1);
+int run_conv2d_cat(const mt_conv2d_desc& d, const void* x2, const int64_t* x2_strides, int64_t c1, void* ws,
+                   size_t ws_bytes, cudaStream_t st);
 int64_t conv_up2x_packed_elems(int64_t K, int64_t C, int dtype);
 size_t conv_up2x_workspace(const mt_conv2d_desc& d);
 int run_conv2d_up2x(const mt_conv2d_desc& d, void* ws, size_t ws_bytes, cudaStream_t st);

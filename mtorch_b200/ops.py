@@ -272,6 +272,87 @@ def conv2d(x: Tensor, w: Tensor, bias: Tensor | None = None, stride=1, padding=0
     return y.squeeze(0) if unbatched else y
 
 
+def cat_fusable(a: Tensor, b: Tensor) -> bool:
+    """Whether `group_norm_cat` / `conv2d_cat` read the channel concatenation [a | b] in place: bf16
+    cuda tensors [N, C, H, W] of equal N, H, W, dense channels-last, channel counts multiples of 64."""
+    return (a.device.type == "cuda" and b.device.type == "cuda" and a.dim() == 4 and b.dim() == 4 and
+            a.dtype is bfloat16 and b.dtype is bfloat16 and a._shape[0] == b._shape[0] and
+            a._shape[2:] == b._shape[2:] and a._shape[1] % 64 == 0 and b._shape[1] % 64 == 0 and
+            a.is_contiguous("channels_last") and b.is_contiguous("channels_last"))
+
+
+def group_norm_cat(a: Tensor, b: Tensor, num_groups: int, weight=None, bias=None, eps=1e-5, *,
+                   fuse_silu=False) -> Tensor:
+    """group_norm(cat([a, b], dim=1)) without forming the concatenation (bit-identical to it);
+    inputs as `cat_fusable` describes, output channels-last."""
+    _require_cuda(a, b, weight, bias)
+    if not cat_fusable(a, b):
+        raise NotImplementedError("group_norm_cat: inputs must satisfy cat_fusable")
+    N, C1 = a._shape[0], a._shape[1]
+    Cc = C1 + b._shape[1]
+    if Cc % num_groups:
+        raise RuntimeError(f"Expected number of channels in input to be divisible by num_groups, but got {Cc} "
+                           f"channels and num_groups={num_groups}")
+    HW = a._shape[2] * a._shape[3]
+    out = _new((N, Cc) + a._shape[2:], a.dtype, a.device, channels_last=True)
+    wbd = (weight if weight is not None else bias).dtype.code if (weight is not None or bias is not None) else L.MT_F32
+    lib = _lib()
+    need = lib.mt_cuda_group_norm_workspace_size(N, Cc, HW, num_groups)
+    ws, wsb = workspace(need, a._idx())
+    L.check(lib.mt_cuda_group_norm_cat(out.data_ptr(), out.dtype.code, L.arr64(_nchw_view_strides(out)), a.data_ptr(),
+                                       L.arr64(_nchw_view_strides(a)), C1, b.data_ptr(),
+                                       L.arr64(_nchw_view_strides(b)), a.dtype.code,
+                                       weight.data_ptr() if weight is not None else None,
+                                       bias.data_ptr() if bias is not None else None, wbd, N, Cc, HW, num_groups,
+                                       float(eps), 1 if fuse_silu else 0, ws, wsb, a._stream()), "group_norm_cat")
+    return out
+
+
+def conv2d_cat(a: Tensor, b: Tensor, w: Tensor, bias: Tensor | None = None, stride=1, padding=0, *,
+               residual: Tensor | None = None, packed=None) -> Tensor:
+    """conv2d(cat([a, b], dim=1), w, bias, stride, padding) without forming the concatenation
+    (bit-identical to it); inputs as `cat_fusable` describes, output channels-last."""
+    _require_cuda(a, b, w, bias, residual)
+    _same_dtype(a, b, w, what="conv2d_cat")
+    if not cat_fusable(a, b):
+        raise NotImplementedError("conv2d_cat: inputs must satisfy cat_fusable")
+    N, C1, H, W = a._shape
+    Cin = C1 + b._shape[1]
+    K, Cg, R, S = w._shape
+    if Cg != Cin:
+        raise RuntimeError(f"conv2d_cat: weight of size {tuple(w._shape)} expects {Cg} input channels, got {Cin}")
+    sh, sw = _pair(stride)
+    ph, pw = _pair(padding)
+    P = (H + 2 * ph - (R - 1) - 1) // sh + 1
+    Q = (W + 2 * pw - (S - 1) - 1) // sw + 1
+    y = _new((N, K, P, Q), a.dtype, a.device, channels_last=True)
+    d = L.Conv2dDesc()
+    d.N, d.C, d.H, d.W, d.K, d.R, d.S, d.P, d.Q = N, Cin, H, W, K, R, S, P, Q
+    d.stride_h, d.stride_w, d.pad_h, d.pad_w, d.dil_h, d.dil_w, d.groups = sh, sw, ph, pw, 1, 1, 1
+    d.dtype = d.out_dtype = a.dtype.code
+    d.x = a.data_ptr()
+    d.x_strides[:] = list(a._strides)
+    if packed is not None:
+        d.w, d.w_packed = packed[0].data_ptr(), 1
+    else:
+        wc = w.contiguous()
+        d.w, d.w_packed = wc.data_ptr(), 0
+    if bias is not None:
+        bias = bias.contiguous()
+        d.bias, d.bias_dtype = bias.data_ptr(), bias.dtype.code
+    if residual is not None:
+        d.residual = residual.data_ptr()
+        d.res_strides[:] = list(residual.expand(y.shape)._strides)
+    d.y = y.data_ptr()
+    d.y_strides[:] = list(y._strides)
+    lib = _lib()
+    bst = L.arr64(list(b._strides))
+    need = lib.mt_cuda_conv2d_cat_workspace_size(C.byref(d), b.data_ptr(), bst, C1)
+    ws, wsb = workspace(need, a._idx())
+    L.check(lib.mt_cuda_conv2d_cat(C.byref(d), b.data_ptr(), bst, C1, ws, wsb, a._stream()), "conv2d_cat")
+    return y
+
+
 def pack_conv_weight(w: Tensor):
     """[K, C, R, S] -> ([K, R, S, Cp] packed, tf32 low part or None) for the implicit-GEMM path."""
     _require_cuda(w)

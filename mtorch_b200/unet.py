@@ -9,7 +9,8 @@ levels, 8 heads, timestep embedding 320 -> 1280.
 
 Layout: activations stay channels-last ([N, C, H, W] with C innermost), so the token view of a
 feature map ([N*H*W, C]) is free and convolutions run as implicit GEMM.  Fusions (each one
-kernel): GroupNorm+SiLU; conv1 + (conv bias + time-embedding projection) as a per-image bias;
+kernel): GroupNorm+SiLU; the up-block skip concatenation read in place by the first GroupNorm
+and the 1x1 shortcut conv (bf16); conv1 + (conv bias + time-embedding projection) as a per-image bias;
 conv2 + shortcut residual; attention-out / FF-out / proj-out projections + residual; GEGLU
 (value * gelu(gate)) in the FF-in GEMM epilogue; QKV as one GEMM with attention reading strided
 head views; attention writing heads-merged output; DDIM update as one kernel.
@@ -49,15 +50,28 @@ class ResnetBlock(Module):
         self.conv_shortcut = Conv2d(cin, cout, 1, device=device, dtype=dtype) if cin != cout else None
         self.cout = cout
 
-    def forward(self, x, temb_silu):
-        n = x.shape[0]
-        h = self.norm1(x, fuse_silu=True)
+    def forward(self, x, temb_silu, skip=None):
+        """`skip` (up blocks): the block's input is cat([x, skip], dim=1).  When the two tensors
+        allow it (ops.cat_fusable) the concatenation is never formed: the first GroupNorm and the
+        1x1 shortcut read both sources in place, with results bit-identical to the concatenated
+        form."""
+        if skip is not None and not (ops.cat_fusable(x, skip) and self.conv_shortcut is not None):
+            x, skip = ops.cat([x, skip], dim=1), None
+        if skip is None:
+            h = self.norm1(x, fuse_silu=True)
+        else:
+            n1 = self.norm1
+            h = ops.group_norm_cat(x, skip, n1.num_groups, n1.weight, n1.bias, n1.eps, fuse_silu=True)
         # per-image bias = time_emb_proj(silu(temb)) + time_emb_proj.bias + conv1.bias  (fp32 [N, C])
         b = add(self.time_emb_proj.bias, self.conv1.bias).float()
         tb = ops.gemm(temb_silu, self.time_emb_proj.weight.transpose(0, 1), bias=b, out_dtype=float32)
         h = self.conv1(h, bias=tb, bias_batch_stride=self.cout)
         h = self.norm2(h, fuse_silu=True)
-        res = x if self.conv_shortcut is None else self.conv_shortcut(x)
+        if skip is not None:
+            sc = self.conv_shortcut
+            res = ops.conv2d_cat(x, skip, sc.weight, sc.bias, packed=sc.packed_weight())
+        else:
+            res = x if self.conv_shortcut is None else self.conv_shortcut(x)
         return self.conv2(h, residual=res)
 
 
@@ -263,7 +277,7 @@ class UNet(Module):
         while i < len(mods):
             m = mods[i]
             if isinstance(m, ResnetBlock):
-                h = m(ops.cat([h, skips.pop()], dim=1), temb)
+                h = m(h, temb, skips.pop())
                 a = mods[i + 1]
                 if not isinstance(a, None_):
                     h = a(h, ctx)

@@ -472,3 +472,32 @@ def test_sdpa_path_of_unet_shapes():
     qb = q.to("bfloat16")
     mask = mt.zeros(64, 64, device="cuda")
     assert mt.ops.sdpa_path(qb, qb, qb, attn_mask=mask) == "simt"
+
+
+@pytest.mark.parametrize("n,c1,c2,hw,silu", [(2, 1280, 1280, 8, True), (3, 640, 320, 16, True), (2, 320, 640, 32, False),
+                                            (1, 64, 128, 12, True)])
+def test_skip_concat_fused_consumers_bitwise(n, c1, c2, hw, silu):
+    """The up-block skip connection: GroupNorm and the 1x1 shortcut conv read cat([a, b], dim=1)
+    in place; both are bit-identical to the same kernels on the materialised concatenation, and
+    within the bf16 tolerance of the oracle."""
+    rng = np.random.default_rng(c1 + c2 + hw)
+    a = cu(rng.standard_normal((n, c1, hw, hw)).astype(np.float32), "bfloat16").contiguous(memory_format=mt.channels_last)
+    b = cu(rng.standard_normal((n, c2, hw, hw)).astype(np.float32) * 2, "bfloat16").contiguous(
+        memory_format=mt.channels_last)
+    C = c1 + c2
+    w = cu(rng.standard_normal(C).astype(np.float32), "bfloat16")
+    bias = cu(rng.standard_normal(C).astype(np.float32), "bfloat16")
+    cat = mt.cat([a, b], dim=1)
+    assert mt.ops.cat_fusable(a, b)
+    got = mt.ops.group_norm_cat(a, b, 32, w, bias, 1e-5, fuse_silu=silu).numpy()
+    np.testing.assert_array_equal(got, mt.group_norm(cat, 32, w, bias, 1e-5, fuse_silu=silu).numpy())
+    ref = oracle.group_norm_f32(cat.numpy(), 32, w.numpy(), bias.numpy())
+    check(got, oracle.silu_f32(ref) if silu else ref, BF16_RTOL)
+    K = 320
+    wc = cu(rng.standard_normal((K, C, 1, 1)).astype(np.float32) * C ** -0.5, "bfloat16")
+    bc = cu(rng.standard_normal(K).astype(np.float32), "bfloat16")
+    got = mt.ops.conv2d_cat(a, b, wc, bc).numpy()
+    np.testing.assert_array_equal(got, mt.conv2d(cat, wc, bc).numpy())
+    check(got, oracle.conv2d_f32(cat.numpy(), wc.numpy(), bc.numpy()), BF16_RTOL)
+    w3 = cu(rng.standard_normal((K, C, 3, 3)).astype(np.float32) * (9 * C) ** -0.5, "bfloat16")
+    np.testing.assert_array_equal(mt.ops.conv2d_cat(a, b, w3, None, 1, 1).numpy(), mt.conv2d(cat, w3, None, 1, 1).numpy())
