@@ -657,14 +657,12 @@ __global__ void gn_apply_generic_kernel(void* y, int yd, int64_t ys0, int64_t ys
   }
 }
 
-// Bytes of input per image group of the channels-last bf16 path: MT_GN_L2_GROUP_MB > 0 processes
-// the batch in groups of that size so that the apply pass re-reads x from L2.  Off by default:
-// measured at 320 channels x 64x64 x 64 images it took 265 us against 124 us for the whole batch
-// at once (three dependent launches per group, and groups too small to fill the GPU).
+// Bytes of input per image group of the channels-last bf16 path (MT_GN_L2_GROUP_MB overrides the
+// default 24 MB; 0 processes the whole batch at once).
 static int64_t gn_l2_group_bytes() {
   static const int64_t v = [] {
     const char* e = getenv("MT_GN_L2_GROUP_MB");
-    return (int64_t)(e ? atof(e) * (1 << 20) : 0.0);
+    return (int64_t)(e ? atof(e) * (1 << 20) : 24.0 * (1 << 20));
   }();
   return v;
 }
@@ -685,249 +683,14 @@ size_t group_norm_workspace(int64_t N, int64_t C, int64_t HW, int64_t G) {
   return gn_part_bytes(N, G) + gn_stats_bytes(N, G) + (size_t)N * C * sizeof(float2);
 }
 
-// ---------------------------------------------------------------------------------------------
-// Single-pass channels-last bf16 GroupNorm: one thread-block cluster per image.  CTA r of the
-// cluster copies pixels [r * pp, (r + 1) * pp) of the image (all C channels) from HBM into its
-// shared memory while summing x and x^2 per channel, reduces them to per-group sums in double,
-// and publishes those; after a cluster barrier every CTA adds the CS CTAs' group sums in rank
-// order (distributed shared memory), derives mean / rstd and the per-channel affine, and writes
-// y from its shared-memory copy.  HBM traffic is one read and one write per element; the
-// reduction order depends only on the image shape, so results are identical for every batch size.
-constexpr int kGnClusterThreads = 512;
-constexpr int kGnClusterSmemMax = 220 * 1024;
-
-__device__ __forceinline__ double ld_dsmem_f64(uint32_t addr) {
-  double v;
-  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(addr) : "memory");
-  return v;
-}
-
-template <bool TWO>
-__global__ void __launch_bounds__(kGnClusterThreads, 1)
-    gn_cluster_kernel(__nv_bfloat16* y, const __nv_bfloat16* x, int64_t sn, const __nv_bfloat16* x2, int64_t sn2,
-                      int C1, const void* w, const void* b, int wbd, int C, int HW, int G, int pp, double eps,
-                      int silu) {
-  extern __shared__ __align__(16) uint8_t gnc_smem[];
-  const int CS = (int)gridDim.x;  // the cluster spans the grid's x dimension
-  const uint32_t rank = cluster_ctarank();
-  const int n = blockIdx.y;
-  const int p0 = (int)rank * pp, p1 = min(HW, p0 + pp);
-  const int V = C / 8;
-  const int lanes = kGnClusterThreads / V;
-  const int t = threadIdx.x;
-  uint4* tile = reinterpret_cast<uint4*>(gnc_smem);                           // [pp][V]
-  float* slots = reinterpret_cast<float*>(gnc_smem + (size_t)pp * C * 2);     // [2][lanes * C]
-  double* gpart = reinterpret_cast<double*>(slots + 2 * lanes * C);           // [G][2]
-  float* gstat = reinterpret_cast<float*>(gpart + 2 * G);                     // [G][2] mean, rstd
-  const bool active = t < lanes * V;
-  const int v = t % V, l = t / V;
-  // phase 1: HBM -> shared memory, per-(lane, channel) sums in registers (four loads in flight)
-  if (active) {
-    const __nv_bfloat16* src = x + (int64_t)n * sn + v * 8;
-    int64_t pitch = TWO ? C1 : C;
-    if (TWO && v * 8 >= C1) {
-      src = x2 + (int64_t)n * sn2 + (v * 8 - C1);
-      pitch = C - C1;
-    }
-    float s[8], q[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[j] = q[j] = 0.f;
-    for (int p = p0 + l; p < p1; p += 4 * lanes) {
-      uint4 u[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int pk = p + k * lanes;
-        u[k] = pk < p1 ? *reinterpret_cast<const uint4*>(src + (int64_t)pk * pitch) : make_uint4(0u, 0u, 0u, 0u);
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int pk = p + k * lanes;
-        if (pk < p1) tile[(pk - p0) * V + v] = u[k];
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[k]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(h[j]);
-          s[2 * j] += f.x;
-          q[2 * j] += f.x * f.x;
-          s[2 * j + 1] += f.y;
-          q[2 * j + 1] += f.y * f.y;
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      slots[l * C + v * 8 + j] = s[j];
-      slots[lanes * C + l * C + v * 8 + j] = q[j];
-    }
-  }
-  __syncthreads();
-  for (int c = t; c < C; c += kGnClusterThreads) {
-    float a = 0.f, q = 0.f;
-    for (int k = 0; k < lanes; ++k) {
-      a += slots[k * C + c];
-      q += slots[lanes * C + k * C + c];
-    }
-    slots[c] = a;
-    slots[lanes * C + c] = q;
-  }
-  __syncthreads();
-  const int Cg = C / G;
-  for (int g = t; g < G; g += kGnClusterThreads) {
-    double a = 0.0, q = 0.0;
-    for (int c = g * Cg; c < (g + 1) * Cg; ++c) {
-      a += slots[c];
-      q += slots[lanes * C + c];
-    }
-    gpart[2 * g] = a;
-    gpart[2 * g + 1] = q;
-  }
-  cluster_sync();  // every CTA's group sums are published
-  // phase 2: image statistics from the CS CTAs' group sums, in rank order
-  const double count = (double)Cg * (double)HW;
-  for (int g = t; g < G; g += kGnClusterThreads) {
-    double a = 0.0, q = 0.0;
-    for (int r = 0; r < CS; ++r) {
-      const uint32_t addr = mapa_rank(&gpart[2 * g], (uint32_t)r);
-      a += ld_dsmem_f64(addr);
-      q += ld_dsmem_f64(addr + 8);
-    }
-    const double mean = a / count;
-    double var = q / count - mean * mean;
-    if (var < 0) var = 0;
-    gstat[2 * g] = (float)mean;
-    gstat[2 * g + 1] = (float)(1.0 / sqrt(var + eps));
-  }
-  __syncthreads();
-  // phase 3: y = x * a + b (+ SiLU) from shared memory, a = rstd * gamma, b = beta - mean * a
-  if (active) {
-    float ga[8], gb[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = v * 8 + j, g = c / Cg;
-      const float mf = gstat[2 * g], rstd = gstat[2 * g + 1];
-      float a = rstd, sh = -mf * rstd;
-      if (w) {
-        const float gm = load_as_f32(w, c, wbd);
-        a *= gm;
-        sh *= gm;
-      }
-      if (b) sh += load_as_f32(b, c, wbd);
-      ga[j] = a;
-      gb[j] = sh;
-    }
-    __nv_bfloat16* dst = y + ((int64_t)n * HW) * C + v * 8;
-    for (int p = p0 + l; p < p1; p += lanes) {
-      uint4 u = tile[(p - p0) * V + v];
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        float r0 = f.x * ga[2 * j] + gb[2 * j], r1 = f.y * ga[2 * j + 1] + gb[2 * j + 1];
-        if (silu) {
-          r0 = silu_f(r0);
-          r1 = silu_f(r1);
-        }
-        h[j] = __floats2bfloat162_rn(r0, r1);
-      }
-      *reinterpret_cast<uint4*>(dst + (int64_t)p * C) = u;
-    }
-  }
-  cluster_sync();  // no CTA leaves while another may still read its group sums
-}
-
-// Cluster size and per-CTA pixel count of the single-pass kernel for one image, or 0 when the
-// image does not fit (CS <= 16 CTAs of at most kGnClusterSmemMax bytes) or the GPU cannot hold
-// such a cluster.  Sets *smem to the dynamic shared memory per CTA.
-static int gn_cluster_plan(bool two, int64_t C, int64_t HW, int64_t G, int* pp_out, int* smem) {
-  static const bool off = getenv("MT_GN_NO_CLUSTER") != nullptr;
-  if (off || C % 8 != 0 || C / 8 > kGnClusterThreads || HW > (1 << 24)) return 0;
-  const int64_t V = C / 8, lanes = kGnClusterThreads / V;
-  const int64_t fixed = 2 * lanes * C * 4 + G * 16 + G * 8;
-  for (int cs = 1; cs <= 16; cs *= 2) {
-    const int64_t pp = (HW + cs - 1) / cs;
-    const int64_t bytes = pp * C * 2 + fixed;
-    if (bytes > kGnClusterSmemMax) continue;
-    // the GPU must be able to run at least one such cluster
-    static std::mutex mu;
-    static int64_t known[64][3];  // (two, cs, bytes) -> ok (cached per device)
-    static int nknown = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int64_t key = ((int64_t)dev << 40) | ((int64_t)two << 32) | ((int64_t)cs << 24) | bytes;
-    std::lock_guard<std::mutex> lock(mu);
-    int ok = -1;
-    for (int i = 0; i < nknown; ++i)
-      if (known[i][0] == key) ok = (int)known[i][1];
-    if (ok < 0) {
-      auto kern = two ? gn_cluster_kernel<true> : gn_cluster_kernel<false>;
-      ok = 0;
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGnClusterSmemMax) == cudaSuccess &&
-          cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)cs, 1);
-        cfg.blockDim = dim3(kGnClusterThreads);
-        cfg.dynamicSmemBytes = (size_t)bytes;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = (unsigned)cs;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        int clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters > 0) ok = 1;
-      }
-      cudaGetLastError();  // a refused query leaves no sticky error behind
-      if (nknown < 64) {
-        known[nknown][0] = key;
-        known[nknown][1] = ok;
-        ++nknown;
-      }
-    }
-    if (!ok) return 0;
-    *pp_out = (int)pp;
-    *smem = (int)bytes;
-    return cs;
-  }
-  return 0;
-}
-
-static int gn_cluster_launch(bool two, int cs, int pp, int smem, __nv_bfloat16* y, const __nv_bfloat16* x, int64_t sn,
-                             const __nv_bfloat16* x2, int64_t sn2, int64_t C1, const void* w, const void* b, int wbd,
-                             int64_t N, int64_t C, int64_t HW, int64_t G, double eps, int silu, cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)cs, (unsigned)N);
-  cfg.blockDim = dim3(kGnClusterThreads);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = two ? cudaLaunchKernelEx(&cfg, gn_cluster_kernel<true>, y, x, sn, x2, sn2, (int)C1, w, b, wbd, (int)C,
-                                           (int)HW, (int)G, pp, eps, silu)
-                      : cudaLaunchKernelEx(&cfg, gn_cluster_kernel<false>, y, x, sn, x2, sn2, (int)C1, w, b, wbd,
-                                           (int)C, (int)HW, (int)G, pp, eps, silu);
-  if (e != cudaSuccess) return fail(MT_ERR_LAUNCH, "group_norm cluster kernel: %s", cudaGetErrorString(e));
-  return check_launch("group_norm cluster");
-}
-
-// The channels-last bf16 path (dense [N, HW, C] in and out, C % 8 == 0): per-image partial sums,
-// finalize into a per-(image, channel) affine table, apply.  With gn_l2_group_bytes() > 0 the
-// images are processed in groups (statistics, table and apply of one group back to back).  The
-// per-image work does not depend on the grouping, so results are identical for every batch size.  x2 != nullptr: the input is the channel concatenation [x (C1 channels) | x2 (C - C1)].
+// The channels-last bf16 path (dense [N, HW, C] in and out, C % 8 == 0).  Images are processed in
+// groups of about gn_l2_group_bytes(): statistics, table and apply of one group run back to back,
+// so the apply pass re-reads x from L2 instead of HBM (one HBM read and one write per element).
+// The per-image work does not depend on the grouping, so results are identical for every batch
+// size.  x2 != nullptr: the input is the channel concatenation [x (C1 channels) | x2 (C - C1)].
 static int gn_fast_cl(__nv_bfloat16* y, const __nv_bfloat16* x, int64_t sn, const __nv_bfloat16* x2, int64_t sn2,
                       int64_t C1, const void* w, const void* b, int wbd, int64_t N, int64_t C, int64_t HW, int64_t G,
                       double eps, int silu, double* part, float2* tab, int chunks, cudaStream_t st) {
-  if (N <= 65535) {
-    int pp = 0, smem = 0;
-    const int cs = gn_cluster_plan(x2 != nullptr, C, HW, G, &pp, &smem);
-    if (cs > 0) return gn_cluster_launch(x2 != nullptr, cs, pp, smem, y, x, sn, x2, sn2, C1, w, b, wbd, N, C, HW, G, eps,
-                                         silu, st);
-  }
   const int64_t img_bytes = HW * C * 2;
   const int64_t group_bytes = gn_l2_group_bytes();
   const int64_t per = group_bytes > 0 ? std::max<int64_t>(1, group_bytes / img_bytes) : N;
