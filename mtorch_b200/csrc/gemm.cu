@@ -34,6 +34,10 @@ struct TileParams {
   int bk;  // elements per 128-byte K chunk
   int a_stages;  // B-resident variant: A-only stages behind the resident B tile
   int m_pairs;   // CTA-pair variant: row-tile pairs, ceil(num_m_tiles / 2)
+  // split K (implicit convolutions): tile t >= base tiles computes K iterations
+  // [s * k_per, (s + 1) * k_per) of tile t % base, s = t / base, and writes raw fp32 partial sums
+  // (EpiParams::part); a reduction kernel adds the splits in order and applies the epilogue
+  int k_splits, k_per;
   // implicit convolution over the channel concatenation of two sources (16-bit only): channel
   // chunks [0, c_split) come from tmA, the rest from the second source's map, passed in the tmAlo
   // slot (unused by 16-bit kernels); 0 = one source
@@ -52,6 +56,8 @@ struct EpiParams {
   float alpha; int act;
   int vec_ok;  // 16-byte aligned rows of D / C / residual
   int bias_vec;  // bias rows 16-byte aligned and bf16 / fp32: vector loads
+  float* part;   // split K: [k_splits][M rows][N] fp32 partial sums (rows in (n, p, q) order)
+  int64_t part_stride;
 };
 
 // 256-bit global accesses (sm_100): one instruction covers a whole 32-byte sector, so a warp whose
@@ -354,10 +360,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   // PAIR: tiles are row-tile pairs; CTA `crank` of the pair takes row tile 2 * pair + crank.
   const uint32_t crank = PAIR ? cluster_ctarank() : 0;
-  const int total_tiles = (PAIR ? tp.m_pairs : tp.num_m_tiles) * tp.num_n_tiles * tp.batch;
+  const int base_tiles = (PAIR ? tp.m_pairs : tp.num_m_tiles) * tp.num_n_tiles * tp.batch;
+  const int splits = tp.k_splits > 1 ? tp.k_splits : 1;
+  const int total_tiles = base_tiles * splits;
   const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  // K iterations [kb, ke) of tile t (all of them without split K)
+  auto k_range = [&](int t, int& kb, int& ke) {
+    if (splits > 1) {
+      kb = (t / base_tiles) * tp.k_per;
+      ke = min(tp.k_iters, kb + tp.k_per);
+    } else {
+      kb = 0;
+      ke = tp.k_iters;
+    }
+  };
   auto decode = [&](int t, int& b, int& mt, int& nt) {
+    t %= base_tiles;
     nt = t % tp.num_n_tiles;
     const int rest = t / tp.num_n_tiles;
     const int mcount = PAIR ? tp.m_pairs : tp.num_m_tiles;
@@ -388,7 +407,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           p0 = ((mt / tp.tiles_q) % tp.tiles_p) * tp.th;
           i0 = (mt / (tp.tiles_q * tp.tiles_p)) * tp.tn;
         }
-        for (int kk = 0; kk < tp.k_iters; ++kk) {
+        int kb, ke;
+        k_range(t, kb, ke);
+        for (int kk = kb; kk < ke; ++kk) {
           if (!mbar_wait(&empty[stage], phase ^ 1, 1, abort_flag)) break;
           // PAIR: the even CTA's barrier counts both CTAs' bytes
           if (crank == 0) mbar_arrive_expect_tx(&full[stage], PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
@@ -452,7 +473,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!mbar_wait(&tempty[buf], tph ^ 1, 2, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kk = 0; kk < tp.k_iters; ++kk) {
+        int kb, ke;
+        k_range(t, kb, ke);
+        for (int kk = kb; kk < ke; ++kk) {
           if (!mbar_wait(&full[stage], phase, 3, abort_flag)) break;
           tc_fence_after();
           const uint32_t a_addr = smem_u32(stage_base + stage * STAGE_BYTES);
@@ -462,7 +485,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = sdesc_sw128(a_addr + k * 32), bd = sdesc_sw128(b_addr + k * 32);
-            const uint32_t acc = (kk > 0 || k > 0) ? 1u : 0u;
+            const uint32_t acc = (kk > kb || k > 0) ? 1u : 0u;
             if (PAIR) {
               umma_f16_pair(d_tmem, ad, bd, idesc, acc);
             } else if (TF32) {
@@ -549,7 +572,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int64_t offR = i0 * ep.r_s0 + i1 * ep.r_s1 + i2 * ep.r_s2;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
       const bool vec = ep.vec_ok != 0;
-      if (!geglu) {
+      if (splits > 1) {
+        // split K: the raw fp32 partial sums of this K range, row (n, p, q) of split t / base
+        float* part = ep.part + (int64_t)(t / base_tiles) * ep.part_stride;
+        const int64_t m_lin = (i0 * ep.P + i1) * ep.Q + i2;
+#pragma unroll 1
+        for (int c0 = half * 32; c0 < BN; c0 += 64) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c0, r);
+          tmem_ld_wait();
+          const int64_t col0 = (int64_t)nt * BN + c0;
+          const int64_t remain = ep.N - col0;
+          const int nvalid = remain < 32 ? (int)remain : 32;
+          if (valid && nvalid > 0) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            row_store(part, MT_F32, m_lin * ep.N + col0, nvalid, true, v);
+          }
+        }
+      } else if (!geglu) {
 #pragma unroll 1
         for (int c0 = half * 32; c0 < BN; c0 += 64) {
           uint32_t r[32];
@@ -645,6 +687,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// Split-K reduction of an implicit convolution: out[n, p, q, c] = epilogue(sum_s part[s][m][c])
+// with m = (n * P + p) * Q + q, the splits added in order 0..S-1 (fixed, so results do not depend
+// on the batch), then the GEMM epilogue's order: alpha, bias (per column or per image), activation,
+// residual.  One thread per 8 consecutive columns.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* part, int splits, int64_t stride,
+                                                            int64_t rows, int64_t N, const EpiParams ep) {
+  const int64_t n8 = N / 8;
+  const int64_t total = rows * n8;
+  const int64_t PQ = ep.P * ep.Q;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / n8, c = (i - m * n8) * 8;
+    float v[8];
+    {
+      const float4* q = reinterpret_cast<const float4*>(part + m * N + c);
+      const float4 a = q[0], b = q[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    for (int s = 1; s < splits; ++s) {
+      const float4* q = reinterpret_cast<const float4*>(part + s * stride + m * N + c);
+      const float4 a = q[0], b = q[1];
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+    const int64_t n = m / PQ, rem = m - n * PQ, pp = rem / ep.Q, qq = rem - pp * ep.Q;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= ep.alpha;
+    if (ep.bias) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += load_as_f32(ep.bias, n * ep.bias_bstride + c + j, ep.bias_dtype);
+    }
+    if (ep.act == MT_EPI_GELU) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = gelu_f(v[j]);
+    } else if (ep.act == MT_EPI_SILU) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = silu_f(v[j]);
+    }
+    if (ep.res) {
+      const int64_t offR = n * ep.r_s0 + pp * ep.r_s1 + qq * ep.r_s2 + c;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += load_as_f32(ep.res, offR + j, ep.out_dtype);
+    }
+    const int64_t offD = n * ep.d_s0 + pp * ep.d_s1 + qq * ep.d_s2 + c;
+    if (ep.vec_ok && (ep.out_dtype == MT_BF16 || ep.out_dtype == MT_F16)) {
+      uint4 w;
+      uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        wp[j] = ep.out_dtype == MT_BF16 ? pack_bf16x2(v[2 * j], v[2 * j + 1]) : pack_f16x2(v[2 * j], v[2 * j + 1]);
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(ep.D) + offD) = w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) store_from_f32(ep.D, offD + j, ep.out_dtype, v[j]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host side.
 
 struct GemmLaunch {
@@ -678,7 +777,8 @@ static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
     if (rc) return rc;
     attr_set[dev & 63] = true;
   }
-  const int64_t tiles = (int64_t)L.tp.num_m_tiles * L.tp.num_n_tiles * L.tp.batch;
+  const int64_t tiles =
+      (int64_t)L.tp.num_m_tiles * L.tp.num_n_tiles * L.tp.batch * std::max(1, L.tp.k_splits);
   if (tiles > 0x7fffffffLL) return fail(MT_ERR_UNSUPPORTED, "gemm: too many tiles");
   int grid = (int)std::min<int64_t>(tiles, num_sms());
   if (BRES) grid = num_sms() / L.tp.num_n_tiles * L.tp.num_n_tiles;  // one column tile per CTA
@@ -736,7 +836,7 @@ static bool use_pair(GemmLaunch& L) {
     const char* e = getenv("MT_GEMM_PAIR");
     return !(e && e[0] == '1');
   }();
-  if (off || L.kind == MT_F32 || !L.b_ptr || L.tp.c_split > 0) return false;
+  if (off || L.kind == MT_F32 || !L.b_ptr || L.tp.c_split > 0 || L.tp.k_splits > 1) return false;
   if (L.bn != 128 && L.bn != 160 && L.bn != 256) return false;
   if (L.tp.num_m_tiles < 2) return false;
   L.tp.m_pairs = (L.tp.num_m_tiles + 1) / 2;
@@ -1076,8 +1176,25 @@ struct ConvCat {
   int64_t c1;
 };
 
+// K splits of an implicit 16-bit convolution: a function of the per-image output size and the
+// reduction length only (never of the batch), so a sample's result is the same at every batch size.
+// Small images (the UNet's 16x16 and 8x8 levels) have few output rows per image; splitting K keeps
+// the GPU busy at small batches and evens out the last wave at large ones.  MT_CONV_SPLITK=0 turns
+// it off.
+static int conv_k_splits(const mt_conv2d_desc& d, int64_t k_iters) {
+  static const bool off = [] {
+    const char* e = getenv("MT_CONV_SPLITK");
+    return e && e[0] == '0';
+  }();
+  if (off || d.dtype == MT_F32 || d.K % 8 != 0 || k_iters < 64) return 1;
+  const int64_t pq = d.P * d.Q;
+  if (pq <= 64) return 4;
+  if (pq <= 256) return 2;
+  return 1;
+}
+
 static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream_t st, GemmLaunch* L,
-                     const ConvCat* cat = nullptr) {
+                     const ConvCat* cat = nullptr, bool allow_split = false) {
   const int es = dtype_size(d.dtype);
   const bool tf32 = d.dtype == MT_F32;
   const bool implicit = conv_implicit_ok(d);
@@ -1167,6 +1284,13 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
       if (rc) return rc;
     }
   }
+  // split-K partial sums (decided from the per-image shape; see conv_k_splits)
+  float* part = nullptr;
+  int splits = 1;
+  if (allow_split && implicit && !tf32) {
+    splits = conv_k_splits(d, d.R * d.S * (d.C / (128 / es)));
+    if (splits > 1) part = (float*)ws.take((size_t)splits * d.N * d.P * d.Q * d.K * sizeof(float));
+  }
   if (!run) return MT_OK;
 
   L->kind = d.dtype;
@@ -1225,7 +1349,14 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
     rc = map_kmajor(&L->a, d.dtype, a, Kg, M, 1, Kg, 0, kBM);
     if (!rc && tf32) rc = map_kmajor(&L->alo, MT_F32, alo, Kg, M, 1, Kg, 0, kBM);
   }
-  if (!tf32) L->bn = narrow_bn(L->bn, d.K, tp.num_m_tiles, false);
+  tp.k_splits = 1;
+  tp.k_per = tp.k_iters;
+  if (splits > 1) {
+    tp.k_splits = splits;
+    tp.k_per = (tp.k_iters + splits - 1) / splits;
+  } else if (!tf32) {
+    L->bn = narrow_bn(L->bn, d.K, tp.num_m_tiles, false);
+  }
   tp.num_n_tiles = (int)((d.K + L->bn - 1) / L->bn);
   if (!rc) rc = map_kmajor(&L->b, d.dtype, wp, Kg, d.K, 1, Kg, 0, L->bn);
   L->b_ptr = wp; L->b_K = Kg; L->b_rows = d.K; L->b_batch = 1; L->b_pitch = Kg; L->b_bstride = 0;
@@ -1249,7 +1380,20 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   const int oes = dtype_size(d.out_dtype);
   ep.vec_ok = aligned16(yout) && (d.K * oes) % 16 == 0 && (!res || aligned16(res));
   ep.bias_vec = bias_vec_ok(d.bias, d.bias_dtype, d.bias_batch_stride);
+  ep.part = part;
+  ep.part_stride = d.N * d.P * d.Q * d.K;
   return MT_OK;
+}
+
+// The reduction that completes a split-K convolution (no-op otherwise).
+static int finish_split(const GemmLaunch& L, cudaStream_t st) {
+  if (L.tp.k_splits <= 1) return MT_OK;
+  const EpiParams& ep = L.ep;
+  const int64_t rows = ep.M * ep.P * ep.Q;
+  const int64_t total = rows * (ep.N / 8);
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
+  splitk_reduce_kernel<<<blocks, 256, 0, st>>>(ep.part, L.tp.k_splits, ep.part_stride, rows, ep.N, ep);
+  return check_launch("splitk_reduce");
 }
 
 static int validate_conv(const mt_conv2d_desc& d) {
@@ -1273,7 +1417,7 @@ static int validate_conv(const mt_conv2d_desc& d) {
 size_t conv_workspace(const mt_conv2d_desc& d) {
   if (validate_conv(d) != MT_OK) return 0;
   WsCursor ws{nullptr, 0};
-  plan_conv(d, ws, false, nullptr, nullptr);
+  plan_conv(d, ws, false, nullptr, nullptr, nullptr, true);
   return ws.off;
 }
 
@@ -1286,9 +1430,10 @@ int run_conv2d(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStream_t
     return fail(MT_ERR_WORKSPACE, "conv2d: workspace of %zu bytes required", need);
   WsCursor ws{(char*)wsp, 0};
   GemmLaunch L{};
-  rc = plan_conv(d, ws, true, st, &L);
+  rc = plan_conv(d, ws, true, st, &L, nullptr, true);
   if (rc) return rc;
   rc = dispatch(L, st);
+  if (!rc) rc = finish_split(L, st);
   if (rc) return rc;
   if (L.ep.D != d.y) {
     int64_t cl[4] = {d.P * d.Q * d.K, 1, d.Q * d.K, d.K};
@@ -1305,7 +1450,7 @@ size_t conv_cat_workspace(const mt_conv2d_desc& d, const void* x2, const int64_t
   for (int i = 0; i < 4; ++i) cat.x2_strides[i] = x2_strides[i];
   cat.c1 = c1;
   WsCursor ws{nullptr, 0};
-  plan_conv(d, ws, false, nullptr, nullptr, &cat);
+  plan_conv(d, ws, false, nullptr, nullptr, &cat, true);
   return ws.off;
 }
 
@@ -1335,9 +1480,10 @@ int run_conv2d_cat(const mt_conv2d_desc& d, const void* x2, const int64_t* x2_st
   cat.c1 = c1;
   WsCursor ws{(char*)wsp, 0};
   GemmLaunch L{};
-  rc = plan_conv(d, ws, true, st, &L, &cat);
+  rc = plan_conv(d, ws, true, st, &L, &cat, true);
   if (rc) return rc;
   rc = dispatch(L, st);
+  if (!rc) rc = finish_split(L, st);
   if (rc) return rc;
   if (L.ep.D != d.y) {
     int64_t cl[4] = {d.P * d.Q * d.K, 1, d.Q * d.K, d.K};

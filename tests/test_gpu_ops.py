@@ -501,3 +501,26 @@ def test_skip_concat_fused_consumers_bitwise(n, c1, c2, hw, silu):
     check(got, oracle.conv2d_f32(cat.numpy(), wc.numpy(), bc.numpy()), BF16_RTOL)
     w3 = cu(rng.standard_normal((K, C, 3, 3)).astype(np.float32) * (9 * C) ** -0.5, "bfloat16")
     np.testing.assert_array_equal(mt.ops.conv2d_cat(a, b, w3, None, 1, 1).numpy(), mt.conv2d(cat, w3, None, 1, 1).numpy())
+
+
+@pytest.mark.parametrize("c,k,hw,stride", [(1280, 1280, 8, 1), (2560, 1280, 8, 1), (1280, 1280, 16, 1), (640, 640, 16, 1),
+                                           (1280, 1280, 16, 2)])
+def test_conv_split_k_deep_levels(c, k, hw, stride):
+    """The 16x16 and 8x8 convolutions split their reduction (2 or 4 ways, chosen from the per-image
+    shape only) and add the fp32 partial sums in a fixed order: within the bf16 tolerance of the
+    oracle, with the per-image bias and residual epilogue, and bitwise independent of the batch."""
+    rng = np.random.default_rng(c + hw)
+    n = 3
+    x = rng.standard_normal((n, c, hw, hw)).astype(np.float32)
+    w = (rng.standard_normal((k, c, 3, 3)) * (9 * c) ** -0.5).astype(np.float32)
+    bias = rng.standard_normal((n, k)).astype(np.float32)
+    p = hw // stride
+    res = rng.standard_normal((n, k, p, p)).astype(np.float32)
+    xd = cu(x, "bfloat16").contiguous(memory_format=mt.channels_last)
+    rd = cu(res, "bfloat16").contiguous(memory_format=mt.channels_last)
+    wd = cu(w, "bfloat16")
+    got = mt.ops.conv2d(xd, wd, cu(bias), stride, 1, bias_batch_stride=k, residual=rd).numpy()
+    ref = np.stack([oracle.conv2d_f32(bf16_round(x)[i:i + 1], bf16_round(w), bias[i], stride, 1)[0] for i in range(n)])
+    check(got, ref + bf16_round(res), BF16_RTOL)
+    one = mt.ops.conv2d(xd[1:2], wd, cu(bias[1:2]), stride, 1, bias_batch_stride=k, residual=rd[1:2]).numpy()
+    np.testing.assert_array_equal(one[0], got[1])
