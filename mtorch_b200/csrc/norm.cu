@@ -251,6 +251,21 @@ int launch_layer_norm(void* y, int yd, const void* x, int xd, const void* w, con
     const unsigned g32 = (unsigned)((rows + 7) / 8), g16 = (unsigned)((rows + 15) / 16);
     auto* yy = (__nv_bfloat16*)y;
     auto* xx = (const __nv_bfloat16*)x;
+    // rows of 5 * LPR vectors (the UNet's 320 / 640 / 1280 columns): 5 vectors per lane, no idle lanes
+    static const bool v5 = [] {
+      const char* e = getenv("MT_LN_V5");
+      return e && e[0] == '1';
+    }();
+    if (v5 && nv % 5 == 0 && (nv / 5 == 8 || nv / 5 == 16 || nv / 5 == 32)) {
+      const unsigned g8 = (unsigned)((rows + 31) / 32);
+      if (nv / 5 == 8)
+        layer_norm_bf16_sub_kernel<5, 8><<<g8, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+      else if (nv / 5 == 16)
+        layer_norm_bf16_sub_kernel<5, 16><<<g16, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+      else
+        layer_norm_bf16_sub_kernel<5, 32><<<g32, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+      return check_launch("layer_norm_bf16_warp");
+    }
     if (nv <= 16)
       layer_norm_bf16_sub_kernel<1, 16><<<g16, 256, 0, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
     else if (nv <= 32)
