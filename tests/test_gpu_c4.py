@@ -134,7 +134,8 @@ def test_c4_up_block_resnet(c4_run):
     device (fp32 per-thread partials combined in double) does not."""
     net, rec, _ = c4_run
     blk = net.up[0]
-    (x, tsilu), got = rec["up_res"]
+    (h, tsilu, skip), got = rec["up_res"]  # the block's input is cat([h, skip], dim=1)
+    x = np.concatenate([h, skip], axis=1)
     assert x.shape == (1, 2560, 8, 8)
     h = oracle.silu_f32(oracle.group_norm_f32(x, 32, npw(blk.norm1.weight), npw(blk.norm1.bias)))
     h = oracle.conv2d_f32(h, npw(blk.conv1.weight), npw(blk.conv1.bias), 1, 1)
