@@ -1186,7 +1186,17 @@ static int conv_k_splits(const mt_conv2d_desc& d, int64_t k_iters) {
     const char* e = getenv("MT_CONV_SPLITK");
     return e && e[0] == '0';
   }();
-  if (off || d.dtype == MT_F32 || d.K % 8 != 0 || k_iters < 64) return 1;
+  if (off || d.K % 8 != 0) return 1;
+  if (d.dtype == MT_F32) {
+    // 3xTF32: the tensor core's fp32 accumulation is biased (measured: relative error growing
+    // linearly with K, 1.6e-4 at K = 23040 even for exactly representable tf32 inputs), so the
+    // reduction is cut into chunks of about 1024 elements (32 iterations of 32) whose sums are
+    // added in IEEE fp32 by the split reduction: relative error ~sqrt(K * 1024) / K of the
+    // unchunked figure (measured 8.6e-5 -> see the fp32 conv tests).
+    const int64_t s = std::min<int64_t>(16, (k_iters + 31) / 32);
+    return s >= 2 ? (int)s : 1;
+  }
+  if (k_iters < 64) return 1;
   const int64_t pq = d.P * d.Q;
   if (pq <= 64) return 4;
   if (pq <= 256) return 2;
@@ -1287,7 +1297,7 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   // split-K partial sums (decided from the per-image shape; see conv_k_splits)
   float* part = nullptr;
   int splits = 1;
-  if (allow_split && implicit && !tf32) {
+  if (allow_split && implicit) {
     splits = conv_k_splits(d, d.R * d.S * (d.C / (128 / es)));
     if (splits > 1) part = (float*)ws.take((size_t)splits * d.N * d.P * d.Q * d.K * sizeof(float));
   }
@@ -1566,7 +1576,7 @@ size_t conv_up2x_workspace(const mt_conv2d_desc& d) {
   // with packed low parts present a plan needs no per-call weight split
   mt_conv2d_desc e = up2x_parity_desc(d, 0, d.w, tf32 ? reinterpret_cast<const float*>(d.w) : nullptr);
   WsCursor ws{nullptr, 0};
-  plan_conv(e, ws, false, nullptr, nullptr);
+  plan_conv(e, ws, false, nullptr, nullptr, nullptr, true);
   return pack + 256 + ws.off;
 }
 
@@ -1601,10 +1611,11 @@ int run_conv2d_up2x(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStr
     const mt_conv2d_desc e = up2x_parity_desc(d, par, wp, wlo);
     WsCursor wsp2{(char*)wsp, base};
     GemmLaunch L{};
-    rc = plan_conv(e, wsp2, true, st, &L);
+    rc = plan_conv(e, wsp2, true, st, &L, nullptr, true);
     if (rc) return rc;
     if (L.ep.D != e.y) return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: output layout");
     rc = dispatch(L, st);
+    if (!rc) rc = finish_split(L, st);
     if (rc) return rc;
   }
   return MT_OK;
