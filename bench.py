@@ -392,7 +392,7 @@ def run_ours(args):
             roofline["exp_unit"] = {"achieved": exp_rate, "peak": exp_peak, "unit": "exp2/s",
                                     "frac": exp_rate / exp_peak, "sm_mhz": mhz}
         base = None
-        if world == 1 and gb == BATCH:  # the reference CPU path on this box's host cores, bounded sample
+        if world == 1 and gb == BATCH and not args.no_cpu_baseline:  # reference CPU path, bounded sample
             try:
                 procs = os.cpu_count() or 1
                 times, smp = cpu_sampled_steps(procs, 1, 2)
@@ -583,7 +583,7 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH, help="samples for --kernel / --workload runs")
     ap.add_argument("--global-batch", type=int, default=BATCH,
                     help="UNet bench: samples of the whole job (64 = config C5; smaller for profiling)")
-    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the reference CPU timing of --workload c4")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the reference CPU timing (cpu_baseline)")
     ap.add_argument("--workload", choices=["sampler", "vae", "text", "c4"], default=None,
                     help="time one of the workloads around the UNet instead of the UNet step")
     args = ap.parse_args()
