@@ -128,10 +128,9 @@ def _f64_resnet(x, tsilu, blk):
 
 
 def test_c4_up_block_resnet(c4_run):
-    """Against the oracle (the reference's arithmetic, whose GroupNorm sums x and x^2 in fp32,
-    tensor.cpp:18797-18841) at 2e-4, and against the exact float64 composition at 1e-4: over 5120-
-    element groups the reference's fp32 sums carry ~1e-4 of relative error themselves, which the
-    device (fp32 per-thread partials combined in double) does not."""
+    """Against the oracle (the reference's arithmetic) and against an exact float64 composition,
+    both at the fp32 bar 1e-4: the block's convolutions reduce over K = 23040 and 11520, where the
+    fp32 path must add its partial sums in IEEE arithmetic (the split reduction) to stay there."""
     net, rec, _ = c4_run
     blk = net.up[0]
     (h, tsilu, skip), got = rec["up_res"]  # the block's input is cat([h, skip], dim=1)
@@ -145,7 +144,7 @@ def test_c4_up_block_resnet(c4_run):
     ref = h + oracle.conv2d_f32(x, npw(blk.conv_shortcut.weight), npw(blk.conv_shortcut.bias))
     exact = _f64_resnet(x, tsilu, blk)
     print(f"C4 oracle (reference arithmetic) vs exact: {np.abs(ref - exact).max() / np.abs(exact).max():.3e}")
-    check("up-block ResNet 2560->1280 at 8x8 vs oracle", got, ref, 2e-4)
+    check("up-block ResNet 2560->1280 at 8x8 vs oracle", got, ref)
     check("up-block ResNet 2560->1280 at 8x8 vs exact float64", got, exact)
 
 

@@ -73,7 +73,7 @@ def test_spatial_transformer_fp32():
     t = t + oracle.linear_f32(g, npw(b.ff.out.weight), npw(b.ff.out.bias))
     t = oracle.linear_f32(t, npw(st.proj_out.weight), npw(st.proj_out.bias))
     ref = t.reshape(n, 6, 6, c).transpose(0, 3, 1, 2) + x
-    check(got, ref, 2e-4)
+    check(got, ref)
 
 
 def test_ddim_step_matches_reference_formula():
