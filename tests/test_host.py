@@ -109,3 +109,26 @@ def test_module_init_is_seeded_and_deterministic():
     np.testing.assert_array_equal(a, b)
     bound = np.sqrt(3.0) * np.sqrt(2.0 / 6.0) / np.sqrt(16)
     assert np.abs(a).max() <= bound
+
+
+def test_reference_binding_installs_and_leaves_the_cpu_path_alone():
+    """mtorch_b200.compat.install patches the reference package in place: `cuda` becomes a device
+    name its Module.to accepts, the functional ops dispatch on device tensors, and calls on the
+    reference's own CPU tensors still run the reference's code (same results as before)."""
+    import oracle
+
+    m = oracle.ref()
+    if m is None:
+        pytest.skip("the reference is not built into oracle/_ref")
+    F = m.nn.functional
+    m.manual_seed(3)
+    x, w = m.randn(1, 4, 5, 5), m.randn(6, 4, 3, 3)
+    before = F.conv2d(x, w, None, 1, 1).numpy()
+    from mtorch_b200 import compat
+
+    compat.install(m)
+    compat.install(m)  # idempotent
+    assert "cuda" in m._DEVICE_NAMES
+    assert m.nn.functional.conv2d.__mtorch_b200_reference__ is not None
+    np.testing.assert_array_equal(F.conv2d(x, w, None, 1, 1).numpy(), before)
+    np.testing.assert_array_equal(m.cat([x, x], dim=1).numpy()[:, 4:], x.numpy())
