@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_cl_kernel(const void* x
 //
 // TWO: the input is the channel concatenation of x (C1 channels per pixel, image stride sn) and
 // x2 (C - C1 channels, image stride sn2), read in place.
-template <bool TWO = false>
+template <bool TWO = false, int U = 4>
 __global__ void __launch_bounds__(kGnThreads, 5) gn_partial_cl_bf16x8_kernel(const __nv_bfloat16* x, int64_t sn,
                                                                           int64_t C, int64_t HW, int64_t G,
                                                                           int chunks, double* part,
@@ -383,15 +383,15 @@ __global__ void __launch_bounds__(kGnThreads, 5) gn_partial_cl_bf16x8_kernel(con
         pitch = C - C1;
       }
     }
-    for (int p = (int)(p0 + lane); p < p1; p += 4 * (int)lanes) {
-      uint4 u[4];
+    for (int p = (int)(p0 + lane); p < p1; p += U * (int)lanes) {
+      uint4 u[U];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < U; ++k) {
         const int pp = p + k * (int)lanes;
         u[k] = pp < p1 ? *reinterpret_cast<const uint4*>(xv + (int64_t)pp * pitch) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < U; ++k) {
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[k]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -686,6 +686,17 @@ static int64_t gn_l2_group_bytes() {
   return v;
 }
 
+// Pixels per statistics chunk of the vectorised channels-last path: 40960 / C (128 at 320
+// channels, 32 at 1280; between 16 and 128), or MT_GN_PX.  A function of C only, so the
+// reduction order never depends on the batch.
+static int64_t gn_chunk_px(int64_t C) {
+  static const int64_t px_env = [] {
+    const char* e = getenv("MT_GN_PX");
+    return (int64_t)(e ? atoi(e) : 0);
+  }();
+  return px_env > 0 ? px_env : std::max<int64_t>(16, std::min<int64_t>(128, 40960 / C));
+}
+
 static int gn_chunks(int64_t C, int64_t HW, int64_t G, bool cl) {
   int64_t chunks = cl ? (HW + 63) / 64 : (C / G * HW + 4095) / 4096;
   if (chunks < 1) chunks = 1;
@@ -734,12 +745,19 @@ static int gn_fast_cl(__nv_bfloat16* y, const __nv_bfloat16* x, int64_t sn, cons
     const __nv_bfloat16* xg = x + n0 * sn;
     const __nv_bfloat16* x2g = x2 ? x2 + n0 * sn2 : nullptr;
     const size_t sh = 2 * slots * sizeof(float);
-    if (x2)
-      gn_partial_cl_bf16x8_kernel<true><<<dim3(chunks, (unsigned)nc), kGnThreads, sh, st>>>(
-          xg, sn, C, HW, G, chunks, part_g, x2g, sn2, C1);
+    static const bool u8 = [] {
+      const char* e = getenv("MT_GN_UNROLL");
+      return e && atoi(e) == 8;
+    }();
+    const dim3 grid(chunks, (unsigned)nc);
+    if (x2 && u8)
+      gn_partial_cl_bf16x8_kernel<true, 8><<<grid, kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks, part_g, x2g, sn2, C1);
+    else if (x2)
+      gn_partial_cl_bf16x8_kernel<true, 4><<<grid, kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks, part_g, x2g, sn2, C1);
+    else if (u8)
+      gn_partial_cl_bf16x8_kernel<false, 8><<<grid, kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks, part_g);
     else
-      gn_partial_cl_bf16x8_kernel<false><<<dim3(chunks, (unsigned)nc), kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks,
-                                                                                           part_g);
+      gn_partial_cl_bf16x8_kernel<false, 4><<<grid, kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks, part_g);
     int rc = check_launch("group_norm partial");
     if (rc) return rc;
     gn_finalize_table_kernel<<<(unsigned)((nc * G * 32 + 255) / 256), 256, 0, st>>>(
@@ -777,7 +795,7 @@ int launch_group_norm(void* y, int yd, const int64_t* ys, const void* x, int xd,
   const bool vec_in = cl && xd == MT_BF16 && C % 8 == 0 && (uintptr_t)x % 16 == 0 && (xs[0] * 2) % 16 == 0;
   // the vectorised channels-last path walks chunks of 40960 / C pixels (128 at 320 channels, 32 at
   // 1280; between 16 and 128): long enough CTAs for narrow images, enough CTAs for wide ones
-  const int64_t gn_px = std::max<int64_t>(16, std::min<int64_t>(128, 40960 / C));
+  const int64_t gn_px = gn_chunk_px(C);
   const int chunks = vec_in ? (int)std::min<int64_t>(kGnMaxChunks, (HW + gn_px - 1) / gn_px) : gn_chunks(C, HW, G, cl);
   const bool ycl = (ys[1] == 1 && ys[2] == C && ys[0] == HW * C);
   const bool fast = vec_in && ycl && xs[0] == HW * C && yd == MT_BF16 && (uintptr_t)y % 16 == 0 &&
@@ -847,7 +865,7 @@ int launch_group_norm_cat(void* y, int yd, const int64_t* ys, const void* x1, co
   if (!ws || ws_bytes < group_norm_workspace(N, C, HW, G)) return fail(MT_ERR_WORKSPACE, "group_norm_cat: workspace");
   double* part = (double*)ws;
   float2* tab = (float2*)((char*)ws + gn_part_bytes(N, G) + gn_stats_bytes(N, G));
-  const int64_t gn_px = std::max<int64_t>(16, std::min<int64_t>(128, 40960 / C));
+  const int64_t gn_px = gn_chunk_px(C);
   const int chunks = (int)std::min<int64_t>(kGnMaxChunks, (HW + gn_px - 1) / gn_px);
   return gn_fast_cl((__nv_bfloat16*)y, (const __nv_bfloat16*)x1, xs1[0], (const __nv_bfloat16*)x2, xs2[0], C1, w, b,
                     wbd, N, C, HW, G, eps, silu, part, tab, chunks, st);
