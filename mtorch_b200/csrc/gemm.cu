@@ -1411,7 +1411,11 @@ static int validate_conv(const mt_conv2d_desc& d) {
     return fail(MT_ERR_INVALID, "conv2d: bad sizes");
   if (d.stride_h <= 0 || d.stride_w <= 0 || d.dil_h <= 0 || d.dil_w <= 0 || d.pad_h < 0 || d.pad_w < 0)
     return fail(MT_ERR_INVALID, "conv2d: bad stride / dilation / padding");
-  if (d.groups != 1) return fail(MT_ERR_UNSUPPORTED, "conv2d: groups != 1 is not implemented on the device path");
+  if (d.groups < 1 || d.C % d.groups || d.K % d.groups)
+    return fail(MT_ERR_INVALID, "conv2d: channels %lld / %lld not divisible by groups %d", (long long)d.C,
+                (long long)d.K, d.groups);
+  if (d.groups > 1 && d.w_packed)
+    return fail(MT_ERR_UNSUPPORTED, "conv2d: grouped convolutions take the unpacked [K, C/groups, R, S] weight");
   if (d.dtype != MT_F32 && d.dtype != MT_BF16 && d.dtype != MT_F16)
     return fail(MT_ERR_UNSUPPORTED, "conv2d: dtype %d", d.dtype);
   if (d.out_dtype != MT_F32 && d.out_dtype != MT_BF16 && d.out_dtype != MT_F16)
@@ -1424,8 +1428,28 @@ static int validate_conv(const mt_conv2d_desc& d) {
   return MT_OK;
 }
 
+// Group g of a grouped convolution (groups > 1, `conv2d` tensor.cpp:26498-26543): input
+// channels [g*C/G, (g+1)*C/G), weight rows and output channels [g*K/G, (g+1)*K/G), as a plain
+// convolution on views of the same buffers (the weight in its unpacked [K, C/G, R, S] layout).
+static mt_conv2d_desc conv_group_desc(const mt_conv2d_desc& d, int g) {
+  mt_conv2d_desc e = d;
+  const int64_t cg = d.C / d.groups, kg = d.K / d.groups;
+  const int es = dtype_size(d.dtype), oes = dtype_size(d.out_dtype);
+  e.groups = 1;
+  e.C = cg;
+  e.K = kg;
+  e.x = static_cast<const char*>(d.x) + (int64_t)g * cg * d.x_strides[1] * es;
+  e.w = static_cast<const char*>(d.w) + (int64_t)g * kg * cg * d.R * d.S * es;
+  e.w_lo = nullptr;
+  if (d.bias) e.bias = static_cast<const char*>(d.bias) + (int64_t)g * kg * dtype_size(d.bias_dtype);
+  if (d.residual) e.residual = static_cast<const char*>(d.residual) + (int64_t)g * kg * d.res_strides[1] * oes;
+  e.y = static_cast<char*>(d.y) + (int64_t)g * kg * d.y_strides[1] * oes;
+  return e;
+}
+
 size_t conv_workspace(const mt_conv2d_desc& d) {
   if (validate_conv(d) != MT_OK) return 0;
+  if (d.groups > 1) return conv_workspace(conv_group_desc(d, 0));  // the same for every group
   WsCursor ws{nullptr, 0};
   plan_conv(d, ws, false, nullptr, nullptr, nullptr, true);
   return ws.off;
@@ -1435,6 +1459,14 @@ int run_conv2d(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStream_t
   int rc = validate_conv(d);
   if (rc) return rc;
   if (d.N == 0 || d.P <= 0 || d.Q <= 0) return MT_OK;
+  if (d.groups > 1) {
+    // one plain convolution per group, stream-ordered on the same workspace
+    for (int g = 0; g < d.groups; ++g) {
+      rc = run_conv2d(conv_group_desc(d, g), wsp, ws_bytes, st);
+      if (rc) return rc;
+    }
+    return MT_OK;
+  }
   const size_t need = conv_workspace(d);
   if (need > 0 && (!wsp || ws_bytes < need))
     return fail(MT_ERR_WORKSPACE, "conv2d: workspace of %zu bytes required", need);

@@ -215,7 +215,7 @@ class Conv2d(Module):
         (the reference keeps version-keyed fp16 weight caches the same way, tensor.h:64-78)."""
         w = self.weight
         key = (id(w), w._version, w.dtype.name, str(w.device))
-        if w.device.type != "cuda":
+        if w.device.type != "cuda" or self.groups != 1:  # grouped convs take the unpacked weight
             return None
         if self._packed is None or self._packed[0] != key:
             self._packed = (key, ops.pack_conv_weight(w))

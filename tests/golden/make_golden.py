@@ -59,6 +59,7 @@ conv_cases = {
     "conv_s2": dict(shape=(1, 4, 10, 10), w=(5, 4, 3, 3), stride=2, padding=1, dilation=1, groups=1),
     "conv_d2": dict(shape=(1, 3, 11, 11), w=(4, 3, 3, 3), stride=1, padding=2, dilation=2, groups=1),
     "conv_1x1": dict(shape=(2, 16, 5, 7), w=(8, 16, 1, 1), stride=1, padding=0, dilation=1, groups=1),
+    "conv_g4": dict(shape=(2, 8, 7, 7), w=(12, 2, 3, 3), stride=1, padding=1, dilation=1, groups=4),
 }
 for seed, (name, c) in enumerate(conv_cases.items(), start=10):
     mtorch.manual_seed(seed)

@@ -258,7 +258,7 @@ def test_linear_batch_independent():
 # conv2d
 
 
-@pytest.mark.parametrize("name", ["conv_p1", "conv_s2", "conv_d2", "conv_1x1"])
+@pytest.mark.parametrize("name", ["conv_p1", "conv_s2", "conv_d2", "conv_1x1", "conv_g4"])
 def test_conv2d_fp32_golden(golden, name):
     s, p, d, g = (int(v) for v in golden[f"{name}.params"])
     got = mt.conv2d(cu(golden[f"{name}.x"]), cu(golden[f"{name}.w"]), cu(golden[f"{name}.b"]), s, p, d, g).numpy()
@@ -524,3 +524,20 @@ def test_conv_split_k_deep_levels(c, k, hw, stride):
     check(got, ref + bf16_round(res), BF16_RTOL)
     one = mt.ops.conv2d(xd[1:2], wd, cu(bias[1:2]), stride, 1, bias_batch_stride=k, residual=rd[1:2]).numpy()
     np.testing.assert_array_equal(one[0], got[1])
+
+
+@pytest.mark.parametrize("dtype,groups", [("float32", 2), ("bfloat16", 4), ("bfloat16", 64)])
+def test_conv2d_grouped(dtype, groups):
+    """groups > 1 (tensor.cpp:26498-26543): one convolution per group, against the oracle's grouped
+    loop; groups == channels is the depthwise case."""
+    rng = np.random.default_rng(groups)
+    x = rng.standard_normal((2, 64, 12, 12)).astype(np.float32)
+    w = (rng.standard_normal((128, 64 // groups, 3, 3)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(128).astype(np.float32)
+    rd = (lambda a: a) if dtype == "float32" else bf16_round  # noqa: E731
+    ref = oracle.conv2d_f32(rd(x), rd(w), rd(b), 1, 1, 1, groups)
+    got = mt.conv2d(cu(x, dtype), cu(w, dtype), cu(b, dtype), 1, 1, 1, groups)
+    check(got.float().numpy(), ref, FP32_RTOL if dtype == "float32" else BF16_RTOL)
+    m = mt.nn.Conv2d(64, 128, 3, padding=1, groups=groups, device="cuda", dtype=dtype)
+    y = m(cu(x, dtype).contiguous(memory_format=mt.channels_last))
+    assert tuple(y.shape) == (2, 128, 12, 12)

@@ -33,7 +33,7 @@ def test_linear(golden):
     close(oracle.linear_f32(golden["linear.x"], golden["linear.w"], golden["linear.b"]), golden["linear.y"], 0, 0)
 
 
-@pytest.mark.parametrize("name", ["conv_p1", "conv_s2", "conv_d2", "conv_1x1"])
+@pytest.mark.parametrize("name", ["conv_p1", "conv_s2", "conv_d2", "conv_1x1", "conv_g4"])
 def test_conv(golden, name):
     s, p, d, g = golden[f"{name}.params"]
     y = oracle.conv2d_f32(golden[f"{name}.x"], golden[f"{name}.w"], golden[f"{name}.b"], int(s), int(p), int(d), int(g))
