@@ -37,7 +37,19 @@ struct FaParams {
   int stages;    // KV stages (K and V tiles together); the lazy kernel: K stages
   int stages_v;  // lazy kernel: V stages
   int causal;    // fa_sm100_kernel: key j of query i is masked when j > i (top-left aligned)
+  // fa_sm100_kernel: attention mask, 0 none / 1 bool (uint8, nonzero keeps) / 2 additive in
+  // mask_dtype, indexed with element strides ms over (b, h, query, key)
+  const void* mask;
+  int mask_kind, mask_dtype;
+  int64_t ms[4];
 };
+
+// log2-domain additive term of the mask for (query row, key) at element offset `off`: 0 / -inf
+// for a bool mask, value * log2(e) for an additive one.
+__device__ __forceinline__ float fa_mask_add(const FaParams& p, int64_t off) {
+  if (p.mask_kind == 1) return static_cast<const uint8_t*>(p.mask)[off] ? 0.f : -INFINITY;
+  return load_as_f32(p.mask, off, p.mask_dtype) * 1.4426950408889634f;
+}
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -295,9 +307,17 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
       int kvalid = min(kFaBN, p.Sk - j * kFaBN);
       if (p.causal) kvalid = max(0, min(kvalid, qbase + x * kFaBM + row - j * kFaBN + 1));
       const bool full = kvalid == kFaBN;
+      // masked rows: element offset of (b, h, query, first key of the tile); rows past Sq read
+      // no mask
+      const int qrow = qbase + x * kFaBM + row;
+      const bool masked = p.mask_kind != 0 && qrow < p.Sq;
+      const int64_t moff = masked ? (int64_t)b * p.ms[0] + (int64_t)h * p.ms[1] + (int64_t)qrow * p.ms[2] +
+                                        (int64_t)j * kFaBN * p.ms[3]
+                                  : 0;
       // TMEM reads are issued 64 columns at a time before one tcgen05.wait::ld, so the load
       // latency is paid twice per pass rather than once per 16 columns.
-      // pass 1: row max of the raw scores (the scale is positive)
+      // pass 1: row max of the raw scores (the scale is positive); masked rows: of the scaled
+      // scores plus the mask in the log2 domain
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c0 = 0; c0 < kFaBN; c0 += 64) {
@@ -305,7 +325,12 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
         tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
-        if (full) {
+        if (masked) {
+#pragma unroll 4
+          for (int i = 0; i < 64; ++i)
+            if (c0 + i < kvalid)
+              mx = fmaxf(mx, __uint_as_float(r[i]) * sl + fa_mask_add(p, moff + (int64_t)(c0 + i) * p.ms[3]));
+        } else if (full) {
           mx = fmaxf(mx, max64(r));
         } else {
 #pragma unroll
@@ -313,9 +338,11 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
             if (c0 + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
         }
       }
-      const float m_new = fmaxf(m_run, mx * sl);
-      const float corr = ex2(m_run - m_new);  // 0 on the first tile (m_run = -inf)
-      const uint64_t negm2 = f2_bits(-m_new, -m_new);
+      // a masked row whose keys so far are all masked keeps m = -inf; exponents then use 0
+      const float m_new = masked ? fmaxf(m_run, mx) : fmaxf(m_run, mx * sl);
+      const float m_use = (masked && m_new == -INFINITY) ? 0.f : m_new;
+      const float corr = ex2(m_run - m_use);  // 0 on the first tile (m_run = -inf)
+      const uint64_t negm2 = f2_bits(-m_use, -m_use);
       // pass 2: p = 2^(s * sl - m), packed row sums, P (bf16/f16) to shared memory
       uint64_t sum2 = f2_bits(0.f, 0.f);
 #pragma unroll 1
@@ -333,6 +360,10 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
             const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[k]), __uint_as_float(r[k + 1])), sl2, negm2);
             float a0, a1;
             f2_unpack(arg, a0, a1);
+            if (masked) {
+              if (c0 + k < kvalid) a0 += fa_mask_add(p, moff + (int64_t)(c0 + k) * p.ms[3]);
+              if (c0 + k + 1 < kvalid) a1 += fa_mask_add(p, moff + (int64_t)(c0 + k + 1) * p.ms[3]);
+            }
             float e0 = ex2(a0), e1 = ex2(a1);
             if (!full) {
               if (c0 + k >= kvalid) e0 = 0.f;
@@ -816,6 +847,10 @@ static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
   p.out_dtype = d.dtype;
   p.stages = stages;
   p.causal = d.causal ? 1 : 0;
+  p.mask = d.mask_kind ? d.mask : nullptr;
+  p.mask_kind = d.mask_kind;
+  p.mask_dtype = d.mask_dtype;
+  for (int i = 0; i < 4; ++i) p.ms[i] = d.mask_strides[i];
   dim3 grid((unsigned)((d.Sq + kFaBM * NQ - 1) / (kFaBM * NQ)), (unsigned)(d.B * d.H));
   kern<<<grid, 64 + 128 * NQ, smem, st>>>(mq, mk, mv, p);
   return check_launch("flash_attention_sm100");
@@ -880,8 +915,11 @@ static int64_t tc_head_pad(int64_t D) {
 // MT_SDPA_PATH_SIMT when the tcgen05 kernels do not take it.
 int sdpa_tc_path(const mt_sdpa_desc& d) {
   if (d.dtype != MT_BF16 && d.dtype != MT_F16) return MT_SDPA_PATH_SIMT;
-  if (d.mask_kind != 0) return MT_SDPA_PATH_SIMT;
+  if (d.mask_kind != 0 && (!d.mask || (d.mask_kind == 2 && d.mask_dtype != MT_F32 && d.mask_dtype != MT_BF16 &&
+                                       d.mask_dtype != MT_F16)))
+    return MT_SDPA_PATH_SIMT;
   if (d.D != d.Dv) return MT_SDPA_PATH_SIMT;
+  if (!(d.scale > 0)) return MT_SDPA_PATH_SIMT;  // the tcgen05 kernels take the row max of unscaled scores
   const int64_t Dp = tc_head_pad(d.D);
   if (Dp == 0) return MT_SDPA_PATH_SIMT;
   if (d.Sq > INT32_MAX || d.Sk > INT32_MAX || d.B * d.H > 65535) return MT_SDPA_PATH_SIMT;
@@ -891,7 +929,8 @@ int sdpa_tc_path(const mt_sdpa_desc& d) {
       return MT_SDPA_PATH_SIMT;
   if (d.q_strides[3] != 1 || d.k_strides[3] != 1 || d.v_strides[3] != 1) return MT_SDPA_PATH_SIMT;
   const bool two = d.Sq > kFaBM;
-  if (two && Dp == 48 && d.scale > 0 && !d.causal && !getenv("MT_FA_NO_LAZY")) return MT_SDPA_PATH_TC_LAZY;
+  if (two && Dp == 48 && d.scale > 0 && !d.causal && d.mask_kind == 0 && !getenv("MT_FA_NO_LAZY"))
+    return MT_SDPA_PATH_TC_LAZY;
   return MT_SDPA_PATH_TC;
 }
 

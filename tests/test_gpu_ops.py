@@ -541,3 +541,32 @@ def test_conv2d_grouped(dtype, groups):
     m = mt.nn.Conv2d(64, 128, 3, padding=1, groups=groups, device="cuda", dtype=dtype)
     y = m(cu(x, dtype).contiguous(memory_format=mt.channels_last))
     assert tuple(y.shape) == (2, 128, 12, 12)
+
+
+@pytest.mark.parametrize("kind,D,causal,bcast", [("bool", 40, False, False), ("float", 64, False, True),
+                                                 ("float", 80, True, False), ("bool", 128, False, True),
+                                                 ("bf16", 40, False, True)])
+def test_sdpa_bf16_masked_tensor_core(kind, D, causal, bcast):
+    """Boolean and additive masks (fp32 or bf16, full [B, H, Sq, Sk] or broadcast [Sq, Sk]) on the
+    tcgen05 kernel, with ragged tiles, causal on top, and rows whose keys are all masked (NaN,
+    as the reference's softmax over an empty set)."""
+    B, H, Sq, Sk = 2, 3, 200, 150
+    rng = np.random.default_rng(D)
+    q, k, v = rnd(B, H, Sq, D), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
+    mshape = (Sq, Sk) if bcast else (B, H, Sq, Sk)
+    if kind == "bool":
+        m = rng.random(mshape) > 0.3
+        m[..., 5, :] = False  # a fully masked query row
+        md = mt.tensor(m).cuda()
+    else:
+        m = (rng.standard_normal(mshape) * 2).astype(np.float32)
+        m[..., 7, 100:] = -np.inf
+        md = cu(m, "bfloat16" if kind == "bf16" else None)
+        m = md.float().numpy()
+    qd, kd, vd = cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")
+    assert mt.ops.sdpa_path(qd, kd, vd, attn_mask=md, is_causal=causal) == "tc"
+    ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v), mask=m, causal=causal)
+    got = mt.scaled_dot_product_attention(qd, kd, vd, attn_mask=md, is_causal=causal).numpy()
+    nan = np.isnan(ref)
+    assert (np.isnan(got) == nan).all()
+    check(np.where(nan, 0, got), np.where(nan, 0, ref), BF16_RTOL)
