@@ -452,7 +452,7 @@ def test_sdpa_bf16_padded_head_dims(B, H, Sq, Sk, D):
 
 def test_sdpa_path_of_unet_shapes():
     """The attention shapes of the SD-1.5 UNet (strided head views of the fused projections) run on
-    the tensor-core kernels; fp32 and masked calls report the SIMT kernel."""
+    the tensor-core kernels; fp32 calls and non-positive scales report the SIMT kernel."""
     def heads(t, n, s, h, d):
         p = t.stride(0)
         return t._view((n, h, s, d), (s * p, d, p, 1))
@@ -471,7 +471,8 @@ def test_sdpa_path_of_unet_shapes():
     assert mt.ops.sdpa_path(q, q, q) == "simt"
     qb = q.to("bfloat16")
     mask = mt.zeros(64, 64, device="cuda")
-    assert mt.ops.sdpa_path(qb, qb, qb, attn_mask=mask) == "simt"
+    assert mt.ops.sdpa_path(qb, qb, qb, attn_mask=mask) == "tc"  # masks run on the general kernel
+    assert mt.ops.sdpa_path(qb, qb, qb, scale=-1.0) == "simt"
 
 
 @pytest.mark.parametrize("n,c1,c2,hw,silu", [(2, 1280, 1280, 8, True), (3, 640, 320, 16, True), (2, 320, 640, 32, False),
