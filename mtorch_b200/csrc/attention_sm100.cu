@@ -130,7 +130,7 @@ __device__ __forceinline__ void tmem_ld16_raw(uint32_t taddr, uint32_t (&r)[16])
       : "r"(taddr));
 }
 
-template <int DP, int DVP, int NQ, bool F16>
+template <int DP, int DVP, int NQ, bool F16, bool MASK = false>
 __global__ void __launch_bounds__(64 + 128 * NQ, 1)
     fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FaParams p) {
@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
       // masked rows: element offset of (b, h, query, first key of the tile); rows past Sq read
       // no mask
       const int qrow = qbase + x * kFaBM + row;
-      const bool masked = p.mask_kind != 0 && qrow < p.Sq;
+      const bool masked = MASK && qrow < p.Sq;
       const int64_t moff = masked ? (int64_t)b * p.ms[0] + (int64_t)h * p.ms[1] + (int64_t)qrow * p.ms[2] +
                                         (int64_t)j * kFaBN * p.ms[3]
                                   : 0;
@@ -817,13 +817,13 @@ static int fa_map(CUtensorMap* m, int dtype, const void* base, int64_t B, int64_
   return make_tensor_map(m, dtype, 5, base, dims, strides, box, 0);
 }
 
-template <int DP, int DVP, int NQ, bool F16>
+template <int DP, int DVP, int NQ, bool F16, bool MASK = false>
 static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
   using Cfg = FaCfg<DP, DVP, NQ>;
   const int stages = Cfg::STAGES;
   if (stages < 1) return fail(MT_ERR_UNSUPPORTED, "flash attention: head dim too large for shared memory");
   const int smem = Cfg::smem_bytes(stages) + 1024;
-  auto kern = fa_sm100_kernel<DP, DVP, NQ, F16>;
+  auto kern = fa_sm100_kernel<DP, DVP, NQ, F16, MASK>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -943,6 +943,18 @@ static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, bool lazy, cudaStream_
     const int rc = d.Dv <= 40 ? fa_lazy_launch<48, 48, F16, true>(d, st, &launched)
                               : fa_lazy_launch<48, 48, F16, false>(d, st, &launched);
     if (rc || launched) return rc;
+  }
+  if (d.mask_kind != 0) {
+    // masked calls: one query tile per CTA, the mask read per score in the softmax
+    switch (Dp) {
+      case 32: return fa_launch<32, 32, 1, F16, true>(d, st);
+      case 48: return fa_launch<48, 48, 1, F16, true>(d, st);
+      case 64: return fa_launch<64, 64, 1, F16, true>(d, st);
+      case 80: return fa_launch<80, 80, 1, F16, true>(d, st);
+      case 128: return fa_launch<128, 128, 1, F16, true>(d, st);
+      case 160: return fa_launch<160, 160, 1, F16, true>(d, st);
+      default: return fail(MT_ERR_UNSUPPORTED, "sdpa: no tcgen05 kernel for padded head dim %lld", (long long)Dp);
+    }
   }
   switch (Dp) {
     case 32: return two ? fa_launch<32, 32, 2, F16>(d, st) : fa_launch<32, 32, 1, F16>(d, st);
