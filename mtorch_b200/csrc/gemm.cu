@@ -36,8 +36,7 @@ struct TileParams {
   int m_pairs;   // CTA-pair variant: row-tile pairs, ceil(num_m_tiles / 2)
   // split K (implicit convolutions): tile t >= base tiles computes K iterations
   // [s * k_per, (s + 1) * k_per) of tile t % base, s = t / base, and writes raw fp32 partial sums
-  // (EpiParams::part); the epilogue warp that finishes last adds the splits in order and applies
-  // the epilogue
+  // (EpiParams::part); a reduction kernel adds the splits in order and applies the epilogue
   int k_splits, k_per;
   // implicit convolution over the channel concatenation of two sources (16-bit only): channel
   // chunks [0, c_split) come from tmA, the rest from the second source's map, passed in the tmAlo
@@ -59,7 +58,6 @@ struct EpiParams {
   int bias_vec;  // bias rows 16-byte aligned and bf16 / fp32: vector loads
   float* part;   // split K: [k_splits][M rows][N] fp32 partial sums (rows in (n, p, q) order)
   int64_t part_stride;
-  int* part_count;  // split K: per (base tile, epilogue warp) count of finished splits, zeroed per launch
 };
 
 // 256-bit global accesses (sm_100): one instruction covers a whole 32-byte sector, so a warp whose
@@ -593,63 +591,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             row_store(part, MT_F32, m_lin * ep.N + col0, nvalid, true, v);
           }
         }
-        // The warp that delivers the last split of its (tile, rows, columns) share adds the
-        // splits in order 0..S-1 and applies the epilogue (alpha, bias, activation, residual).
-        // Counting per warp needs no CTA-wide barrier, so a warp that gave up on a wait cannot
-        // leave the others blocked; it only leaves its share unwritten (the error is reported).
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          int* cnt = ep.part_count + (int64_t)(t % base_tiles) * 8 + (warp - 2);
-          last = atomicAdd(cnt, 1) == splits - 1;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          __threadfence();
-#pragma unroll 1
-          for (int c0 = half * 32; c0 < BN; c0 += 64) {
-            const int64_t col0 = (int64_t)nt * BN + c0;
-            const int64_t remain = ep.N - col0;
-            const int nvalid = remain < 32 ? (int)remain : 32;
-            if (valid && nvalid > 0) {
-              float v[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = 0.f;
-              // partials of other SMs: read at L2 (ld.global.cg), never from this SM's L1
-              for (int sp = 0; sp < splits; ++sp) {
-                const float* src = ep.part + (int64_t)sp * ep.part_stride + m_lin * ep.N + col0;
-                if (nvalid >= 32) {
-#pragma unroll
-                  for (int i = 0; i < 8; ++i) {
-                    const float4 f = __ldcg(reinterpret_cast<const float4*>(src) + i);
-                    v[4 * i] += f.x;
-                    v[4 * i + 1] += f.y;
-                    v[4 * i + 2] += f.z;
-                    v[4 * i + 3] += f.w;
-                  }
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j)
-                    if (j < nvalid) v[j] += __ldcg(src + j);
-                }
-              }
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] *= ep.alpha;
-              if (ep.bias)
-                row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, ep.bias_vec != 0, 1.f, v);
-              if (ep.act == MT_EPI_GELU) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = gelu_f(v[j]);
-              } else if (ep.act == MT_EPI_SILU) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
-              }
-              if (ep.res) row_load_add(ep.res, ep.out_dtype, offR + col0, nvalid, vec, 1.f, v);
-              row_store(ep.D, ep.out_dtype, offD + col0, nvalid, vec, v);
-            }
-          }
-        }
       } else if (!geglu) {
 #pragma unroll 1
         for (int c0 = half * 32; c0 < BN; c0 += 64) {
@@ -746,6 +687,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// Split-K reduction of an implicit convolution: out[n, p, q, c] = epilogue(sum_s part[s][m][c])
+// with m = (n * P + p) * Q + q, the splits added in order 0..S-1 (fixed, so results do not depend
+// on the batch), then the GEMM epilogue's order: alpha, bias (per column or per image), activation,
+// residual.  One thread per 8 consecutive columns.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* part, int splits, int64_t stride,
+                                                            int64_t rows, int64_t N, const EpiParams ep) {
+  const int64_t n8 = N / 8;
+  const int64_t total = rows * n8;
+  const int64_t PQ = ep.P * ep.Q;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / n8, c = (i - m * n8) * 8;
+    float v[8];
+    {
+      const float4* q = reinterpret_cast<const float4*>(part + m * N + c);
+      const float4 a = q[0], b = q[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    for (int s = 1; s < splits; ++s) {
+      const float4* q = reinterpret_cast<const float4*>(part + s * stride + m * N + c);
+      const float4 a = q[0], b = q[1];
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+    const int64_t n = m / PQ, rem = m - n * PQ, pp = rem / ep.Q, qq = rem - pp * ep.Q;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= ep.alpha;
+    if (ep.bias) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += load_as_f32(ep.bias, n * ep.bias_bstride + c + j, ep.bias_dtype);
+    }
+    if (ep.act == MT_EPI_GELU) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = gelu_f(v[j]);
+    } else if (ep.act == MT_EPI_SILU) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = silu_f(v[j]);
+    }
+    if (ep.res) {
+      const int64_t offR = n * ep.r_s0 + pp * ep.r_s1 + qq * ep.r_s2 + c;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += load_as_f32(ep.res, offR + j, ep.out_dtype);
+    }
+    const int64_t offD = n * ep.d_s0 + pp * ep.d_s1 + qq * ep.d_s2 + c;
+    if (ep.vec_ok && (ep.out_dtype == MT_BF16 || ep.out_dtype == MT_F16)) {
+      uint4 w;
+      uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        wp[j] = ep.out_dtype == MT_BF16 ? pack_bf16x2(v[2 * j], v[2 * j + 1]) : pack_f16x2(v[2 * j], v[2 * j + 1]);
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(ep.D) + offD) = w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) store_from_f32(ep.D, offD + j, ep.out_dtype, v[j]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host side.
 
 struct GemmLaunch {
@@ -760,7 +758,6 @@ struct GemmLaunch {
   // TMA-store epilogue: output map (32 x 32 boxes, 64-byte swizzle) when `tst`
   CUtensorMap d;
   bool tst;
-  size_t part_count_bytes;  // split K: bytes of the split counters to zero before the launch
 };
 
 static int map_kmajor(CUtensorMap* m, int dtype, const void* base, int64_t K, int64_t rows, int64_t batch,
@@ -1206,12 +1203,6 @@ static int conv_k_splits(const mt_conv2d_desc& d, int64_t k_iters) {
   return 1;
 }
 
-// Bytes of split-K counters for convolution d: 8 epilogue warps x (an upper bound of) its tiles.
-static size_t split_count_bytes(const mt_conv2d_desc& d) {
-  const int64_t row_tiles = (d.N * d.P * d.Q + 31) / 32, col_tiles = (d.K + 63) / 64;
-  return (size_t)(row_tiles * col_tiles * 8) * sizeof(int);
-}
-
 static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream_t st, GemmLaunch* L,
                      const ConvCat* cat = nullptr, bool allow_split = false) {
   const int es = dtype_size(d.dtype);
@@ -1305,16 +1296,10 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   }
   // split-K partial sums (decided from the per-image shape; see conv_k_splits)
   float* part = nullptr;
-  int* part_count = nullptr;
   int splits = 1;
   if (allow_split && implicit) {
     splits = conv_k_splits(d, d.R * d.S * (d.C / (128 / es)));
-    if (splits > 1) {
-      part = (float*)ws.take((size_t)splits * d.N * d.P * d.Q * d.K * sizeof(float));
-      // per (row tile, column tile, epilogue warp) counters; row tiles <= N*P*Q / 32 and column
-      // tiles <= K / 64 bound the count whatever tile shape is chosen below
-      part_count = (int*)ws.take(split_count_bytes(d));
-    }
+    if (splits > 1) part = (float*)ws.take((size_t)splits * d.N * d.P * d.Q * d.K * sizeof(float));
   }
   if (!run) return MT_OK;
 
@@ -1407,18 +1392,18 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   ep.bias_vec = bias_vec_ok(d.bias, d.bias_dtype, d.bias_batch_stride);
   ep.part = part;
   ep.part_stride = d.N * d.P * d.Q * d.K;
-  ep.part_count = part_count;
-  L->part_count_bytes = part_count ? split_count_bytes(d) : 0;
-  if (part_count && (size_t)tp.num_m_tiles * tp.num_n_tiles * 8 * sizeof(int) > L->part_count_bytes)
-    return fail(MT_ERR_INVALID, "conv2d: split-K counter bound exceeded");
   return MT_OK;
 }
 
-// Before a split-K convolution: zero its per-(tile, warp) split counters (no-op otherwise).  The
-// splits are added by the warp that finishes last (see the kernel's epilogue).
-static int prepare_split(const GemmLaunch& L, cudaStream_t st) {
+// The reduction that completes a split-K convolution (no-op otherwise).
+static int finish_split(const GemmLaunch& L, cudaStream_t st) {
   if (L.tp.k_splits <= 1) return MT_OK;
-  return cuda_check(cudaMemsetAsync(L.ep.part_count, 0, L.part_count_bytes, st), "split-K counters");
+  const EpiParams& ep = L.ep;
+  const int64_t rows = ep.M * ep.P * ep.Q;
+  const int64_t total = rows * (ep.N / 8);
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
+  splitk_reduce_kernel<<<blocks, 256, 0, st>>>(ep.part, L.tp.k_splits, ep.part_stride, rows, ep.N, ep);
+  return check_launch("splitk_reduce");
 }
 
 static int validate_conv(const mt_conv2d_desc& d) {
@@ -1489,8 +1474,8 @@ int run_conv2d(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStream_t
   GemmLaunch L{};
   rc = plan_conv(d, ws, true, st, &L, nullptr, true);
   if (rc) return rc;
-  rc = prepare_split(L, st);
-  if (!rc) rc = dispatch(L, st);
+  rc = dispatch(L, st);
+  if (!rc) rc = finish_split(L, st);
   if (rc) return rc;
   if (L.ep.D != d.y) {
     int64_t cl[4] = {d.P * d.Q * d.K, 1, d.Q * d.K, d.K};
@@ -1539,8 +1524,8 @@ int run_conv2d_cat(const mt_conv2d_desc& d, const void* x2, const int64_t* x2_st
   GemmLaunch L{};
   rc = plan_conv(d, ws, true, st, &L, &cat, true);
   if (rc) return rc;
-  rc = prepare_split(L, st);
-  if (!rc) rc = dispatch(L, st);
+  rc = dispatch(L, st);
+  if (!rc) rc = finish_split(L, st);
   if (rc) return rc;
   if (L.ep.D != d.y) {
     int64_t cl[4] = {d.P * d.Q * d.K, 1, d.Q * d.K, d.K};
@@ -1661,8 +1646,8 @@ int run_conv2d_up2x(const mt_conv2d_desc& d, void* wsp, size_t ws_bytes, cudaStr
     rc = plan_conv(e, wsp2, true, st, &L, nullptr, true);
     if (rc) return rc;
     if (L.ep.D != e.y) return fail(MT_ERR_UNSUPPORTED, "conv2d_up2x: output layout");
-    rc = prepare_split(L, st);
-    if (!rc) rc = dispatch(L, st);
+    rc = dispatch(L, st);
+    if (!rc) rc = finish_split(L, st);
     if (rc) return rc;
   }
   return MT_OK;
