@@ -117,3 +117,20 @@ def test_tiny_unet_bf16_runs_and_is_batch_independent():
     assert y.shape == (4, 4, 16, 16) and np.isfinite(y).all()
     y2 = net(x[2:], te[2:], ctx[2:]).numpy()
     np.testing.assert_array_equal(y[2:], y2)
+
+
+def test_full_unet_batch8_equals_batch64_bitwise():
+    """The SD-1.5 UNet (bf16) on 8 samples equals, bit for bit, the same 8 samples inside a batch
+    of 64: the per-GPU work of the 8-GPU job against the 1-GPU job.  Split-K counts, GroupNorm
+    chunking and attention tiling depend only on the per-image shape; column-tile widths may
+    change with the row count (they do not change any element's K-reduction order)."""
+    mt.manual_seed(0)
+    net = U.UNet(device="cuda", dtype="bfloat16")
+    mt.manual_seed(1)
+    x = mt.randn(64, 4, 64, 64).to("bfloat16").cuda()
+    ctx = mt.randn(64, 77, 768).to("bfloat16").cuda()
+    te = mt.tensor(U.timestep_embedding(np.full(64, 741.0)), dtype="bfloat16").cuda()
+    y64 = net(x, te, ctx).numpy()
+    for lo in (0, 56):
+        y8 = net(x[lo:lo + 8], te[lo:lo + 8], ctx[lo:lo + 8]).numpy()
+        np.testing.assert_array_equal(y8, y64[lo:lo + 8])
