@@ -311,11 +311,13 @@ int mt_cuda_sdpa(const mt_sdpa_desc* desc, void* workspace, size_t workspace_byt
  * CPU path): the tcgen05 kernel with the output kept in TMEM (head dims 33-48, more than 128
  * queries, no mask or causal), the general tcgen05 kernel (16-bit types, head dims that are
  * multiples of 8 up to 160, padded to 32/48/64/80/128/160; bool or f32/bf16/f16 additive masks,
- * causal, positive scale), or the fp32 SIMT kernel (fp32, other head dims, scales or strides).
- * Returns 0 for an invalid descriptor. */
+ * causal, positive scale), the short-key tcgen05 kernel (at most 128 keys, head dims up to 128,
+ * no mask or causal: K and V loaded once per CTA for several query tiles), or the fp32 SIMT
+ * kernel (fp32, other head dims, scales or strides).  Returns 0 for an invalid descriptor. */
 #define MT_SDPA_PATH_TC_LAZY 1
 #define MT_SDPA_PATH_TC 2
 #define MT_SDPA_PATH_SIMT 3
+#define MT_SDPA_PATH_TC_SHORT 4
 int mt_cuda_sdpa_path(const mt_sdpa_desc* desc);
 
 /* ---- host random generator: the reference's RandomState (module.cpp:47-183) ------------- */

@@ -16,7 +16,7 @@ MT_OK, MT_ERR_INVALID, MT_ERR_UNSUPPORTED, MT_ERR_LAUNCH, MT_ERR_TIMEOUT, MT_ERR
 UNARY = {"silu": 0, "gelu": 1, "gelu_tanh": 2, "neg": 3, "exp": 4, "sigmoid": 5, "relu": 6, "quick_gelu": 7}
 BINARY = {"add": 0, "sub": 1, "mul": 2, "div": 3}
 EPI_NONE, EPI_GELU, EPI_SILU, EPI_GEGLU, EPI_QUICK_GELU = range(5)
-SDPA_PATH_TC_LAZY, SDPA_PATH_TC, SDPA_PATH_SIMT = 1, 2, 3
+SDPA_PATH_TC_LAZY, SDPA_PATH_TC, SDPA_PATH_SIMT, SDPA_PATH_TC_SHORT = 1, 2, 3, 4
 
 I64 = C.c_int64
 I64_4 = I64 * 4

@@ -42,6 +42,7 @@ struct FaParams {
   const void* mask;
   int mask_kind, mask_dtype;
   int64_t ms[4];
+  int pairs;  // fa_short_sm100_kernel: pairs of 128-query tiles per CTA
 };
 
 // log2-domain additive term of the mask for (query row, key) at element offset `off`: 0 / -inf
@@ -793,6 +794,252 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// Attention over at most one key tile (Sk <= 128: the UNet's cross-attention to 77 context tokens).
+//
+// With one key tile a CTA of the general kernels spends most of its life on fixed costs (TMEM
+// allocation, barrier set-up, the first Q load, the output store) for a few hundred cycles of
+// work.  Here a CTA loads K and V once and walks `p.pairs` consecutive pairs of 128-query tiles of
+// one (b, h): warp 0 streams Q (one buffer per warpgroup), warp 1 issues S = Q K^T and O = P V,
+// warpgroup x (warps 2-5, 6-9) takes query tile x of every pair: softmax of its S row (the whole
+// row is in TMEM, so the maximum is exact and no rescale exists), P to shared memory, then O / l to
+// global.  While a warpgroup finishes pair i, the MMA warp already computes S for the other
+// warpgroup and, once S is released and the next Q has landed, for pair i + 1.
+template <int DP, int DVP, bool F16, bool SUMCOL>
+__global__ void __launch_bounds__(320, 1)
+    fa_short_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+  constexpr int Q_BYTES = kFaBM * DP * 2;
+  constexpr int K_BYTES = kFaBN * DP * 2;
+  constexpr int V_BYTES = kFaBN * DVP * 2;
+  constexpr int V_TX = SUMCOL ? V_BYTES - kFaBN * 16 : V_BYTES;
+  constexpr int P_BYTES = kFaBM * kFaBN * 2;
+  constexpr uint32_t kLbo = kFaBM * 16;
+  constexpr uint32_t kSbo = 128;
+  constexpr int FMT = F16 ? 0 : 1;
+  constexpr uint32_t idesc_s = make_idesc(FMT, kFaBM, kFaBN);
+  constexpr uint32_t idesc_o = make_idesc(FMT, kFaBM, DVP) | (1u << 16);
+  static_assert(2 * 128 + 2 * DVP <= 512, "TMEM budget");
+
+  extern __shared__ uint8_t fa_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;             // [2][Q]
+  uint8_t* sP = sQ + 2 * Q_BYTES;  // [2][P]
+  uint8_t* sK = sP + 2 * P_BYTES;
+  uint8_t* sV = sK + K_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + V_BYTES);
+  uint64_t* kv_full = bars;        // K and V loaded
+  uint64_t* q_full = bars + 1;     // [2]
+  uint64_t* q_empty = q_full + 2;  // [2]
+  uint64_t* s_full = q_empty + 2;  // [2]
+  uint64_t* s_empty = s_full + 2;  // [2]
+  uint64_t* p_full = s_empty + 2;  // [2]
+  uint64_t* o_full = p_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / (p.H / p.Hkv);
+  const int pair0 = blockIdx.x * p.pairs;
+  const int total_pairs = (p.Sq + 2 * kFaBM - 1) / (2 * kFaBM);
+  const int npairs = min(p.pairs, total_pairs - pair0);
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (SUMCOL) {  // the unloaded last 8-column chunk of V: a column of ones (row sums of P)
+    for (int i = threadIdx.x; i < kFaBN; i += blockDim.x) {
+      uint4* d = reinterpret_cast<uint4*>(sV + (DVP / 8 - 1) * kFaBN * 16) + i;
+      *d = make_uint4(F16 ? 0x3C00u : 0x3F80u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_o0 = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0 && npairs > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(kv_full, K_BYTES + V_TX);
+      tma_load_5d(sK, &tmK, kv_full, 0, 0, 0, hk, b);
+      tma_load_5d(sV, &tmV, kv_full, 0, 0, 0, hk, b);
+      for (int i = 0; i < npairs; ++i)
+        for (int x = 0; x < 2; ++x) {
+          if (!mbar_wait(&q_empty[x], (i & 1) ^ 1, 41, abort_flag)) i = npairs;
+          if (i >= npairs) break;
+          mbar_arrive_expect_tx(&q_full[x], Q_BYTES);
+          tma_load_5d(sQ + x * Q_BYTES, &tmQ, &q_full[x], 0, ((pair0 + i) * 2 + x) * kFaBM, 0, h, b);
+        }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && npairs > 0) {
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      bool ok = mbar_wait(kv_full, 0, 42, abort_flag);
+      for (int i = 0; ok && i < npairs; ++i) {
+        for (int x = 0; x < 2 && ok; ++x) {
+          ok = mbar_wait(&q_full[x], i & 1, 43, abort_flag) && mbar_wait(&s_empty[x], (i & 1) ^ 1, 44, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t qa = q_addr + x * Q_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < DP / 16; ++kk)
+            umma_f16(tmem + x * 128, sdesc_none(qa + kk * 2 * kLbo, kLbo, kSbo),
+                     sdesc_none(k_addr + kk * 2 * kLbo, kLbo, kSbo), idesc_s, kk > 0 ? 1u : 0u);
+          umma_commit(&s_full[x]);
+          umma_commit(&q_empty[x]);
+        }
+        for (int x = 0; x < 2 && ok; ++x) {
+          // P of pair i is written only after the warpgroup has read O of pair i - 1, so the
+          // product below never overwrites an O still being read
+          ok = mbar_wait(&p_full[x], i & 1, 45, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t pa = p_addr + x * P_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kFaBN / 16; ++kk)
+            umma_f16(t_o0 + x * DVP, sdesc_none(pa + kk * 2 * kLbo, kLbo, kSbo),
+                     sdesc_none(v_addr + kk * 256, 128, kFaBN * 16), idesc_o, kk > 0 ? 1u : 0u);
+          umma_commit(&o_full[x]);
+        }
+      }
+    }
+  } else {
+    const int x = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t t_o = t_o0 + x * DVP + lane_off;
+    const uint32_t ts = tmem + x * 128 + lane_off;
+    const float sl = p.scale_log2;
+    const uint64_t sl2 = f2_bits(sl, sl);
+    const int kvalid = p.Sk;  // <= kFaBN
+    const bool full = kvalid == kFaBN;
+    uint8_t* sPx = sP + x * P_BYTES;
+    for (int i = 0; i < npairs; ++i) {
+      if (!mbar_wait(&s_full[x], i & 1, 46, abort_flag)) break;
+      tc_fence_after();
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
+        uint32_t r[64];
+        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld_wait();
+        if (full) {
+          mx = fmaxf(mx, max64(r));
+        } else {
+#pragma unroll
+          for (int k = 0; k < 64; ++k)
+            if (c0 + k < kvalid) mx = fmaxf(mx, __uint_as_float(r[k]));
+        }
+      }
+      const uint64_t negm2 = f2_bits(-mx * sl, -mx * sl);
+      uint64_t sum2 = f2_bits(0.f, 0.f);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
+        uint32_t r[64];
+        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld_wait();
+        if (c0 == kFaBN - 64) {  // the last read of S: the next QK^T may overwrite it
+          tc_fence_before();
+          mbar_arrive(&s_empty[x]);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int k2 = 0; k2 < 16; k2 += 2) {
+            const int k = q * 16 + k2;
+            const uint64_t arg = ffma2(f2_bits(__uint_as_float(r[k]), __uint_as_float(r[k + 1])), sl2, negm2);
+            float a0, a1;
+            f2_unpack(arg, a0, a1);
+            float e0 = ex2(a0), e1 = ex2(a1);
+            if (!full) {
+              if (c0 + k >= kvalid) e0 = 0.f;
+              if (c0 + k + 1 >= kvalid) e1 = 0.f;
+            }
+            if (!SUMCOL) sum2 = fadd2(sum2, f2_bits(e0, e1));
+            pk[k2 / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+          }
+          const int c = c0 + q * 16;
+          uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
+          uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
+          *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *d1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[x]);
+      if (!mbar_wait(&o_full[x], i & 1, 47, abort_flag)) break;
+      tc_fence_after();
+      float o[DVP];
+#pragma unroll
+      for (int c0 = 0; c0 < DVP; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16_raw(t_o + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) o[c0 + k] = __uint_as_float(r[k]);
+      }
+      float s0, s1;
+      f2_unpack(sum2, s0, s1);
+      const int qi = ((pair0 + i) * 2 + x) * kFaBM + row;
+      if (qi < p.Sq) {
+        const float inv = 1.0f / (SUMCOL ? o[DVP - 8] : s0 + s1);
+        char* base = static_cast<char*>(p.o);
+        const int64_t off = (int64_t)b * p.os[0] + (int64_t)h * p.os[1] + (int64_t)qi * p.os[2];
+        if (p.os[3] == 1 && (p.Dv % 8) == 0 && ((reinterpret_cast<uintptr_t>(base) + off * 2) % 16) == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(base + off * 2);
+#pragma unroll
+          for (int c = 0; c < DVP; c += 8) {
+            if (c < p.Dv) {
+              uint32_t w[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                w[k] = F16 ? pack_f16x2(o[c + 2 * k] * inv, o[c + 2 * k + 1] * inv)
+                           : pack_bf16x2(o[c + 2 * k] * inv, o[c + 2 * k + 1] * inv);
+              dst[c / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < DVP; ++c)
+            if (c < p.Dv) store_from_f32(p.o, off + (int64_t)c * p.os[3], p.out_dtype, o[c] * inv);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host side.
 
 template <int DP, int DVP, int NQ>
@@ -898,6 +1145,43 @@ static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched
   return check_launch("flash_attention_lazy_sm100");
 }
 
+// Launch of the short-KV kernel (Sk <= 128): CTAs of `pairs` 256-query pairs of one (b, h), about
+// four CTAs per SM in total so that the last wave is short.
+template <int DP, int DVP, bool F16, bool SUMCOL>
+static int fa_short_launch(const mt_sdpa_desc& d, cudaStream_t st) {
+  constexpr int SMEM = 2 * kFaBM * DP * 2 + 2 * kFaBM * kFaBN * 2 + kFaBN * (DP + DVP) * 2 + 1024 + 1024;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  auto kern = fa_short_sm100_kernel<DP, DVP, F16, SUMCOL>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
+                        "short attention smem attribute");
+    if (rc) return rc;
+    attr[dev & 63] = true;
+  }
+  CUtensorMap mq, mk, mv;
+  int rc = fa_map(&mq, d.dtype, d.q, d.B, d.H, d.Sq, d.D, d.q_strides, DP / 8);
+  if (!rc) rc = fa_map(&mk, d.dtype, d.k, d.B, d.Hkv, d.Sk, d.D, d.k_strides, DP / 8);
+  if (!rc) rc = fa_map(&mv, d.dtype, d.v, d.B, d.Hkv, d.Sk, d.Dv, d.v_strides, SUMCOL ? DVP / 8 - 1 : DVP / 8);
+  if (rc) return rc;
+  FaParams p{};
+  p.Sq = (int)d.Sq; p.Sk = (int)d.Sk; p.H = (int)d.H; p.Hkv = (int)d.Hkv; p.B = (int)d.B;
+  p.scale_log2 = (float)(d.scale * 1.4426950408889634);
+  p.o = d.o;
+  for (int i = 0; i < 4; ++i) p.os[i] = d.o_strides[i];
+  p.Dv = (int)d.Dv;
+  p.out_dtype = d.dtype;
+  const int64_t pairs_bh = (d.Sq + 2 * kFaBM - 1) / (2 * kFaBM);
+  const int64_t bh = d.B * d.H;
+  const int64_t cpb = std::min<int64_t>(pairs_bh, std::max<int64_t>(1, (4 * (int64_t)num_sms() + bh - 1) / bh));
+  p.pairs = (int)((pairs_bh + cpb - 1) / cpb);
+  dim3 grid((unsigned)((pairs_bh + p.pairs - 1) / p.pairs), (unsigned)bh);
+  kern<<<grid, 320, SMEM, st>>>(mq, mk, mv, p);
+  return check_launch("flash_attention_short_sm100");
+}
+
 size_t sdpa_tc_workspace(const mt_sdpa_desc&) { return 0; }
 
 static bool aligned16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -929,9 +1213,25 @@ int sdpa_tc_path(const mt_sdpa_desc& d) {
       return MT_SDPA_PATH_SIMT;
   if (d.q_strides[3] != 1 || d.k_strides[3] != 1 || d.v_strides[3] != 1) return MT_SDPA_PATH_SIMT;
   const bool two = d.Sq > kFaBM;
+  static const bool no_short = getenv("MT_FA_NO_SHORT") != nullptr;
+  if (d.Sk <= kFaBN && Dp <= 128 && !d.causal && d.mask_kind == 0 && !no_short) return MT_SDPA_PATH_TC_SHORT;
   if (two && Dp == 48 && d.scale > 0 && !d.causal && d.mask_kind == 0 && !getenv("MT_FA_NO_LAZY"))
     return MT_SDPA_PATH_TC_LAZY;
   return MT_SDPA_PATH_TC;
+}
+
+template <bool F16>
+static int fa_short_dispatch(const mt_sdpa_desc& d, int64_t Dp, cudaStream_t st) {
+  const bool sumcol = d.Dv <= Dp - 8;
+  switch (Dp) {
+    case 32: return sumcol ? fa_short_launch<32, 32, F16, true>(d, st) : fa_short_launch<32, 32, F16, false>(d, st);
+    case 48: return sumcol ? fa_short_launch<48, 48, F16, true>(d, st) : fa_short_launch<48, 48, F16, false>(d, st);
+    case 64: return sumcol ? fa_short_launch<64, 64, F16, true>(d, st) : fa_short_launch<64, 64, F16, false>(d, st);
+    case 80: return sumcol ? fa_short_launch<80, 80, F16, true>(d, st) : fa_short_launch<80, 80, F16, false>(d, st);
+    case 128:
+      return sumcol ? fa_short_launch<128, 128, F16, true>(d, st) : fa_short_launch<128, 128, F16, false>(d, st);
+    default: return fail(MT_ERR_UNSUPPORTED, "sdpa: no short-KV kernel for padded head dim %lld", (long long)Dp);
+  }
 }
 
 template <bool F16>
@@ -972,6 +1272,8 @@ int run_sdpa_tc(const mt_sdpa_desc& d, void*, size_t, cudaStream_t st, bool* han
   *handled = path != MT_SDPA_PATH_SIMT;
   if (!*handled) return MT_OK;
   const int64_t Dp = tc_head_pad(d.D);
+  if (path == MT_SDPA_PATH_TC_SHORT)
+    return d.dtype == MT_F16 ? fa_short_dispatch<true>(d, Dp, st) : fa_short_dispatch<false>(d, Dp, st);
   const bool lazy = path == MT_SDPA_PATH_TC_LAZY;
   return d.dtype == MT_F16 ? fa_dispatch<true>(d, Dp, lazy, st) : fa_dispatch<false>(d, Dp, lazy, st);
 }

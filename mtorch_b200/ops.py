@@ -485,15 +485,16 @@ def _sdpa_desc(q, k, v, out, attn_mask, is_causal, scale, enable_gqa):
 def sdpa_path(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None = None, is_causal=False, scale=None,
               enable_gqa=False) -> str:
     """Which device kernel scaled_dot_product_attention runs for these arguments: "tc_lazy" (the
-    tcgen05 kernel with the output in TMEM), "tc" (the general tcgen05 kernel) or "simt" (the fp32
-    SIMT kernel).  Nothing is launched."""
+    tcgen05 kernel with the output in TMEM), "tc" (the general tcgen05 kernel), "tc_short" (the
+    tcgen05 kernel for at most 128 keys) or "simt" (the fp32 SIMT kernel).  Nothing is launched."""
     _require_cuda(q, k, v, attn_mask)
     out = _new(q._shape[:-2] + (q._shape[-2], v._shape[-1]), q.dtype, q.device)
     d = _sdpa_desc(q, k, v, out, attn_mask, is_causal, scale, enable_gqa)
     code = _lib().mt_cuda_sdpa_path(C.byref(d))
     if code == 0:
         raise ValueError("sdpa_path: invalid arguments")
-    return {L.SDPA_PATH_TC_LAZY: "tc_lazy", L.SDPA_PATH_TC: "tc", L.SDPA_PATH_SIMT: "simt"}[code]
+    return {L.SDPA_PATH_TC_LAZY: "tc_lazy", L.SDPA_PATH_TC: "tc", L.SDPA_PATH_SIMT: "simt",
+            L.SDPA_PATH_TC_SHORT: "tc_short"}[code]
 
 
 def scaled_dot_product_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None = None, dropout_p=0.0,

@@ -466,7 +466,7 @@ def test_sdpa_path_of_unet_shapes():
         assert mt.ops.sdpa_path(q, k, v) == want, (c, s)
         kv = mt.empty(n * 77, 2 * c, dtype="bfloat16", device="cuda")
         kc, vc = heads(kv[:, 0:c], n, 77, 8, d), heads(kv[:, c:2 * c], n, 77, 8, d)
-        assert mt.ops.sdpa_path(q, kc, vc) == want, (c, s, "cross")
+        assert mt.ops.sdpa_path(q, kc, vc) == ("tc_short" if d <= 128 else "tc"), (c, s, "cross")
     q = mt.empty(1, 2, 64, 40, device="cuda")
     assert mt.ops.sdpa_path(q, q, q) == "simt"
     qb = q.to("bfloat16")
@@ -571,3 +571,19 @@ def test_sdpa_bf16_masked_tensor_core(kind, D, causal, bcast):
     nan = np.isnan(ref)
     assert (np.isnan(got) == nan).all()
     check(np.where(nan, 0, got), np.where(nan, 0, ref), BF16_RTOL)
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk,D,dtype", [(2, 8, 4096, 77, 40, "bfloat16"), (2, 8, 1024, 77, 80, "bfloat16"),
+                                               (1, 3, 300, 128, 64, "bfloat16"), (3, 2, 100, 1, 40, "bfloat16"),
+                                               (1, 4, 1000, 50, 128, "float16"), (2, 2, 700, 77, 16, "bfloat16"),
+                                               (1, 2, 257, 120, 48, "float16")])
+def test_sdpa_short_keys(B, H, Sq, Sk, D, dtype):
+    """At most 128 keys (cross-attention to the 77-token context): the persistent short-key
+    kernel, K and V loaded once per CTA for several query-tile pairs; ragged query counts, one key,
+    the ones-column row sum (head dim <= padded - 8) and the softmax-side row sum."""
+    q, k, v = rnd(B, H, Sq, D, scale=1.5), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
+    qd, kd, vd = cu(q, dtype), cu(k, dtype), cu(v, dtype)
+    assert mt.ops.sdpa_path(qd, kd, vd) == "tc_short"
+    r = bf16_round if dtype == "bfloat16" else (lambda a: np.asarray(a, np.float32).astype(np.float16).astype(np.float32))
+    ref = oracle.sdpa_f32(r(q), r(k), r(v))
+    check(mt.scaled_dot_product_attention(qd, kd, vd).float().numpy(), ref, BF16_RTOL)
