@@ -445,7 +445,7 @@ def test_sdpa_bf16_padded_head_dims(B, H, Sq, Sk, D):
     extra columns zero-filled by TMA."""
     q, k, v = rnd(B, H, Sq, D), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
     qd, kd, vd = cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")
-    assert mt.ops.sdpa_path(qd, kd, vd) == "tc"
+    assert mt.ops.sdpa_path(qd, kd, vd) == ("tc_short" if Sk <= 128 and D <= 128 else "tc")
     ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
     check(mt.scaled_dot_product_attention(qd, kd, vd).numpy(), ref, BF16_RTOL)
 
