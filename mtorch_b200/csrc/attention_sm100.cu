@@ -969,6 +969,14 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint32_t pk[8];
+          const int c = c0 + q * 16;
+          if (c >= kvalid) {  // 16 keys past the end: P is zero, no exponentials (uniform branch)
+            uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
+            uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
+            *d0 = make_uint4(0u, 0u, 0u, 0u);
+            *d1 = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+          }
 #pragma unroll
           for (int k2 = 0; k2 < 16; k2 += 2) {
             const int k = q * 16 + k2;
@@ -983,7 +991,6 @@ __global__ void __launch_bounds__(320, 1)
             if (!SUMCOL) sum2 = fadd2(sum2, f2_bits(e0, e1));
             pk[k2 / 2] = F16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
           }
-          const int c = c0 + q * 16;
           uint4* d0 = reinterpret_cast<uint4*>(sPx + (c / 8) * (kFaBM * 16) + row * 16);
           uint4* d1 = reinterpret_cast<uint4*>(sPx + (c / 8 + 1) * (kFaBM * 16) + row * 16);
           *d0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
