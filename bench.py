@@ -489,7 +489,9 @@ def run_workload(args):
       vae      SD-1.5 VAE decode of `batch` latents 64x64 -> 512x512 images; unit = images/s
       text     SD-1.5 CLIP text encoder on `batch` sequences of 77 tokens; unit = sequences/s
       c4       BASELINE config C4: the fp32 UNet on one latent, one UNet eval + DDIM update (CUDA
-               graph); unit = steps/s, beside the reference CPU path on the same per-sample work"""
+               graph); unit = steps/s, beside the reference CPU path on the same per-sample work
+      c1-c3    BASELINE configs C1 (fp32 matmul 2048^2), C2 (fp32 ResNet block), C3 (bf16 attention
+               block), beside the reference CPU path computing each in full (see run_config)"""
     import torch
 
     import mtorch_b200 as mt
@@ -498,6 +500,9 @@ def run_workload(args):
     nb = args.batch
     mt.manual_seed(0)
     base = None
+    if args.workload in ("c1", "c2", "c3"):
+        run_config(args)
+        return
     if args.workload == "c4":
         from mtorch_b200.graphs import Graphed
         from mtorch_b200.unet import DDIM, UNet, timestep_embedding, unet_flops_per_sample
@@ -571,6 +576,72 @@ def run_workload(args):
     print(json.dumps(line))
 
 
+def run_config(args):
+    """BASELINE configs C1-C3 on one GPU (CUDA events, `steps` runs after `warmup`), beside the
+    reference's own CPU path computing the same configuration in full on all host cores (each op
+    cut into row slices spread over single-threaded processes; oracle/cpu_bench.FullRun)."""
+    import torch
+
+    import mtorch_b200 as mt
+    from mtorch_b200 import ops
+    from mtorch_b200.unet import BasicTransformerBlock
+
+    stream = torch.cuda.current_stream()
+    mt.manual_seed(0)
+    if args.workload == "c1":
+        a = mt.randn(2048, 2048).cuda()
+        b = mt.randn(2048, 2048).cuda()
+        fn = lambda: mt.matmul(a, b)  # noqa: E731
+        flops, name, dtype = 2.0 * 2048 ** 3, "C1: fp32 matmul 2048 x 2048 x 2048 (3xTF32)", "f32"
+    elif args.workload == "c2":
+        x = mt.randn(2, 320, 64, 64).cuda().contiguous(memory_format=mt.channels_last)
+        gn1, gn2 = mt.nn.GroupNorm(32, 320, device="cuda"), mt.nn.GroupNorm(32, 320, device="cuda")
+        c1 = mt.nn.Conv2d(320, 320, 3, padding=1, device="cuda")
+        c2 = mt.nn.Conv2d(320, 320, 3, padding=1, device="cuda")
+        fn = lambda: c2(gn2(c1(gn1(x, fuse_silu=True)), fuse_silu=True), residual=x)  # noqa: E731
+        flops, name, dtype = 2 * 2.0 * 2 * 4096 * 320 * 320 * 9, "C2: SD ResNet block fp32, [2, 320, 64, 64]", "f32"
+    else:
+        blk = BasicTransformerBlock(320, 8, 768, device="cuda", dtype="bfloat16")
+        h = mt.randn(2 * 4096, 320).to("bfloat16").cuda()
+        ctx = mt.randn(2, 77, 768).to("bfloat16").cuda()
+        fn = lambda: blk(h, ctx, 2, 4096)  # noqa: E731
+        from oracle.cpu_bench import config_ops, op_flops
+
+        flops = sum(op_flops(o) for o in config_ops("c3"))
+        name, dtype = "C3: SD attention block bf16 (self 4096 + cross 77 + GEGLU FFN), [2, 4096, 320]", "bf16"
+    for _ in range(max(args.warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    _, tf_burst, _, kind = peaks()
+    tflops = flops / (ms * 1e-3) / 1e12
+    line = {"workload": name, "value": 1000.0 / ms, "unit": "runs/s", "ms_per_run": ms, "dtype": dtype,
+            "data": "synthetic (mtorch.manual_seed(0) N(0,1) inputs), random-init weights", "tflops": tflops,
+            "frac_of_bf16_peak": tflops / tf_burst, "peak_kind": f"{kind} bf16 burst"}
+    if not args.no_cpu_baseline:
+        from oracle import cpu_bench
+
+        procs = os.cpu_count() or 1
+        run = cpu_bench.FullRun(args.workload, procs)
+        try:
+            run.step()
+            times = [run.step() for _ in range(2)]
+        finally:
+            run.close()
+        sec = statistics.median(times)
+        line["cpu_baseline"] = {"value": 1.0 / sec, "unit": "runs/s", "cores": procs, "kind": run.kind,
+                                "sample": run.describe(f"{args.workload.upper()} in full",
+                                                      "one run = 1") + f"; median {sec:.2f} s per run",
+                                "gflops_per_s": run.full_flops / run.r / sec / 1e9}
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -584,7 +655,7 @@ def main():
     ap.add_argument("--global-batch", type=int, default=BATCH,
                     help="UNet bench: samples of the whole job (64 = config C5; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the reference CPU timing (cpu_baseline)")
-    ap.add_argument("--workload", choices=["sampler", "vae", "text", "c4"], default=None,
+    ap.add_argument("--workload", choices=["sampler", "vae", "text", "c1", "c2", "c3", "c4"], default=None,
                     help="time one of the workloads around the UNet instead of the UNet step")
     args = ap.parse_args()
     if args.workload:

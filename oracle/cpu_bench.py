@@ -29,6 +29,31 @@ HEADS = 8
 CTX_LEN, CTX_DIM, TDIM = 77, 768, 1280
 
 
+def resnet_ops(cin, cout, h):
+    """Ops of one sample's SD ResNet block at h x h: GN + SiLU, conv3x3, time-embedding linear and
+    add, GN + SiLU, conv3x3, (1x1 shortcut), residual add."""
+    hw = h * h
+    ops = [("gn", cin, hw), ("ew", cin * hw), ("conv", cin, cout, 3, 1, h, h), ("lin", 1, TDIM, cout),
+           ("ew", cout * hw), ("gn", cout, hw), ("ew", cout * hw), ("conv", cout, cout, 3, 1, h, h)]
+    if cin != cout:
+        ops.append(("conv", cin, cout, 1, 1, h, h))
+    ops.append(("ew", cout * hw))
+    return ops
+
+
+def transformer_ops(c, h):
+    """Ops of one sample's SD spatial transformer at h x h with c channels: GN, proj_in, self-
+    attention (LN, QKV, SDPA, out + residual), cross-attention to the 77x768 context, GEGLU FFN,
+    proj_out + residual."""
+    s = h * h
+    d = c // HEADS
+    return [("gn", c, s), ("lin", s, c, c), ("ln", s, c), ("lin", s, c, 3 * c), ("attn", HEADS, s, s, d),
+            ("lin", s, c, c), ("ew", s * c), ("ln", s, c), ("lin", s, c, c), ("lin", CTX_LEN, CTX_DIM, 2 * c),
+            ("attn", HEADS, s, CTX_LEN, d), ("lin", s, c, c), ("ew", s * c), ("ln", s, c),
+            ("lin", s, c, 8 * c), ("ew", s * 4 * c), ("ew", s * 4 * c), ("lin", s, 4 * c, c), ("ew", s * c),
+            ("lin", s, c, c), ("ew", s * c)]
+
+
 def unet_ops(size=64):
     """The op list of one sample's SD-1.5 UNet forward (fp32, unfused, in the reference's op
     order).  Each entry: (kind, dims...) with
@@ -37,55 +62,37 @@ def unet_ops(size=64):
       lin   (rows, in, out)
       gn    (C, HW)      ln (rows, C)      ew (elements)      up (C, H, W) nearest 2x"""
     ops = []
-    hw = lambda h: h * h  # noqa: E731
-
-    def resnet(cin, cout, h):
-        ops.extend([("gn", cin, hw(h)), ("ew", cin * hw(h)), ("conv", cin, cout, 3, 1, h, h), ("lin", 1, TDIM, cout),
-                    ("ew", cout * hw(h)), ("gn", cout, hw(h)), ("ew", cout * hw(h)), ("conv", cout, cout, 3, 1, h, h)])
-        if cin != cout:
-            ops.append(("conv", cin, cout, 1, 1, h, h))
-        ops.append(("ew", cout * hw(h)))
-
-    def transformer(c, h):
-        s = hw(h)
-        d = c // HEADS
-        ops.extend([("gn", c, s), ("lin", s, c, c), ("ln", s, c), ("lin", s, c, 3 * c), ("attn", HEADS, s, s, d),
-                    ("lin", s, c, c), ("ew", s * c), ("ln", s, c), ("lin", s, c, c), ("lin", CTX_LEN, CTX_DIM, 2 * c),
-                    ("attn", HEADS, s, CTX_LEN, d), ("lin", s, c, c), ("ew", s * c), ("ln", s, c),
-                    ("lin", s, c, 8 * c), ("ew", s * 4 * c), ("ew", s * 4 * c), ("lin", s, 4 * c, c), ("ew", s * c),
-                    ("lin", s, c, c), ("ew", s * c)])
-
     ops.extend([("lin", 1, CHANS[0], TDIM), ("ew", TDIM), ("lin", 1, TDIM, TDIM), ("ew", TDIM)])
     h = size
     ops.append(("conv", 4, CHANS[0], 3, 1, h, h))
     c, skip = CHANS[0], [CHANS[0]]
     for lvl, co in enumerate(CHANS):
         for _ in range(2):
-            resnet(c, co, h)
+            ops.extend(resnet_ops(c, co, h))
             c = co
             if ATTN[lvl]:
-                transformer(c, h)
+                ops.extend(transformer_ops(c, h))
             skip.append(c)
         if lvl != len(CHANS) - 1:
             h //= 2
             ops.append(("conv", c, c, 3, 2, h, h))
             skip.append(c)
-    resnet(c, c, h)
-    transformer(c, h)
-    resnet(c, c, h)
+    ops.extend(resnet_ops(c, c, h))
+    ops.extend(transformer_ops(c, h))
+    ops.extend(resnet_ops(c, c, h))
     for lvl, co in reversed(list(enumerate(CHANS))):
         for _ in range(3):
             cin = c + skip.pop()
-            ops.append(("ew", cin * hw(h)))  # cat
-            resnet(cin, co, h)
+            ops.append(("ew", cin * h * h))  # cat
+            ops.extend(resnet_ops(cin, co, h))
             c = co
             if ATTN[lvl]:
-                transformer(c, h)
+                ops.extend(transformer_ops(c, h))
         if lvl != 0:
             ops.append(("up", c, h, h))
             h *= 2
             ops.append(("conv", c, c, 3, 1, h, h))
-    ops.extend([("gn", c, hw(h)), ("ew", c * hw(h)), ("conv", c, 4, 3, 1, h, h)])
+    ops.extend([("gn", c, h * h), ("ew", c * h * h), ("conv", c, 4, 3, 1, h, h)])
     return ops
 
 
@@ -100,6 +107,9 @@ def op_flops(op) -> float:
     if k == "lin":
         _, rows, i, o = op
         return 2.0 * rows * i * o
+    if k == "mm":
+        _, m, kk, n = op
+        return 2.0 * m * kk * n
     return 0.0
 
 
@@ -134,6 +144,10 @@ class _Ref:
             _, rows, i, o = op
             x, w, b = self.randn(_rows(rows, r), i), self.randn(o, i), self.randn(o)
             return lambda: self.F.linear(x, w, b)
+        if k == "mm":
+            _, m, kk, n = op
+            a, b2 = self.randn(_rows(m, r), kk), self.randn(kk, n)
+            return lambda: self.m.matmul(a, b2)
         if k == "gn":
             _, c, hw = op
             x, w, b = self.randn(1, c, _rows(hw, r), 1), self.randn(c), self.randn(c)
@@ -178,6 +192,10 @@ class _Port:
             _, rows, i, oo = op
             x, w, b = self.randn(_rows(rows, r), i), self.randn(oo, i), self.randn(oo)
             return lambda: o.linear_f32(x, w, b)
+        if k == "mm":
+            _, m, kk, n = op
+            a, b2 = self.randn(_rows(m, r), kk), self.randn(kk, n)
+            return lambda: o.matmul_f32(a, b2)
         if k == "gn":
             _, c, hw = op
             x = self.randn(1, c, _rows(hw, r), 1)
@@ -211,12 +229,13 @@ def _worker(conn, ops, r):
         conn.send(("done", time.perf_counter() - t0))
 
 
-class SampledUNet:
-    """P worker processes, each owning a FLOP-balanced share of the sampled op list."""
+class SampledOps:
+    """P worker processes, each owning a FLOP-balanced share of a sampled op list (one sample's ops;
+    every op on 1/r of its output rows)."""
 
-    def __init__(self, processes: int, r: int, size: int = 64):
+    def __init__(self, ops, processes: int, r: int):
         self.r, self.processes = r, max(1, processes)
-        ops = unet_ops(size)
+        self.nops = len(ops)
         self.full_flops = sum(op_flops(o) for o in ops)
         shares: list[list] = [[] for _ in range(self.processes)]
         load = [0.0] * self.processes
@@ -252,11 +271,43 @@ class SampledUNet:
         for p in self.procs:
             p.join(timeout=10)
 
-    def describe(self) -> str:
-        return (f"every op of one sample's SD-1.5 UNet forward (fp32; {len(unet_ops())} ops: conv2d, linear, sdpa, "
-                f"group/layer norm, silu/gelu, add/mul/cat, interpolate) at full widths on 1/{self.r} of each op's "
-                f"output rows, spread over {self.processes} single-threaded processes; a C5 step (64 samples) = "
-                f"64 x {self.r} sampled steps")
+    def describe(self, what="one sample's SD-1.5 UNet forward", unit="a C5 step (64 samples) = 64") -> str:
+        return (f"every op of {what} (fp32; {self.nops} ops: conv2d, linear, sdpa, group/layer norm, silu/gelu, "
+                f"add/mul/cat, interpolate) at full widths on 1/{self.r} of each op's output rows, spread over "
+                f"{self.processes} single-threaded processes; {unit} x {self.r} sampled steps")
+
+
+class SampledUNet(SampledOps):
+    """The sampled op list of one sample's SD-1.5 UNet forward."""
+
+    def __init__(self, processes: int, r: int, size: int = 64):
+        super().__init__(unet_ops(size), processes, r)
+
+
+def config_ops(name: str):
+    """One run of a BASELINE configuration as a list of ops: C1 the 2048^2 fp32 matmul, C2 the SD
+    ResNet block (GN -> SiLU -> conv3x3 -> GN -> SiLU -> conv3x3 + residual) on [2, 320, 64, 64],
+    C3 the attention block (self-attention over 4096 tokens, cross-attention to 77 projected context
+    tokens, GEGLU FFN) on [2, 4096, 320]."""
+    if name == "c1":
+        return [("mm", 2048, 2048, 2048)]
+    if name == "c2":
+        one = [("gn", 320, 4096), ("ew", 320 * 4096), ("conv", 320, 320, 3, 1, 64, 64), ("gn", 320, 4096),
+               ("ew", 320 * 4096), ("conv", 320, 320, 3, 1, 64, 64), ("ew", 320 * 4096)]
+        return one * 2
+    if name == "c3":
+        return transformer_ops(320, 64)[2:-2] * 2  # without GroupNorm / proj_in and proj_out / residual
+    raise ValueError(name)
+
+
+class FullRun(SampledOps):
+    """A whole configuration on all host cores: every op cut into r row slices (each slice the
+    reference's own op on 1/r of the rows), the slices spread over the processes, so one step
+    computes the full configuration."""
+
+    def __init__(self, name: str, processes: int, r: int = 32):
+        super().__init__(config_ops(name) * r, processes, r)
+        self.name = name
 
 
 def default_r(cores: int) -> int:
