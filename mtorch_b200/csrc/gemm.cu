@@ -269,8 +269,14 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = (A_BYTES + B_STAGE_BYTES) * OPS;
   static constexpr int ST_BYTES = TST ? kStoreBytes : 0;
   // TST: the staging buffers come on top of the usual ring where the 227 KB limit allows
-  static constexpr int STAGES_RAW = TST ? (226 * 1024 - ST_BYTES) / STAGE_BYTES : (200 * 1024) / STAGE_BYTES;
+  // (320-wide tiles: 56 KB stages, four of them fill the 227 KB limit)
+  static constexpr int STAGES_RAW = TST ? (226 * 1024 - ST_BYTES) / STAGE_BYTES
+                                        : (BN > 256 ? 224 * 1024 : 200 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
+  // tiles wider than 256 columns (a single MMA's and a TMA box's limit) use two halves: two B
+  // loads and two N = BN / 2 MMAs per K step, and one TMEM accumulator instead of two
+  static constexpr bool SPLIT_N = BN > 256;
+  static constexpr int NBUF = 2 * BN <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = (2 * BN <= 32)    ? 32
                                    : (2 * BN <= 64)  ? 64
                                    : (2 * BN <= 128) ? 128
@@ -303,6 +309,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   static_assert(!TST || (!TF32 && !CONV && !PAIR), "TMA-store epilogue: plain 16-bit GEMMs");
   static_assert(!BRES || (!TF32 && !CONV), "B-resident variant: 16-bit GEMMs only");
   static_assert(!PAIR || (!TF32 && !BRES), "CTA-pair variant: 16-bit streaming GEMMs only");
+  static_assert(!Cfg::SPLIT_N || (!TF32 && !BRES && !PAIR), "320-wide tiles: 16-bit streaming GEMMs only");
   const int STAGES = BRES ? tp.a_stages : Cfg::STAGES;
   // stage s: A at stage_base + s * STAGE_BYTES; B (not BRES) right after it
   constexpr int STAGE_BYTES = BRES ? Cfg::A_BYTES : Cfg::STAGE_BYTES;
@@ -430,9 +437,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               // second source of a channel concatenation: its own channel coordinate
               tma_load_4d(sa, &tmAlo, &full[stage], (cc - tp.c_split) * tp.bk, wx, hy, i0);
               tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, 0);
+              if (Cfg::SPLIT_N) tma_load_3d(sb + Cfg::B_BYTES / 2, &tmB, &full[stage], kk * tp.bk, n0 + BN / 2, 0);
             } else {
               tma_load_4d(sa, &tmA, &full[stage], cx, wx, hy, i0);
               tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, 0);
+              if (Cfg::SPLIT_N) tma_load_3d(sb + Cfg::B_BYTES / 2, &tmB, &full[stage], kk * tp.bk, n0 + BN / 2, 0);
             }
             if (TF32) {
               tma_load_4d(salo, &tmAlo, &full[stage], cx, wx, hy, i0);
@@ -447,6 +456,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             } else {
               tma_load_3d(sa, &tmA, &full[stage], kk * tp.bk, mt * kBM, ab);
               if (!BRES) tma_load_3d(sb, &tmB, &full[stage], kk * tp.bk, n0, bb);
+              if (Cfg::SPLIT_N) tma_load_3d(sb + Cfg::B_BYTES / 2, &tmB, &full[stage], kk * tp.bk, n0 + BN / 2, bb);
             }
             if (TF32) {
               tma_load_3d(salo, &tmAlo, &full[stage], kk * tp.bk, mt * kBM, ab);
@@ -468,8 +478,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int local = 0;
       if (BRES && blockIdx.x < total_tiles && !mbar_wait(b_full, 0, 4, abort_flag)) local = -1;
       for (int t = tile0; local >= 0 && t < total_tiles && !*abort_flag; t += tstep, ++local) {
-        const int buf = local & 1;
-        const uint32_t tph = (local >> 1) & 1;
+        const int buf = Cfg::NBUF == 2 ? (local & 1) : 0;
+        const uint32_t tph = Cfg::NBUF == 2 ? ((local >> 1) & 1) : (local & 1);
         if (!mbar_wait(&tempty[buf], tph ^ 1, 2, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
@@ -492,6 +502,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               umma_tf32(d_tmem, ad, bd, idesc, acc);
               umma_tf32(d_tmem, ad, sdesc_sw128(blo_addr + k * 32), idesc, 1u);
               umma_tf32(d_tmem, sdesc_sw128(alo_addr + k * 32), bd, idesc, 1u);
+            } else if (Cfg::SPLIT_N) {
+              umma_f16(d_tmem, ad, bd, idesc, acc);
+              umma_f16(d_tmem + BN / 2, ad, sdesc_sw128(b_addr + Cfg::B_BYTES / 2 + k * 32), idesc, acc);
             } else {
               umma_f16(d_tmem, ad, bd, idesc, acc);
             }
@@ -537,8 +550,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       sbuf ^= 1;
     };
     for (int t = tile0; t < total_tiles; t += tstep, ++local) {
-      const int buf = local & 1;
-      const uint32_t tph = (local >> 1) & 1;
+      const int buf = Cfg::NBUF == 2 ? (local & 1) : 0;
+      const uint32_t tph = Cfg::NBUF == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!mbar_wait(&tfull[buf], tph, 4, abort_flag)) break;
       tc_fence_after();
       int b, mt, nt;
@@ -806,7 +819,7 @@ static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
     if (e != cudaSuccess) return fail(MT_ERR_LAUNCH, "gemm_sm100 (CTA pairs): %s", cudaGetErrorString(e));
     return check_launch("gemm_sm100_pair");
   }
-  const uint32_t idesc = make_idesc(fmt, kBM, BN);
+  const uint32_t idesc = make_idesc(fmt, kBM, Cfg::SPLIT_N ? BN / 2 : BN);
   kern<<<grid, kGemmThreads, smem, st>>>(L.a, L.b, L.alo, L.blo, TST ? L.d : L.a, L.tp, L.ep, idesc);
   return check_launch("gemm_sm100");
 }
@@ -870,6 +883,7 @@ static int dispatch(GemmLaunch& L, cudaStream_t st) {
       case 64: return launch_variant<64, false, true>(L, st);
       case 128: return launch_variant<128, false, true>(L, st);
       case 160: return launch_variant<160, false, true>(L, st);
+      case 320: return launch_variant<320, false, true>(L, st);
       default: return launch_variant<256, false, true>(L, st);
     }
   }
@@ -913,8 +927,9 @@ static int pick_bn(int64_t N, int kind, bool geglu, bool conv) {
   static const int forced = [] {
     const char* e = getenv("MT_GEMM_BN");
     const int v = e ? atoi(e) : 0;
-    return (v == 64 || v == 128 || v == 160 || v == 256) ? v : 0;
+    return (v == 64 || v == 128 || v == 160 || v == 256 || v == 320) ? v : 0;
   }();
+  if (forced == 320 && (geglu || !conv)) return 256;  // 320-wide tiles: implicit convolutions only
   if (forced && !(geglu && forced % 128)) return forced;
   if (geglu) return N % 256 == 0 ? 256 : 128;
   if (N <= 64) return 64;
@@ -1367,8 +1382,18 @@ static int plan_conv(const mt_conv2d_desc& d, WsCursor& ws, bool run, cudaStream
   } else if (!tf32) {
     L->bn = narrow_bn(L->bn, d.K, tp.num_m_tiles, false);
   }
+  // 320-wide tiles (one TMEM accumulator, two N = 160 MMAs per K step) for 3x3 convolutions with
+  // output channels in multiples of 320: 0.77-0.90 of the bf16 peak against 0.57-0.72 for the 160 /
+  // 256-wide tiles at the UNet's 64x64 and 32x32 levels, and faster at 16x16; not at 8x8, where the
+  // split-K tiles are short and the accumulator's drain is not hidden, nor with fewer tiles than
+  // SMs (measured; same box).  MT_GEMM_BN forces a width; MT_GEMM_NO_BN320 keeps the old choice.
+  static const bool bn320_off = getenv("MT_GEMM_NO_BN320") != nullptr || getenv("MT_GEMM_BN") != nullptr;
+  if (!bn320_off && !tf32 && implicit && d.K % 320 == 0 && d.R * d.S > 1 && d.P * d.Q >= 256 &&
+      (int64_t)tp.num_m_tiles * (d.K / 320) >= num_sms())
+    L->bn = 320;
   tp.num_n_tiles = (int)((d.K + L->bn - 1) / L->bn);
-  if (!rc) rc = map_kmajor(&L->b, d.dtype, wp, Kg, d.K, 1, Kg, 0, L->bn);
+  // (320-wide tiles load B in two 160-row boxes)
+  if (!rc) rc = map_kmajor(&L->b, d.dtype, wp, Kg, d.K, 1, Kg, 0, L->bn > 256 ? L->bn / 2 : L->bn);
   L->b_ptr = wp; L->b_K = Kg; L->b_rows = d.K; L->b_batch = 1; L->b_pitch = Kg; L->b_bstride = 0;
   if (!rc && tf32) rc = map_kmajor(&L->blo, MT_F32, wlo, Kg, d.K, 1, Kg, 0, L->bn);
   if (rc) return rc;
