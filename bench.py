@@ -35,8 +35,8 @@ H = W = 64
 CTX = 77
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch per sample, from one ncu
 # capture of `bench.py --kernel attn|conv --batch 64` (the ncu summaries under profiles/): 654.3 MB
-# and 291.2 MB per 64-sample launch.
-DRAM_BYTES_PER_SAMPLE = {"attn": (503461632 + 150793472) / 64, "conv": (169972224 + 121186816) / 64}
+# and 296.6 MB per 64-sample launch.
+DRAM_BYTES_PER_SAMPLE = {"attn": (503461632 + 150793472) / 64, "conv": (169706752 + 126914048) / 64}
 METRIC = "UNet denoise steps/s (SD-1.5 shape, bf16, batch 64 latents 64x64, context 77x768)"
 
 
@@ -338,7 +338,7 @@ def run_ours(args):
         memory_format=mt.channels_last)
     conv_ms = timed(lambda: conv(xin))  # input 168 MB at nb = 64 > L2
     conv_ach = 2.0 * nb * H * W * 320 * 320 * 9 / (conv_ms * 1e-3) / 1e12
-    roofline_conv = {"bound": "tensor", "kernel": f"gemm_sm100_kernel<160,bf16,implicit conv> (3x3 320->320, "
+    roofline_conv = {"bound": "tensor", "kernel": f"gemm_sm100_kernel<320,bf16,implicit conv> (3x3 320->320, "
                      f"64x64, batch {nb})", "achieved": conv_ach, "peak": tf_burst, "unit": "TFLOP/s",
                      "frac": conv_ach / tf_burst, "peak_kind": f"{peak_kind} bf16 burst",
                      "traffic": DRAM_BYTES_PER_SAMPLE["conv"] * nb, "ms_per_launch": conv_ms}
