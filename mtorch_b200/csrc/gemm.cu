@@ -829,7 +829,7 @@ static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
 // and every CTA gets at least 8 tiles to amortise its B load.  A_stages is set as a side effect.
 static bool use_bres(GemmLaunch& L) {
   static const bool off = getenv("MT_GEMM_NO_BRES") != nullptr;
-  if (off || L.kind == MT_F32 || L.conv || L.tp.batch != 1) return false;
+  if (off || L.kind == MT_F32 || L.conv || L.tp.batch != 1 || L.bn > 256) return false;
   const int b_bytes = L.bn * 128 * L.tp.k_iters;
   const int stages = std::min(kMaxResStages, (kResBytes - (L.tst ? kStoreBytes : 0) - b_bytes) / (kBM * 128));
   if (stages < 3) return false;
@@ -900,6 +900,7 @@ static int dispatch(GemmLaunch& L, cudaStream_t st) {
       case 64: return launch_variant<64, false, false, false, false, true>(L, st);
       case 128: return launch_variant<128, false, false, false, false, true>(L, st);
       case 160: return launch_variant<160, false, false, false, false, true>(L, st);
+      case 320: return launch_variant<320, false, false, false, false, true>(L, st);
       default: return launch_variant<256, false, false, false, false, true>(L, st);
     }
   }
@@ -915,6 +916,7 @@ static int dispatch(GemmLaunch& L, cudaStream_t st) {
     case 64: return launch_variant<64, false, false>(L, st);
     case 128: return launch_variant<128, false, false>(L, st);
     case 160: return launch_variant<160, false, false>(L, st);
+    case 320: return launch_variant<320, false, false>(L, st);
     default: return launch_variant<256, false, false>(L, st);
   }
 }
@@ -929,7 +931,7 @@ static int pick_bn(int64_t N, int kind, bool geglu, bool conv) {
     const int v = e ? atoi(e) : 0;
     return (v == 64 || v == 128 || v == 160 || v == 256 || v == 320) ? v : 0;
   }();
-  if (forced == 320 && (geglu || !conv)) return 256;  // 320-wide tiles: implicit convolutions only
+  if (forced == 320 && geglu) return 256;  // GEGLU tiles pair 64-column value / gate groups
   if (forced && !(geglu && forced % 128)) return forced;
   if (geglu) return N % 256 == 0 ? 256 : 128;
   if (N <= 64) return 64;
@@ -1110,7 +1112,7 @@ int run_gemm(const mt_gemm_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st)
   if (d.dtype != MT_F32) L.bn = narrow_bn(L.bn, d.N, (int64_t)((d.M + kBM - 1) / kBM) * d.batch, geglu);
   const int64_t a_b = p.a_batched ? d.batch : 1, b_b = p.b_batched ? d.batch : 1;
   rc = map_kmajor(&L.a, d.dtype, p.A, d.K, d.M, a_b, p.lda, p.sa, kBM);
-  if (!rc) rc = map_kmajor(&L.b, d.dtype, p.B, d.K, d.N, b_b, p.ldb, p.sb, L.bn);
+  if (!rc) rc = map_kmajor(&L.b, d.dtype, p.B, d.K, d.N, b_b, p.ldb, p.sb, L.bn > 256 ? L.bn / 2 : L.bn);
   L.b_ptr = p.B; L.b_K = d.K; L.b_rows = d.N; L.b_batch = b_b; L.b_pitch = p.ldb; L.b_bstride = p.sb;
   if (!rc && d.dtype == MT_F32) {
     rc = map_kmajor(&L.alo, MT_F32, p.Alo, d.K, d.M, a_b, p.Kp, d.M * p.Kp, kBM);
