@@ -58,6 +58,9 @@ struct EpiParams {
   int bias_vec;  // bias rows 16-byte aligned and bf16 / fp32: vector loads
   float* part;   // split K: [k_splits][M rows][N] fp32 partial sums (rows in (n, p, q) order)
   int64_t part_stride;
+  // TMA-store epilogue of a plain GEMM: the residual is read through a tensor map (32 x 32 boxes,
+  // 64-byte swizzle, passed in the tmAlo slot) into the output staging buffers, a tile ahead
+  int res_tma;
 };
 
 // 256-bit global accesses (sm_100): one instruction covers a whole 32-byte sector, so a warp whose
@@ -226,9 +229,19 @@ __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b,
 
 // Shared memory of the B-resident variant's operand region (B tile + A stages).
 constexpr int kResBytes = 200 * 1024;
-// TMA-store epilogue: each epilogue warp stages its 32 x 32 output chunk in one of two private
-// 2 KB shared-memory buffers (64-byte swizzle) and stores it with one bulk tensor store.
-constexpr int kStoreBytes = 8 * 2 * 2048;
+// TMA-store epilogue: each epilogue warp stages its 32 x 32 output chunks in private 2 KB
+// shared-memory buffers (64-byte swizzle), one per chunk the warp owns in a tile (at least two),
+// and stores each with one bulk tensor store.  With a residual, the residual chunk is first
+// TMA-loaded into the same buffer (prefetched a tile ahead), added, and overwritten by the output.
+// Only the residual instance (TST == 2, streaming column tiles of 128 / 160 / 256) has more than two
+// buffers per warp: the others keep the room for their operand ring.
+__host__ __device__ constexpr int store_bufs(int bn, bool rt) {
+  return rt && (bn / 32 + 1) / 2 > 2 ? (bn / 32 + 1) / 2 : 2;
+}
+__host__ __device__ constexpr int store_bytes(int bn, bool rt) { return 8 * store_bufs(bn, rt) * 2048; }
+// barriers of the GEMM kernel: ring (<= 8 + 8), TMEM (2 + 2), resident B, TMEM slot + abort flag,
+// residual buffers (8 warps x <= 5)
+constexpr int kGemmBarBytes = 512;
 
 __device__ __forceinline__ void gemm_fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -241,6 +254,7 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Stage 32 output values of this lane's row (bf16 / f16) into the warp's 32 x 64-byte buffer with
@@ -259,7 +273,7 @@ __device__ __forceinline__ void stage_row32(uint8_t* buf, int lane, int dtype, c
 }
 constexpr int kMaxResStages = 8;
 
-template <int BN, bool TF32, bool PAIR = false, bool TST = false>
+template <int BN, bool TF32, bool PAIR = false, int TST = 0>
 struct GemmCfg {
   static constexpr int A_BYTES = kBM * 128;
   static constexpr int B_BYTES = BN * 128;
@@ -267,7 +281,8 @@ struct GemmCfg {
   static constexpr int B_STAGE_BYTES = PAIR ? B_BYTES / 2 : B_BYTES;
   static constexpr int OPS = TF32 ? 2 : 1;
   static constexpr int STAGE_BYTES = (A_BYTES + B_STAGE_BYTES) * OPS;
-  static constexpr int ST_BYTES = TST ? kStoreBytes : 0;
+  static constexpr int ST_BUFS = store_bufs(BN, TST == 2);
+  static constexpr int ST_BYTES = TST ? store_bytes(BN, TST == 2) : 0;
   // TST: the staging buffers come on top of the usual ring where the 227 KB limit allows
   // (320-wide tiles: 56 KB stages, four of them fill the 227 KB limit)
   static constexpr int STAGES_RAW = TST ? (226 * 1024 - ST_BYTES) / STAGE_BYTES
@@ -282,9 +297,10 @@ struct GemmCfg {
                                    : (2 * BN <= 128) ? 128
                                    : (2 * BN <= 256) ? 256
                                                      : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + ST_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + ST_BYTES + 1024 /*align*/ + kGemmBarBytes;
   // B-resident variant: [B tile, all K chunks][A stages] within kResBytes, barriers after it.
-  static constexpr int RES_SMEM_BYTES = kResBytes + 1024 + 256;
+  static constexpr int RES_SMEM_BYTES = kResBytes + 1024 + kGemmBarBytes;
+  static_assert(SMEM_BYTES <= 227 * 1024 && RES_SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
 // BRES (B resident): every tile of this CTA has the same column tile (the grid is a multiple of
@@ -299,7 +315,7 @@ struct GemmCfg {
 //
 // TST (TMA-store epilogue, plain GEMMs with 16-bit output): output chunks go through per-warp
 // shared-memory buffers and bulk tensor stores (tmD) instead of per-row global stores.
-template <int BN, bool TF32, bool CONV, bool BRES, bool PAIR = false, bool TST = false>
+template <int BN, bool TF32, bool CONV, bool BRES, bool PAIR = false, int TST = 0>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmAlo, const __grid_constant__ CUtensorMap tmBlo,
@@ -307,6 +323,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                       const uint32_t idesc) {
   using Cfg = GemmCfg<BN, TF32, PAIR, TST>;
   static_assert(!TST || (!TF32 && !CONV && !PAIR), "TMA-store epilogue: plain 16-bit GEMMs");
+  static_assert(TST != 2 || (!BRES && BN <= 256), "residual through the store buffers: streaming tiles");
   static_assert(!BRES || (!TF32 && !CONV), "B-resident variant: 16-bit GEMMs only");
   static_assert(!PAIR || (!TF32 && !BRES), "CTA-pair variant: 16-bit streaming GEMMs only");
   static_assert(!Cfg::SPLIT_N || (!TF32 && !BRES && !PAIR), "320-wide tiles: 16-bit streaming GEMMs only");
@@ -317,7 +334,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sbres = smem;  // BRES: k_iters chunks of B_BYTES
   uint8_t* stage_base = BRES ? smem + tp.k_iters * Cfg::B_BYTES : smem;
-  // TST staging: after the ring, or (BRES) the last kStoreBytes of the resident region (the host
+  // TST staging: after the ring, or (BRES) the last store_bytes(BN, false) of the resident region (the host
   // sizes the B tile + A stages to leave it free)
   uint8_t* sstore = BRES ? smem + kResBytes - Cfg::ST_BYTES : smem + Cfg::STAGES * Cfg::STAGE_BYTES;
   uint64_t* full =
@@ -328,6 +345,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* b_full = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(tmem_slot + 2);  // TST residual: [8 warps][ST_BUFS]
+  static_assert((2 * 8 + 2 + 2 + 1 + 1 + 8 * Cfg::ST_BUFS) * 8 <= kGemmBarBytes, "GEMM barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -340,13 +359,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty[b], PAIR ? 512 : 256);  // pair: both CTAs' epilogue threads
     }
     mbar_init(b_full, 1);
+    if (TST == 2)
+      for (int i = 0; i < 8 * Cfg::ST_BUFS; ++i) mbar_init(&rbar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (TF32 || (CONV && tp.c_split > 0)) {
+    if (TF32 || (CONV && tp.c_split > 0) || TST == 2) {
       tma_prefetch_desc(&tmAlo);
       tma_prefetch_desc(&tmBlo);
     }
@@ -535,6 +556,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int64_t n_out = geglu ? ep.N / 2 : ep.N;
     int local = 0;
     int sbuf = 0;  // TST: which of this warp's two staging buffers is next
+    // TST + residual map: buffer i of this warp holds chunk i (tile columns half*32 + 64 i) of the
+    // tile being stored and, once that store has read it, the residual chunk i of the warp's next
+    // tile.  `rpend` / `rpar`: per buffer, a residual load in flight / the parity it completes.
+    constexpr bool rtma = TST == 2;
+    const int nch = (BN - half * 32 + 63) / 64;
+    uint64_t* rbar_w = rbar + (warp - 2) * Cfg::ST_BUFS;
+    uint8_t* sbw = sstore + (warp - 2) * Cfg::ST_BUFS * 2048;
+    uint32_t rpend = 0, rpar = 0;
+    // whether chunk i of tile tt exists (columns below N, this warp's rows below M)
+    auto res_chunk = [&](int tt, int i, int& x, int& y, int& z) -> bool {
+      int b2, mt2, nt2;
+      decode(tt, b2, mt2, nt2);
+      x = nt2 * BN + half * 32 + 64 * i;
+      y = mt2 * kBM + quarter * 32;
+      z = b2;
+      return x < n_out && y < ep.M;
+    };
+    // every lane keeps the bookkeeping; lane 0 issues the load
+    auto res_issue = [&](int tt, int i) {
+      int x, y, z;
+      if (tt < total_tiles && res_chunk(tt, i, x, y, z)) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&rbar_w[i], 2048);
+          tma_load_3d(sbw + i * 2048, &tmAlo, &rbar_w[i], x, y, z);
+        }
+        rpend |= 1u << i;
+      }
+    };
+    if (rtma)
+      for (int i = 0; i < nch; ++i) res_issue(tile0, i);
     // TST: the warp's 32 output rows x 32 columns via shared memory and one bulk tensor store
     auto store_chunk = [&](const float (&v)[32], int64_t col0, int mt, int b) {
       uint8_t* sb = sstore + ((warp - 2) * 2 + sbuf) * 2048;
@@ -604,6 +655,78 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             row_store(part, MT_F32, m_lin * ep.N + col0, nvalid, true, v);
           }
         }
+      } else if (rtma) {
+        // plain GEMM, TMA-store epilogue, residual from the prefetched buffers (mode 0, no GEGLU)
+        const int tnext = t + tstep;
+        uint32_t issued = 0;  // buffers already refilled for tnext
+#pragma unroll 1
+        for (int i = 0; i < nch; ++i) {
+          const int c0 = half * 32 + 64 * i;
+          uint32_t r[32];
+          tmem_ld32(taddr + c0, r);
+          tmem_ld_wait();
+          const int64_t col0 = (int64_t)nt * BN + c0;
+          if (col0 >= n_out) break;  // chunks past N: none after this one either
+          const int nvalid = n_out - col0 < 32 ? (int)(n_out - col0) : 32;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
+          if (ep.bias)
+            row_load_add(ep.bias, ep.bias_dtype, i0 * ep.bias_bstride + col0, nvalid, ep.bias_vec != 0, 1.f, v);
+          if (ep.C && valid) row_load_add(ep.C, ep.out_dtype, offC + col0, nvalid, vec, ep.beta, v);
+          if (ep.act == MT_EPI_GELU) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) gelu_poly_pair(v[j], v[j + 1]);
+          } else if (ep.act == MT_EPI_SILU) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+          } else if (ep.act == MT_EPI_QUICK_GELU) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = v[j] * (1.0f / (1.0f + expf(-__fmul_rn(v[j], 1.702f))));
+          }
+          uint8_t* sb = sbw + i * 2048;
+          if ((rpend >> i) & 1) {
+            const bool got = mbar_wait(&rbar_w[i], (rpar >> i) & 1, 19, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) break;
+            rpend &= ~(1u << i);
+            rpar ^= 1u << i;
+            // this lane's row: 16-byte chunk k at k ^ ((lane >> 1) & 3) (64-byte swizzle)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint4 u = *reinterpret_cast<const uint4*>(sb + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16));
+              const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float2 f;
+                if (ep.out_dtype == MT_BF16) {
+                  f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+                } else {
+                  f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+                }
+                v[8 * k + 2 * j] += f.x;
+                v[8 * k + 2 * j + 1] += f.y;
+              }
+            }
+            __syncwarp();  // every lane has read the residual before the buffer is overwritten
+          }
+          stage_row32(sb, lane, ep.out_dtype, v);
+          gemm_fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmD, sb, (int)col0, mt * kBM + quarter * 32, b);
+            bulk_commit();
+            if (i > 0) bulk_wait_read1();  // the store of chunk i - 1 has read its buffer
+          }
+          if (i > 0) {  // refill buffer i - 1 with the residual of tnext
+            res_issue(tnext, i - 1);
+            issued |= 1u << (i - 1);
+          }
+        }
+        if (lane == 0) bulk_wait_read0();
+        for (int i = 0; i < nch; ++i)
+          if (!((issued >> i) & 1) && !((rpend >> i) & 1)) res_issue(tnext, i);
+        __syncwarp();
+        if (*abort_flag) break;
       } else if (!geglu) {
 #pragma unroll 1
         for (int c0 = half * 32; c0 < BN; c0 += 64) {
@@ -687,6 +810,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_arrive(&tempty[buf]);
     }
     if (TST && lane == 0) bulk_wait_all();  // this warp's stores are done before the CTA exits
+    if (rtma && lane == 0) {
+      // after an abort: let residual loads still in flight land (bounded) before the CTA exits
+      for (int i = 0; i < nch; ++i) {
+        if (!((rpend >> i) & 1)) continue;
+        const long long start = clock64();
+        while (!mbar_try_wait(&rbar_w[i], (rpar >> i) & 1) && clock64() - start < kWaitBudgetCycles) {
+        }
+      }
+    }
   }
   __syncthreads();
   if (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal its barriers
@@ -776,7 +908,7 @@ struct GemmLaunch {
 static int map_kmajor(CUtensorMap* m, int dtype, const void* base, int64_t K, int64_t rows, int64_t batch,
                       int64_t pitch, int64_t bstride, int box_rows);
 
-template <int BN, bool TF32, bool CONV, bool BRES = false, bool PAIR = false, bool TST = false>
+template <int BN, bool TF32, bool CONV, bool BRES = false, bool PAIR = false, int TST = 0>
 static int launch_variant(const GemmLaunch& L, cudaStream_t st) {
   using Cfg = GemmCfg<BN, TF32, PAIR, TST>;
   constexpr int smem = BRES ? Cfg::RES_SMEM_BYTES : Cfg::SMEM_BYTES;
@@ -831,7 +963,7 @@ static bool use_bres(GemmLaunch& L) {
   static const bool off = getenv("MT_GEMM_NO_BRES") != nullptr;
   if (off || L.kind == MT_F32 || L.conv || L.tp.batch != 1 || L.bn > 256) return false;
   const int b_bytes = L.bn * 128 * L.tp.k_iters;
-  const int stages = std::min(kMaxResStages, (kResBytes - (L.tst ? kStoreBytes : 0) - b_bytes) / (kBM * 128));
+  const int stages = std::min(kMaxResStages, (kResBytes - (L.tst ? store_bytes(L.bn, false) : 0) - b_bytes) / (kBM * 128));
   if (stages < 3) return false;
   const int sms = num_sms(), nn = L.tp.num_n_tiles;
   if (nn > sms) return false;
@@ -888,6 +1020,16 @@ static int dispatch(GemmLaunch& L, cudaStream_t st) {
     }
   }
   if (L.tst) {
+    // the residual instance gives up a stage of the operand ring for its staging buffers: it pays
+    // for short reductions (measured: K = 640 gains 15 %, K = 1280 loses 3 %)
+    if (L.ep.res_tma && (L.bn == 128 || L.bn == 160 || L.bn == 256) && L.tp.k_iters <= 10 && !use_bres(L)) {
+      switch (L.bn) {
+        case 128: return launch_variant<128, false, false, false, false, 2>(L, st);
+        case 160: return launch_variant<160, false, false, false, false, 2>(L, st);
+        default: return launch_variant<256, false, false, false, false, 2>(L, st);
+      }
+    }
+    L.ep.res_tma = 0;
     if (use_bres(L)) {
       switch (L.bn) {
         case 64: return launch_variant<64, false, false, true, false, true>(L, st);
@@ -1159,6 +1301,15 @@ int run_gemm(const mt_gemm_desc& d, void* wsp, size_t ws_bytes, cudaStream_t st)
     uint64_t strides[2] = {(uint64_t)(d.ldd * oes), (uint64_t)((d.batch > 1 ? d.stride_d : d.M * d.ldd) * oes)};
     uint32_t box[3] = {32, 32, 1};
     L.tst = make_tensor_map(&L.d, d.out_dtype, 3, d.D, dims, strides, box, 64) == MT_OK;
+    // the residual through the same box geometry (MT_GEMM_RES_TMA=0 turns it off)
+    static const bool rt_off = [] {
+      const char* e = getenv("MT_GEMM_RES_TMA");
+      return e && e[0] == '0';
+    }();
+    if (L.tst && !rt_off && ep.res && !geglu && (d.batch == 1 || d.stride_r != 0)) {
+      uint64_t rstrides[2] = {(uint64_t)(d.ldr * oes), (uint64_t)((d.batch > 1 ? d.stride_r : d.M * d.ldr) * oes)};
+      ep.res_tma = make_tensor_map(&L.alo, d.out_dtype, 3, d.residual, dims, rstrides, box, 64) == MT_OK;
+    }
   }
   return dispatch(L, st);
 }

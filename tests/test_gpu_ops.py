@@ -247,6 +247,43 @@ def test_small_problem_tiling_is_batch_invariant():
     np.testing.assert_array_equal(full[:2], mt.conv2d(xi[:2], wc, None, 1, 1).numpy())
 
 
+@pytest.mark.parametrize("M,K,N,dtype,act", [
+    (76000, 320, 320, "bfloat16", "none"),   # B-resident tiles (per-row residual loads); last tile 96 rows
+    (40000, 320, 640, "bfloat16", "gelu"),   # residual map, several tiles per CTA (prefetched a tile ahead);
+                                             # last tile 64 rows: two warps' rows all past M
+    (5000, 640, 200, "float16", "none"),     # N = 200: partial 32-column chunk, chunks past N
+    (300, 640, 1280, "bfloat16", "silu"),    # fewer tiles than CTAs
+    (2000, 1280, 1280, "bfloat16", "none"),  # long K: per-row residual loads
+])
+def test_linear_residual_epilogue(M, K, N, dtype, act):
+    """D = act(x W^T + b) + residual with the residual read through a tensor map into the output
+    staging buffers (TMA-store epilogue), against the oracle on the same 16-bit inputs."""
+    from mtorch_b200 import _lib
+
+    x, w, b, r = rnd(M, K, seed=1), rnd(N, K, seed=2, scale=K ** -0.5), rnd(N, seed=3), rnd(M, N, seed=4)
+    rd = bf16_round if dtype == "bfloat16" else (lambda a: mt.tensor(a).to("float16").numpy())  # noqa: E731
+    pre = oracle.linear_f32(rd(x), rd(w), rd(b))
+    f = {"none": lambda a: a, "gelu": oracle.gelu_f32, "silu": oracle.silu_f32}[act]
+    epi = {"none": _lib.EPI_NONE, "gelu": _lib.EPI_GELU, "silu": _lib.EPI_SILU}[act]
+    got = mt.ops.linear(cu(x, dtype), cu(w, dtype), cu(b, dtype), epilogue=epi, residual=cu(r, dtype)).numpy()
+    check(got, f(pre) + rd(r), BF16_RTOL)
+
+
+def test_gemm_residual_batched_and_pitched():
+    """Batched GEMM with a per-batch residual, and a residual that is a column slice of a wider
+    matrix (row pitch > N): both through the residual tensor map."""
+    a, bm = rnd(3, 700, 256, seed=5), rnd(3, 256, 384, seed=6, scale=1 / 16)
+    r = rnd(3, 700, 384, seed=7)
+    got = mt.ops.gemm(cu(a, "bfloat16"), cu(bm, "bfloat16"), residual=cu(r, "bfloat16")).numpy()
+    ref = np.stack([oracle.matmul_f32(bf16_round(a[i]), bf16_round(bm[i])) for i in range(3)]) + bf16_round(r)
+    check(got, ref, BF16_RTOL)
+    wide = cu(rnd(2000, 512, seed=8), "bfloat16")
+    x, w = rnd(2000, 320, seed=9), rnd(320, 320, seed=10, scale=320 ** -0.5)
+    got = mt.ops.linear(cu(x, "bfloat16"), cu(w, "bfloat16"), None, residual=wide[:, 64:384]).numpy()
+    ref = oracle.linear_f32(bf16_round(x), bf16_round(w)) + wide.numpy()[:, 64:384]
+    check(got, ref, BF16_RTOL)
+
+
 def test_linear_batch_independent():
     x = cu(rnd(3000, 320), "bfloat16")
     w = cu(rnd(640, 320, seed=1, scale=0.05), "bfloat16")
