@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(64 + 128 * NQ, 1)
 // for its previous PV product — only for the S tile it consumes.
 constexpr float kLazyThreshold = 8.0f;  // log2 of the largest p allowed before rescaling
 
-template <int DP, int DVP, bool F16, bool SUMCOL>
+template <int DP, int DVP, bool F16, bool SUMCOL, int PB>
 __global__ void __launch_bounds__(320, 1)
     fa_lazy_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const FaParams p) {
@@ -477,15 +477,19 @@ __global__ void __launch_bounds__(320, 1)
   constexpr uint32_t idesc_s = make_idesc(FMT, kFaBM, kFaBN);
   constexpr uint32_t idesc_o = make_idesc(FMT, kFaBM, DVP) | (1u << 16);
   static_assert(2 * 128 + 2 * DVP <= 512, "TMEM budget");
+  // PB P buffers per query tile (2 where shared memory allows): buffer and use number of tile j
+  static_assert(PB == 1 || PB == 2, "P buffers");
+  auto pbuf = [](int x, int j) { return x * PB + (PB == 2 ? (j & 1) : 0); };
+  auto puse = [](int j) { return PB == 2 ? (j >> 1) : j; };
 
   extern __shared__ uint8_t fa_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                    // [2][Q]
-  uint8_t* sP = sQ + NQ * Q_BYTES;       // [2 tiles][2 buffers][P]
+  uint8_t* sP = sQ + NQ * Q_BYTES;       // [2 tiles][PB buffers][P]
   // K and V in separate rings: a K tile is released once both QK^T products have read it, a V
   // tile only after both PV products, so loading K ahead never waits for the softmax.
   const int stages_k = p.stages, stages_v = p.stages_v;
-  uint8_t* sK = sP + NQ * 2 * P_BYTES;  // [stages_k][K]
+  uint8_t* sK = sP + NQ * PB * P_BYTES;  // [stages_k][K]
   uint8_t* sV = sK + stages_k * K_BYTES;  // [stages_v][V]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + stages_v * V_BYTES);
   uint64_t* q_full = bars;
@@ -614,17 +618,17 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t v_addr = smem_u32(sV + vs * V_BYTES);
           bool pok = true;
           for (int x = 0; x < NQ; ++x) {
-            if (!mbar_wait(&p_full[x * 2 + (jj & 1)], (jj >> 1) & 1, 25, abort_flag)) {
+            if (!mbar_wait(&p_full[pbuf(x, jj)], puse(jj) & 1, 25, abort_flag)) {
               pok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t pa = p_addr + (x * 2 + (jj & 1)) * P_BYTES;
+            const uint32_t pa = p_addr + pbuf(x, jj) * P_BYTES;
 #pragma unroll
             for (int kk = 0; kk < kFaBN / 16; ++kk)
               umma_f16(t_o0 + x * DVP, sdesc_none(pa + kk * 2 * kLbo, kLbo, kSbo),
                        sdesc_none(v_addr + kk * 256, 128, kFaBN * 16), idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
-            umma_commit(&p_free[x * 2 + (jj & 1)]);
+            umma_commit(&p_free[pbuf(x, jj)]);
           }
           if (!pok) break;
           umma_commit(&v_empty[vs]);
@@ -681,7 +685,7 @@ __global__ void __launch_bounds__(320, 1)
           // PV_{j-1} released P buffer (j-1)&1 (its use number (j-1)>>1); commits complete in issue
           // order, so this also covers every earlier PV.  Phases of p_free are consumed in order,
           // which keeps the parity test unambiguous.
-          if (!mbar_wait(&p_free[x * 2 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, 27, abort_flag)) {
+          if (!mbar_wait(&p_free[pbuf(x, j - 1)], puse(j - 1) & 1, 27, abort_flag)) {
             ok = false;
             break;
           }
@@ -701,11 +705,11 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       // the P buffer this tile writes was read by the PV two tiles back
-      if (!mbar_wait(&p_free[x * 2 + (j & 1)], ((j >> 1) & 1) ^ 1, 28, abort_flag)) {
+      if (!mbar_wait(&p_free[pbuf(x, j)], (puse(j) & 1) ^ 1, 28, abort_flag)) {
         ok = false;
         break;
       }
-      uint8_t* sPx = sP + (x * 2 + (j & 1)) * P_BYTES;
+      uint8_t* sPx = sP + pbuf(x, j) * P_BYTES;
       const uint64_t negm2 = f2_bits(-m_used, -m_used);
       uint64_t sum2 = f2_bits(0.f, 0.f);
 #pragma unroll 1
@@ -743,13 +747,13 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&p_full[x * 2 + (j & 1)]);
+      mbar_arrive(&p_full[pbuf(x, j)]);
       float s0, s1;
       f2_unpack(sum2, s0, s1);
       l_run += s0 + s1;
     }
     // final: O (all PV products accumulated) / l
-    if (ok && mbar_wait(&p_free[x * 2 + ((n_tiles - 1) & 1)], ((n_tiles - 1) >> 1) & 1, 29, abort_flag)) {
+    if (ok && mbar_wait(&p_free[pbuf(x, n_tiles - 1)], puse(n_tiles - 1) & 1, 29, abort_flag)) {
       tc_fence_after();
       float o[DVP];
 #pragma unroll
@@ -1110,10 +1114,11 @@ static int fa_launch(const mt_sdpa_desc& d, cudaStream_t st) {
   return check_launch("flash_attention_sm100");
 }
 
-// Launch of the lazy-rescale variant; returns false (not launched) when two KV stages do not fit.
-template <int DP, int DVP, bool F16, bool SUMCOL>
+// Launch of the lazy-rescale variant with PB P buffers per query tile; returns false (not
+// launched) when two KV stages do not fit.
+template <int DP, int DVP, bool F16, bool SUMCOL, int PB>
 static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched) {
-  constexpr int FIXED = 2 * (kFaBM * DP * 2 + 2 * kFaBM * kFaBN * 2);
+  constexpr int FIXED = 2 * (kFaBM * DP * 2 + PB * kFaBM * kFaBN * 2);
   constexpr int K_BYTES = kFaBN * DP * 2, V_BYTES = kFaBN * DVP * 2;
   constexpr int SMEM_MAX = 224 * 1024;
   const int stages_v = 2;
@@ -1122,7 +1127,7 @@ static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched
   *launched = false;
   if (stages_k < 2) return MT_OK;
   const int smem = FIXED + stages_k * K_BYTES + stages_v * V_BYTES + 2048 + 1024;
-  auto kern = fa_lazy_sm100_kernel<DP, DVP, F16, SUMCOL>;
+  auto kern = fa_lazy_sm100_kernel<DP, DVP, F16, SUMCOL, PB>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1222,7 +1227,12 @@ int sdpa_tc_path(const mt_sdpa_desc& d) {
   const bool two = d.Sq > kFaBM;
   static const bool no_short = getenv("MT_FA_NO_SHORT") != nullptr;
   if (d.Sk <= kFaBN && Dp <= 128 && !d.causal && d.mask_kind == 0 && !no_short) return MT_SDPA_PATH_TC_SHORT;
-  if (two && Dp == 48 && d.scale > 0 && !d.causal && d.mask_kind == 0 && !getenv("MT_FA_NO_LAZY"))
+  // the lazy variant (O in TMEM) for padded head dims up to 80 (MT_FA_LAZY_MAX lowers the limit)
+  static const int lazy_max = [] {
+    const char* e = getenv("MT_FA_LAZY_MAX");
+    return e ? atoi(e) : 80;
+  }();
+  if (two && Dp <= lazy_max && Dp <= 80 && d.scale > 0 && !d.causal && d.mask_kind == 0 && !getenv("MT_FA_NO_LAZY"))
     return MT_SDPA_PATH_TC_LAZY;
   return MT_SDPA_PATH_TC;
 }
@@ -1247,8 +1257,18 @@ static int fa_dispatch(const mt_sdpa_desc& d, int64_t Dp, bool lazy, cudaStream_
   const bool two = d.Sq > kFaBM;
   if (lazy) {
     bool launched = false;
-    const int rc = d.Dv <= 40 ? fa_lazy_launch<48, 48, F16, true>(d, st, &launched)
-                              : fa_lazy_launch<48, 48, F16, false>(d, st, &launched);
+    // double-buffered P up to head dim 48; one P buffer per query tile beyond (shared memory)
+    int rc = MT_OK;
+    switch (Dp) {
+      case 32: rc = d.Dv <= 24 ? fa_lazy_launch<32, 32, F16, true, 2>(d, st, &launched)
+                               : fa_lazy_launch<32, 32, F16, false, 2>(d, st, &launched); break;
+      case 48: rc = d.Dv <= 40 ? fa_lazy_launch<48, 48, F16, true, 2>(d, st, &launched)
+                               : fa_lazy_launch<48, 48, F16, false, 2>(d, st, &launched); break;
+      case 64: rc = d.Dv <= 56 ? fa_lazy_launch<64, 64, F16, true, 1>(d, st, &launched)
+                               : fa_lazy_launch<64, 64, F16, false, 1>(d, st, &launched); break;
+      default: rc = d.Dv <= 72 ? fa_lazy_launch<80, 80, F16, true, 1>(d, st, &launched)
+                               : fa_lazy_launch<80, 80, F16, false, 1>(d, st, &launched); break;
+    }
     if (rc || launched) return rc;
   }
   if (d.mask_kind != 0) {

@@ -421,20 +421,25 @@ def test_sdpa_bf16_causal(B, H, Sq, Sk, D):
     check(got, ref, BF16_RTOL)
 
 
-def test_sdpa_bf16_growing_scores_rescale():
+@pytest.mark.parametrize("D,dtype", [(40, "bfloat16"), (64, "bfloat16"), (80, "bfloat16"), (80, "float16"),
+                                     (72, "bfloat16"), (32, "bfloat16")])
+def test_sdpa_bf16_growing_scores_rescale(D, dtype):
     """Later key tiles score much higher than earlier ones, so the running maximum grows by far more
-    than the lazy-rescale threshold several times within a row."""
-    B, H, S, D = 2, 4, 640, 40
+    than the lazy-rescale threshold several times within a row.  Head dims 64 / 72 / 80 run the
+    lazy kernel with one P buffer per query tile (72: row sum from a ones column of V's padding)."""
+    B, H, S = 2, 4, 640
     q = rnd(B, H, S, D, scale=2.0)
     k = rnd(B, H, S, D, seed=1)
     k *= (1.0 + np.repeat(np.arange(S // 128), 128) * 1.5)[None, None, :, None].astype(np.float32)
     v = rnd(B, H, S, D, seed=2)
-    ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
-    got = mt.scaled_dot_product_attention(cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")).numpy()
-    check(got, ref, BF16_RTOL)
+    rd = bf16_round if dtype == "bfloat16" else (lambda a: mt.tensor(a).to("float16").numpy())  # noqa: E731
+    ref = oracle.sdpa_f32(rd(q), rd(k), rd(v))
+    qd, kd, vd = cu(q, dtype), cu(k, dtype), cu(v, dtype)
+    assert mt.ops.sdpa_path(qd, kd, vd) == "tc_lazy"
+    check(mt.scaled_dot_product_attention(qd, kd, vd).numpy(), ref, BF16_RTOL)
 
 
-@pytest.mark.parametrize("D", [40, 48])
+@pytest.mark.parametrize("D", [40, 48, 80])
 def test_sdpa_bf16_max_jumps_inside_key_tiles(D):
     """The score maximum jumps in the second half of key tiles (the P columns already written for
     the tile are rescaled) and the last key tile is ragged.  D 40 takes the row sum from the
@@ -482,7 +487,8 @@ def test_sdpa_bf16_padded_head_dims(B, H, Sq, Sk, D):
     extra columns zero-filled by TMA."""
     q, k, v = rnd(B, H, Sq, D), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
     qd, kd, vd = cu(q, "bfloat16"), cu(k, "bfloat16"), cu(v, "bfloat16")
-    assert mt.ops.sdpa_path(qd, kd, vd) == ("tc_short" if Sk <= 128 and D <= 128 else "tc")
+    lazy = Sq > 128 and D <= 80  # padded to 32 / 48 / 64 / 80
+    assert mt.ops.sdpa_path(qd, kd, vd) == ("tc_short" if Sk <= 128 and D <= 128 else "tc_lazy" if lazy else "tc")
     ref = oracle.sdpa_f32(bf16_round(q), bf16_round(k), bf16_round(v))
     check(mt.scaled_dot_product_attention(qd, kd, vd).numpy(), ref, BF16_RTOL)
 
@@ -499,7 +505,7 @@ def test_sdpa_path_of_unet_shapes():
         d = c // 8
         qkv = mt.empty(n * s, 3 * c, dtype="bfloat16", device="cuda")
         q, k, v = (heads(qkv[:, i * c:(i + 1) * c], n, s, 8, d) for i in range(3))
-        want = "tc_lazy" if d <= 48 and s > 128 else "tc"
+        want = "tc_lazy" if d <= 80 and s > 128 else "tc"
         assert mt.ops.sdpa_path(q, k, v) == want, (c, s)
         kv = mt.empty(n * 77, 2 * c, dtype="bfloat16", device="cuda")
         kc, vc = heads(kv[:, 0:c], n, 77, 8, d), heads(kv[:, c:2 * c], n, 77, 8, d)
