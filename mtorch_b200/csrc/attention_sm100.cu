@@ -808,21 +808,25 @@ __global__ void __launch_bounds__(320, 1)
 // row is in TMEM, so the maximum is exact and no rescale exists), P to shared memory, then O / l to
 // global.  While a warpgroup finishes pair i, the MMA warp already computes S for the other
 // warpgroup and, once S is released and the next Q has landed, for pair i + 1.
-template <int DP, int DVP, bool F16, bool SUMCOL>
-__global__ void __launch_bounds__(320, 1)
+template <int DP, int DVP, bool F16, bool SUMCOL, int SN>
+__global__ void __launch_bounds__(320, (2 * SN + 2 * DVP <= 256) ? 2 : 1)
     fa_short_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const FaParams p) {
   constexpr int Q_BYTES = kFaBM * DP * 2;
   constexpr int K_BYTES = kFaBN * DP * 2;
   constexpr int V_BYTES = kFaBN * DVP * 2;
   constexpr int V_TX = SUMCOL ? V_BYTES - kFaBN * 16 : V_BYTES;
-  constexpr int P_BYTES = kFaBM * kFaBN * 2;
+  constexpr int P_BYTES = kFaBM * SN * 2;
   constexpr uint32_t kLbo = kFaBM * 16;
   constexpr uint32_t kSbo = 128;
   constexpr int FMT = F16 ? 0 : 1;
-  constexpr uint32_t idesc_s = make_idesc(FMT, kFaBM, kFaBN);
+  // SN score columns (keys rounded up to 16: 80 for the 77 context tokens, else 128): with
+  // 2 SN + 2 DVP <= 256 TMEM columns (SN 80, head dims up to 48) two CTAs share an SM
+  static_assert(SN % 16 == 0 && SN <= kFaBN, "score width");
+  constexpr int TCOLS = (2 * SN + 2 * DVP <= 256) ? 256 : 512;
+  constexpr uint32_t idesc_s = make_idesc(FMT, kFaBM, SN);
   constexpr uint32_t idesc_o = make_idesc(FMT, kFaBM, DVP) | (1u << 16);
-  static_assert(2 * 128 + 2 * DVP <= 512, "TMEM budget");
+  static_assert(2 * SN + 2 * DVP <= 512, "TMEM budget");
 
   extern __shared__ uint8_t fa_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -870,14 +874,14 @@ __global__ void __launch_bounds__(320, 1)
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, TCOLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_o0 = tmem + 256;
+  const uint32_t t_o0 = tmem + 2 * SN;  // S slots at [0, SN) and [SN, 2 SN), then O of each tile
 
   if (warp == 0) {
     if (lane == 0 && npairs > 0) {
@@ -908,7 +912,7 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t qa = q_addr + x * Q_BYTES;
 #pragma unroll
           for (int kk = 0; kk < DP / 16; ++kk)
-            umma_f16(tmem + x * 128, sdesc_none(qa + kk * 2 * kLbo, kLbo, kSbo),
+            umma_f16(tmem + x * SN, sdesc_none(qa + kk * 2 * kLbo, kLbo, kSbo),
                      sdesc_none(k_addr + kk * 2 * kLbo, kLbo, kSbo), idesc_s, kk > 0 ? 1u : 0u);
           umma_commit(&s_full[x]);
           umma_commit(&q_empty[x]);
@@ -921,7 +925,7 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_after();
           const uint32_t pa = p_addr + x * P_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < kFaBN / 16; ++kk)
+          for (int kk = 0; kk < SN / 16; ++kk)
             umma_f16(t_o0 + x * DVP, sdesc_none(pa + kk * 2 * kLbo, kLbo, kSbo),
                      sdesc_none(v_addr + kk * 256, 128, kFaBN * 16), idesc_o, kk > 0 ? 1u : 0u);
           umma_commit(&o_full[x]);
@@ -934,7 +938,7 @@ __global__ void __launch_bounds__(320, 1)
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t t_o = t_o0 + x * DVP + lane_off;
-    const uint32_t ts = tmem + x * 128 + lane_off;
+    const uint32_t ts = tmem + x * SN + lane_off;
     const float sl = p.scale_log2;
     const uint64_t sl2 = f2_bits(sl, sl);
     const int kvalid = p.Sk;  // <= kFaBN
@@ -944,34 +948,51 @@ __global__ void __launch_bounds__(320, 1)
       if (!mbar_wait(&s_full[x], i & 1, 46, abort_flag)) break;
       tc_fence_after();
       float mx = -INFINITY;
+      if (SN == kFaBN) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
-        uint32_t r[64];
-        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-        tmem_ld_wait();
-        if (full) {
-          mx = fmaxf(mx, max64(r));
-        } else {
+        for (int c0 = 0; c0 < kFaBN; c0 += 64) {
+          uint32_t r[64];
+          tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          tmem_ld_wait();
+          if (full) {
+            mx = fmaxf(mx, max64(r));
+          } else {
 #pragma unroll
-          for (int k = 0; k < 64; ++k)
-            if (c0 + k < kvalid) mx = fmaxf(mx, __uint_as_float(r[k]));
+            for (int k = 0; k < 64; ++k)
+              if (c0 + k < kvalid) mx = fmaxf(mx, __uint_as_float(r[k]));
+          }
         }
+      } else {
+        // the whole SN-column row in one round of loads (16-column pieces)
+        uint32_t r[SN];
+#pragma unroll
+        for (int c0 = 0; c0 < SN; c0 += 16) tmem_ld16_raw(ts + c0, *reinterpret_cast<uint32_t(*)[16]>(&r[c0]));
+        tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < SN; ++k)
+          if (k < kvalid) mx = fmaxf(mx, __uint_as_float(r[k]));
       }
       const uint64_t negm2 = f2_bits(-mx * sl, -mx * sl);
       uint64_t sum2 = f2_bits(0.f, 0.f);
+      constexpr int CW = SN == kFaBN ? 64 : SN;  // columns per round of TMEM loads
 #pragma unroll 1
-      for (int c0 = 0; c0 < kFaBN; c0 += 64) {
-        uint32_t r[64];
-        tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-        tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      for (int c0 = 0; c0 < SN; c0 += CW) {
+        uint32_t r[CW];
+        if (CW == 64) {
+          tmem_ld32(ts + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld32(ts + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32 % CW]));
+        } else {
+#pragma unroll
+          for (int cc = 0; cc < CW; cc += 16) tmem_ld16_raw(ts + c0 + cc, *reinterpret_cast<uint32_t(*)[16]>(&r[cc]));
+        }
         tmem_ld_wait();
-        if (c0 == kFaBN - 64) {  // the last read of S: the next QK^T may overwrite it
+        if (c0 == SN - CW) {  // the last read of S: the next QK^T may overwrite it
           tc_fence_before();
           mbar_arrive(&s_empty[x]);
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < CW / 16; ++q) {
           uint32_t pk[8];
           const int c = c0 + q * 16;
           if (c >= kvalid) {  // 16 keys past the end: P is zero, no exponentials (uniform branch)
@@ -1046,7 +1067,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, TCOLS);
   }
 }
 
@@ -1159,11 +1180,25 @@ static int fa_lazy_launch(const mt_sdpa_desc& d, cudaStream_t st, bool* launched
 
 // Launch of the short-KV kernel (Sk <= 128): CTAs of `pairs` 256-query pairs of one (b, h), about
 // four CTAs per SM in total so that the last wave is short.
+template <int DP, int DVP, bool F16, bool SUMCOL, int SN>
+static int fa_short_launch_sn(const mt_sdpa_desc& d, cudaStream_t st);
+
 template <int DP, int DVP, bool F16, bool SUMCOL>
 static int fa_short_launch(const mt_sdpa_desc& d, cudaStream_t st) {
-  constexpr int SMEM = 2 * kFaBM * DP * 2 + 2 * kFaBM * kFaBN * 2 + kFaBN * (DP + DVP) * 2 + 1024 + 1024;
+  // 80 score columns (two CTAs per SM where TMEM allows) for up to 80 keys, else 128
+  if constexpr (2 * 80 + 2 * DVP <= 256) {
+    static const bool wide = getenv("MT_FA_SHORT_WIDE") != nullptr;
+    if (d.Sk <= 80 && !wide) return fa_short_launch_sn<DP, DVP, F16, SUMCOL, 80>(d, st);
+  }
+  return fa_short_launch_sn<DP, DVP, F16, SUMCOL, kFaBN>(d, st);
+}
+
+template <int DP, int DVP, bool F16, bool SUMCOL, int SN>
+static int fa_short_launch_sn(const mt_sdpa_desc& d, cudaStream_t st) {
+  constexpr int SMEM = 2 * kFaBM * DP * 2 + 2 * kFaBM * SN * 2 + kFaBN * (DP + DVP) * 2 + 1024 + 1024;
   static_assert(SMEM <= 227 * 1024, "shared memory");
-  auto kern = fa_short_sm100_kernel<DP, DVP, F16, SUMCOL>;
+  constexpr int OCC = (2 * SN + 2 * DVP <= 256) ? 2 : 1;  // CTAs per SM
+  auto kern = fa_short_sm100_kernel<DP, DVP, F16, SUMCOL, SN>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1187,7 +1222,8 @@ static int fa_short_launch(const mt_sdpa_desc& d, cudaStream_t st) {
   p.out_dtype = d.dtype;
   const int64_t pairs_bh = (d.Sq + 2 * kFaBM - 1) / (2 * kFaBM);
   const int64_t bh = d.B * d.H;
-  const int64_t cpb = std::min<int64_t>(pairs_bh, std::max<int64_t>(1, (4 * (int64_t)num_sms() + bh - 1) / bh));
+  const int64_t cpb =
+      std::min<int64_t>(pairs_bh, std::max<int64_t>(1, (4 * OCC * (int64_t)num_sms() + bh - 1) / bh));
   p.pairs = (int)((pairs_bh + cpb - 1) / cpb);
   dim3 grid((unsigned)((pairs_bh + p.pairs - 1) / p.pairs), (unsigned)bh);
   kern<<<grid, 320, SMEM, st>>>(mq, mk, mv, p);

@@ -619,11 +619,13 @@ def test_sdpa_bf16_masked_tensor_core(kind, D, causal, bcast):
 @pytest.mark.parametrize("B,H,Sq,Sk,D,dtype", [(2, 8, 4096, 77, 40, "bfloat16"), (2, 8, 1024, 77, 80, "bfloat16"),
                                                (1, 3, 300, 128, 64, "bfloat16"), (3, 2, 100, 1, 40, "bfloat16"),
                                                (1, 4, 1000, 50, 128, "float16"), (2, 2, 700, 77, 16, "bfloat16"),
-                                               (1, 2, 257, 120, 48, "float16")])
+                                               (1, 2, 257, 120, 48, "float16"), (1, 2, 513, 80, 48, "float16"),
+                                               (2, 3, 300, 64, 24, "bfloat16")])
 def test_sdpa_short_keys(B, H, Sq, Sk, D, dtype):
     """At most 128 keys (cross-attention to the 77-token context): the persistent short-key
     kernel, K and V loaded once per CTA for several query-tile pairs; ragged query counts, one key,
-    the ones-column row sum (head dim <= padded - 8) and the softmax-side row sum."""
+    the ones-column row sum (head dim <= padded - 8) and the softmax-side row sum.  Up to 80 keys
+    at padded head dims <= 48 use 80-column score tiles (two CTAs per SM)."""
     q, k, v = rnd(B, H, Sq, D, scale=1.5), rnd(B, H, Sk, D, seed=1), rnd(B, H, Sk, D, seed=2)
     qd, kd, vd = cu(q, dtype), cu(k, dtype), cu(v, dtype)
     assert mt.ops.sdpa_path(qd, kd, vd) == "tc_short"
