@@ -28,7 +28,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REF = Path(os.environ.get("MTORCH_REFERENCE", "/root/reference"))
+# The reference checkout: MTORCH_REFERENCE, else a "reference" folder beside this repository.
+REF = Path(os.environ.get("MTORCH_REFERENCE", str(HERE.parent.parent / "reference")))
 
 
 def _extract_function(source: str, signature: str) -> str:
