@@ -197,10 +197,11 @@ def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        dist = parallel.init("nccl", device_id=torch.device(f"cuda:{local}"))
+    mt.cuda.set_device(local)
+    dist = comm = None
+    if world > 1:  # host plumbing over gloo; the device all-gather is NCCL through the C ABI
+        dist = parallel.init("gloo")
+        comm = parallel.NcclCommunicator(rank, world, dist.distributed_c10d._get_default_store())
     gb = args.global_batch
     lo, hi = parallel.shard(gb, world, rank)
     nb = hi - lo
@@ -221,7 +222,7 @@ def run_ours(args):
                 for t in sched.timesteps]
     x = lat_h.to(dev)
     ctx = ctx_h.to(dev)
-    stream = torch.cuda.current_stream()
+    stream = mt.cuda.current_stream()
 
     # The UNet forward is captured once as a CUDA graph (static latent / time-embedding / context
     # buffers); each step copies its inputs in, replays it and applies the fused DDIM update.
@@ -236,7 +237,7 @@ def run_ours(args):
 
     for i in range(args.warmup):
         x = step(i, x)
-    torch.cuda.synchronize()
+    mt.cuda.synchronize()
 
     # ---- device-timed region ----
     lib = _lib.lib()
@@ -244,18 +245,18 @@ def run_ours(args):
     with clocks:
         if dist:
             dist.barrier()
-        torch.cuda.synchronize()
+        mt.cuda.synchronize()
         n0 = lib.mt_cuda_launch_count()
         r0 = graphed.replays if use_graph else 0
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = mt.cuda.Event(), mt.cuda.Event()
         e0.record(stream)
         for i in range(args.steps):
             x = step(args.warmup + i, x)
         gathered = None
-        if dist:  # output latents, all ranks
-            gathered = parallel.gather_shards(x.contiguous()._buf[:x.numel() * 2])
+        if comm:  # output latents, all ranks
+            gathered = comm.all_gather(x)
         e1.record(stream)
-        torch.cuda.synchronize()
+        mt.cuda.synchronize()
         if dist:
             dist.barrier()
         # kernels launched directly + this library's kernels replayed inside the CUDA graph
@@ -264,24 +265,24 @@ def run_ours(args):
             launches += (graphed.replays - r0) * graphed.kernels_per_replay
     ms = e0.elapsed_time(e1)
     if dist:
-        tt = torch.tensor([ms], device=dev)
+        tt = torch.tensor([ms])
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
     ms_per_step = ms / args.steps
     value = 1000.0 / ms_per_step
 
     # ---- end to end through the public API with host buffers (pinned), every step ----
-    lat_pin = torch.from_numpy(lat_h._buf[:lat_h.numel()].copy()).pin_memory()
-    ctx_pin = torch.from_numpy(ctx_h._buf[:ctx_h.numel()].copy()).pin_memory()
-    out_pin = torch.empty(lat_h.numel(), dtype=torch.int16).pin_memory()
+    lat_pin = lat_h.pin_memory()
+    ctx_pin = ctx_h.pin_memory()
+    out_pin = mt.empty(nb, 4, H, W, dtype="bfloat16").pin_memory()
     xd = mt.empty(nb, 4, H, W, dtype="bfloat16", device=dev)
     cd = mt.empty(nb, CTX, 768, dtype="bfloat16", device=dev)
     h2d = (lat_pin.numel() + ctx_pin.numel()) * 2
     d2h = out_pin.numel() * 2
     if dist:
         dist.barrier()
-    torch.cuda.synchronize()
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mt.cuda.synchronize()
+    e2, e3 = mt.cuda.Event(), mt.cuda.Event()
     e2.record(stream)
     if use_graph:  # copy straight into the graph's static input buffers
         xd, cd = graphed.static_in[0], graphed.static_in[2]
@@ -295,10 +296,10 @@ def run_ours(args):
         lib.mt_cuda_memcpy(out_pin.data_ptr(), y.data_ptr(), d2h, 1, stream.cuda_stream)
         stream.synchronize()
     e3.record(stream)
-    torch.cuda.synchronize()
+    mt.cuda.synchronize()
     ms_e2e = e2.elapsed_time(e3)
     if dist:
-        tt = torch.tensor([ms_e2e], device=dev)
+        tt = torch.tensor([ms_e2e])
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms_e2e = float(tt.item())
     e2e = {"value": 1000.0 * args.steps / ms_e2e, "unit": "steps/s", "h2d_bytes_per_step": h2d * world,
@@ -310,13 +311,13 @@ def run_ours(args):
     def timed(fn, reps=10):
         for _ in range(3):
             fn()
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-        torch.cuda.synchronize()
+        ev = [mt.cuda.Event() for _ in range(2)]
+        mt.cuda.synchronize()
         ev[0].record(stream)
         for _ in range(reps):
             fn()
         ev[1].record(stream)
-        torch.cuda.synchronize()
+        mt.cuda.synchronize()
         return ev[0].elapsed_time(ev[1]) / reps
 
     # self-attention of the 64x64 level: 8 heads x 4096 tokens x head dim 40 (Q, K, V, O 168 MB
@@ -375,9 +376,9 @@ def run_ours(args):
                 te = temb64[i % len(temb64)]
                 eps = g64(x64, te, ctx64) if use_graph else unet(x64, te, ctx64)
                 x64 = sched.step(x64, eps, sched.timesteps[i % len(sched.timesteps)])
-            torch.cuda.synchronize()
-            ref = x64.contiguous()._buf[:x64.numel() * 2]
-            bitwise = bool(torch.equal(ref, gathered))
+            mt.cuda.synchronize()
+            ref = x64.contiguous().to("cpu")._buf[:x64.numel()]
+            bitwise = bool(np.array_equal(ref, gathered.to("cpu")._buf[:gathered.numel()]))
         dist.barrier()
 
     clk = clock_summary([out_dir / f"clocks_rank{r}.csv" for r in range(world)]) if rank == 0 else None
@@ -411,20 +412,21 @@ def run_ours(args):
                 "cpu_baseline": base, "bitwise_equal_to_1gpu": bitwise,
                 "clocks": clk}
         print(json.dumps(line))
+    if comm:
+        comm.close()
     if dist:
         dist.destroy_process_group()
 
 
 def run_kernel(args):
     """One hot kernel alone at its level-0 UNet shape: `steps` timed launches after `warmup`,
-    CUDA events on torch's current stream.  Used for ncu captures of a single kernel."""
-    import torch
+    CUDA events on the library stream.  Used for ncu captures of a single kernel."""
 
     import mtorch_b200 as mt
     from mtorch_b200 import _lib, ops
 
     nb = args.batch
-    stream = torch.cuda.current_stream()
+    stream = mt.cuda.current_stream()
     mt.manual_seed(0)
     if args.kernel == "conv":
         conv = mt.nn.Conv2d(320, 320, 3, padding=1, device="cuda", dtype="bfloat16")
@@ -460,13 +462,13 @@ def run_kernel(args):
         name = "flash attention, 8 heads x 4096 tokens x 40"
     for _ in range(args.warmup):
         fn()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mt.cuda.synchronize()
+    e0, e1 = mt.cuda.Event(), mt.cuda.Event()
     e0.record(stream)
     for _ in range(args.steps):
         fn()
     e1.record(stream)
-    torch.cuda.synchronize()
+    mt.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     hbm, tf_burst, _, kind = peaks()
     if flops is None:
@@ -480,7 +482,7 @@ def run_kernel(args):
 
 
 def run_workload(args):
-    """The §8(f) workloads around the UNet, one GPU, device-timed (CUDA events on torch's current
+    """The §8(f) workloads around the UNet, one GPU, device-timed (CUDA events on the library's
     stream, after `warmup` untimed runs), each as one JSON line with its FLOP rate against the
     measured bf16 peak:
       sampler  guided denoising (classifier-free guidance 7.5) of `batch` latents: the UNet on the
@@ -492,11 +494,10 @@ def run_workload(args):
                graph); unit = steps/s, beside the reference CPU path on the same per-sample work
       c1-c3    BASELINE configs C1 (fp32 matmul 2048^2), C2 (fp32 ResNet block), C3 (bf16 attention
                block), beside the reference CPU path computing each in full (see run_config)"""
-    import torch
 
     import mtorch_b200 as mt
 
-    stream = torch.cuda.current_stream()
+    stream = mt.cuda.current_stream()
     nb = args.batch
     mt.manual_seed(0)
     base = None
@@ -554,13 +555,13 @@ def run_workload(args):
         name = f"SD-1.5 CLIP text encoder, {nb} x 77 tokens"
     for _ in range(max(args.warmup, 1)):
         fn()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mt.cuda.synchronize()
+    e0, e1 = mt.cuda.Event(), mt.cuda.Event()
     e0.record(stream)
     for _ in range(args.steps):
         fn()
     e1.record(stream)
-    torch.cuda.synchronize()
+    mt.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     _, tf_burst, tf_sust, kind = peaks()
     tflops = flops / (ms * 1e-3) / 1e12
@@ -580,13 +581,12 @@ def run_config(args):
     """BASELINE configs C1-C3 on one GPU (CUDA events, `steps` runs after `warmup`), beside the
     reference's own CPU path computing the same configuration in full on all host cores (each op
     cut into row slices spread over single-threaded processes; oracle/cpu_bench.FullRun)."""
-    import torch
 
     import mtorch_b200 as mt
     from mtorch_b200 import ops
     from mtorch_b200.unet import BasicTransformerBlock
 
-    stream = torch.cuda.current_stream()
+    stream = mt.cuda.current_stream()
     mt.manual_seed(0)
     if args.workload == "c1":
         a = mt.randn(2048, 2048).cuda()
@@ -611,13 +611,13 @@ def run_config(args):
         name, dtype = "C3: SD attention block bf16 (self 4096 + cross 77 + GEGLU FFN), [2, 4096, 320]", "bf16"
     for _ in range(max(args.warmup, 3)):
         fn()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mt.cuda.synchronize()
+    e0, e1 = mt.cuda.Event(), mt.cuda.Event()
     e0.record(stream)
     for _ in range(args.steps):
         fn()
     e1.record(stream)
-    torch.cuda.synchronize()
+    mt.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     _, tf_burst, _, kind = peaks()
     tflops = flops / (ms * 1e-3) / 1e12

@@ -65,6 +65,54 @@ uint64_t mt_cuda_launch_count(void);
 /* kind: 0 = host->device, 1 = device->host, 2 = device->device. */
 int mt_cuda_memcpy(void* dst, const void* src, size_t bytes, int kind, void* stream);
 int mt_cuda_memset(void* dst, int value, size_t bytes, void* stream);
+
+/* ---- device runtime: storage, streams, events, graphs, NCCL ------------------------------ */
+/* The reference keeps tensor bytes in a host `Storage` (cpp/mtorch/core/tensor.h:60-63, a
+ * shared `std::vector<uint8_t>`) allocated by `Storage(size_t)`; the device counterpart is this
+ * caching allocator.  mt_cuda_malloc serves a block on the CURRENT device (mt_cuda_set_device)
+ * from the device's free list or cudaMalloc; mt_cuda_free returns it to the free list.  Blocks
+ * are reused in stream order: issue all of a device's work on one stream (mt_cuda_library_stream)
+ * or synchronise before freeing a block another stream still reads.  While a graph capture is
+ * open on a device (mt_cuda_graph_begin), allocations come from a pool private to that graph
+ * that lives until mt_cuda_graph_destroy.  On out-of-memory the cached blocks are released and
+ * the allocation retried once. */
+int mt_cuda_malloc(void** ptr, size_t bytes);
+int mt_cuda_free(void* ptr);
+/* Bytes handed out and bytes held in free lists on `device`. */
+int mt_cuda_memory_stats(int device, size_t* in_use, size_t* cached);
+/* Releases the current device's cached free blocks (synchronises the device). */
+int mt_cuda_empty_cache(void);
+/* Page-locked host memory for asynchronous host<->device copies. */
+int mt_cuda_host_alloc(void** ptr, size_t bytes);
+int mt_cuda_host_free(void* ptr);
+/* Streams: mt_cuda_library_stream returns the device's own non-blocking stream (created on
+ * first request, lives until exit) on which the host layer issues all of that device's work. */
+int mt_cuda_stream_create(void** stream);
+int mt_cuda_stream_destroy(void* stream);
+int mt_cuda_library_stream(int device, void** stream);
+/* Timing events (cudaEvent_t as void*). */
+int mt_cuda_event_create(void** event);
+int mt_cuda_event_destroy(void* event);
+int mt_cuda_event_record(void* event, void* stream);
+int mt_cuda_event_synchronize(void* event);
+int mt_cuda_event_elapsed_ms(void* start, void* end, float* ms);
+/* CUDA-graph capture of the work issued on `stream` (thread-local capture mode) between begin
+ * and end; end instantiates it and returns an opaque graph handle for launch / destroy.  The
+ * graph's private allocation pool is released by destroy (blocks still held by the caller are
+ * released when they are freed). */
+int mt_cuda_graph_begin(void* stream);
+int mt_cuda_graph_end(void* stream, void** graph);
+int mt_cuda_graph_launch(void* graph, void* stream);
+int mt_cuda_graph_destroy(void* graph);
+/* NCCL over NVLink for the batch-sharded job (no counterpart in the single-process reference):
+ * libnccl.so.2 is loaded on first use.  The unique id (128 bytes) is made on one rank and
+ * handed to the others by the host layer; all_gather concatenates `bytes_per_rank` bytes from
+ * every rank in rank order into `recv`. */
+int mt_nccl_available(void);
+int mt_nccl_unique_id(void* id, size_t bytes);
+int mt_nccl_comm_init(void** comm, const void* id, size_t bytes, int world, int rank);
+int mt_nccl_all_gather(const void* send, void* recv, size_t bytes_per_rank, void* comm, void* stream);
+int mt_nccl_comm_destroy(void* comm);
 /* Strided copy with dtype conversion (f32/bf16/f16/f64 <-> each other):
  * dst[i0..] = cast(src[i0..]) over `ndim` dims of `sizes`, each side with its own strides. */
 int mt_cuda_copy_strided(void* dst, int dst_dtype, const int64_t* dst_strides, const void* src, int src_dtype,

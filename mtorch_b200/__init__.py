@@ -12,6 +12,7 @@ from __future__ import annotations
 import contextlib
 
 from . import _lib
+from . import runtime as _runtime
 from .tensor import (Size, Tensor, add, bfloat16, bool_, device, div, dtype, empty, empty_like, float16, float32,
                      float64, from_numpy, full, int32, int64, mul, ones, sub, tensor, zeros, zeros_like)
 
@@ -62,8 +63,7 @@ class _Cuda:
 
     @staticmethod
     def synchronize(device=None):
-        _lib.check(_lib.lib().mt_cuda_synchronize(None), "synchronize")
-        _lib.check(_lib.lib().mt_cuda_device_status(1), "device status")
+        _runtime.synchronize(device)
 
     @staticmethod
     def is_bf16_supported() -> bool:
@@ -73,11 +73,13 @@ class _Cuda:
     def manual_seed(seed):
         return None
 
-    @staticmethod
-    def current_device() -> int:
-        from .tensor import _t
-
-        return _t().cuda.current_device()
+    current_device = staticmethod(_runtime.current_device)
+    set_device = staticmethod(_runtime.set_device)
+    current_stream = staticmethod(_runtime.current_stream)
+    Stream = _runtime.Stream
+    Event = _runtime.Event
+    memory_stats = staticmethod(_runtime.memory_stats)
+    empty_cache = staticmethod(_runtime.empty_cache)
 
 
 cuda = _Cuda()

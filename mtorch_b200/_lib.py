@@ -85,6 +85,29 @@ SIGNATURES = {
     "mt_cuda_launch_count": (C.c_uint64, []),
     "mt_cuda_memcpy":(C.c_int, [VP, VP, C.c_size_t, C.c_int, VP]),
     "mt_cuda_memset": (C.c_int, [VP, C.c_int, C.c_size_t, VP]),
+    "mt_cuda_malloc": (C.c_int, [C.POINTER(VP), C.c_size_t]),
+    "mt_cuda_free": (C.c_int, [VP]),
+    "mt_cuda_memory_stats": (C.c_int, [C.c_int, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+    "mt_cuda_empty_cache": (C.c_int, []),
+    "mt_cuda_host_alloc": (C.c_int, [C.POINTER(VP), C.c_size_t]),
+    "mt_cuda_host_free": (C.c_int, [VP]),
+    "mt_cuda_stream_create": (C.c_int, [C.POINTER(VP)]),
+    "mt_cuda_stream_destroy": (C.c_int, [VP]),
+    "mt_cuda_library_stream": (C.c_int, [C.c_int, C.POINTER(VP)]),
+    "mt_cuda_event_create": (C.c_int, [C.POINTER(VP)]),
+    "mt_cuda_event_destroy": (C.c_int, [VP]),
+    "mt_cuda_event_record": (C.c_int, [VP, VP]),
+    "mt_cuda_event_synchronize": (C.c_int, [VP]),
+    "mt_cuda_event_elapsed_ms": (C.c_int, [VP, VP, C.POINTER(C.c_float)]),
+    "mt_cuda_graph_begin": (C.c_int, [VP]),
+    "mt_cuda_graph_end": (C.c_int, [VP, C.POINTER(VP)]),
+    "mt_cuda_graph_launch": (C.c_int, [VP, VP]),
+    "mt_cuda_graph_destroy": (C.c_int, [VP]),
+    "mt_nccl_available": (C.c_int, []),
+    "mt_nccl_unique_id": (C.c_int, [VP, C.c_size_t]),
+    "mt_nccl_comm_init": (C.c_int, [C.POINTER(VP), VP, C.c_size_t, C.c_int, C.c_int]),
+    "mt_nccl_all_gather": (C.c_int, [VP, VP, C.c_size_t, VP, VP]),
+    "mt_nccl_comm_destroy": (C.c_int, [VP]),
     "mt_cuda_copy_strided": (C.c_int, [VP, C.c_int, _P64, VP, C.c_int, _P64, _P64, C.c_int, VP]),
     "mt_cuda_fill_uniform": (C.c_int, [VP, C.c_int, I64, C.c_uint64, C.c_double, C.c_double, VP]),
     "mt_cuda_fill": (C.c_int, [VP, C.c_int, I64, C.c_double, VP]),

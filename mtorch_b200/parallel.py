@@ -6,10 +6,21 @@ each rank denoises its slice of the batch with replicated weights and no collect
 path, and the output latents are all-gathered once at the end (NCCL over NVLink on the GPU
 box; gloo in the CPU tests).  Every kernel's tiling is independent of the batch size, so the
 gathered result equals a single-GPU run bit for bit.
+
+The device all-gather is NCCL called through the library's C ABI (`NcclCommunicator`:
+`mt_nccl_comm_init` / `mt_nccl_all_gather` on the library stream).  Only the host-side
+rendezvous — handing rank 0's NCCL unique id to the other ranks — needs a key-value store, and
+any object with blocking `set(key, bytes)` / `get(key) -> bytes` serves (torch.distributed's
+TCPStore in bench.py).  `init` / `gather_shards` are the host (gloo) process-group helpers the
+CPU tests use.
 """
 from __future__ import annotations
 
+import ctypes as C
 import datetime
+
+from . import _lib as L
+from . import runtime
 
 
 def shard(batch: int, world: int, rank: int) -> tuple[int, int]:
@@ -49,3 +60,44 @@ def gather_shards(local, group=None):
         parts = list(out.chunk(world))
         dist.all_gather(parts, local, group=group)
     return out
+
+
+class NcclCommunicator:
+    """An NCCL communicator over this process's current device, built from a rendezvous store."""
+
+    ID_BYTES = 128
+
+    def __init__(self, rank: int, world: int, store, key: str = "mtorch_b200/nccl_id"):
+        lib = L.lib()
+        if not lib.mt_nccl_available():
+            raise RuntimeError("NCCL (libnccl.so.2) could not be loaded")
+        self.rank, self.world = int(rank), int(world)
+        self.device = runtime.current_device()
+        if self.rank == 0:
+            uid = (C.c_uint8 * self.ID_BYTES)()
+            L.check(lib.mt_nccl_unique_id(uid, self.ID_BYTES), "nccl unique id")
+            store.set(key, bytes(uid))
+        raw = bytes(store.get(key))
+        if len(raw) != self.ID_BYTES:
+            raise RuntimeError(f"NCCL unique id from the store has {len(raw)} bytes, not {self.ID_BYTES}")
+        uid = (C.c_uint8 * self.ID_BYTES).from_buffer_copy(raw)
+        comm = C.c_void_p()
+        L.check(lib.mt_nccl_comm_init(C.byref(comm), uid, self.ID_BYTES, self.world, self.rank), "nccl init")
+        self.comm = comm.value
+
+    def all_gather(self, local):
+        """Concatenates every rank's contiguous device tensor `local` (same shape everywhere)
+        along dim 0 in rank order; returns a new device tensor on the library stream."""
+        from .tensor import empty
+
+        src = local.contiguous()
+        out = empty(src.shape[0] * self.world, *src.shape[1:], dtype=src.dtype, device=src.device)
+        nbytes = src.numel() * src.dtype.itemsize
+        L.check(L.lib().mt_nccl_all_gather(src.data_ptr(), out.data_ptr(), nbytes, self.comm,
+                                           runtime.stream_ptr(src._idx())), "nccl all_gather")
+        return out
+
+    def close(self):
+        if self.comm:
+            L.check(L.lib().mt_nccl_comm_destroy(self.comm), "nccl destroy")
+            self.comm = None

@@ -6,9 +6,9 @@ The reference keeps tensors as ``Storage`` (a byte vector) plus view metadata
 
 * ``cpu`` storage is a numpy array (host memory), used for creation, the seeded generator and
   transfers — compute on CPU tensors stays with mtorch itself and raises here;
-* ``cuda`` storage is a device byte buffer obtained from torch's caching allocator (allocation
-  and streams are the only things torch provides); every byte of compute on it is a kernel of
-  ``libmtorch_cuda.so`` called through the C ABI.
+* ``cuda`` storage is a device byte buffer from ``libmtorch_cuda.so``'s caching allocator
+  (``runtime.DeviceBuffer``), and every byte of compute on it is a kernel of the same library
+  called through the C ABI on the device's library stream.
 
 Views (reshape/permute/transpose/narrow/expand/...) are metadata only, exactly like the reference
 (``reshape`` tensor.cpp:8584, ``transpose`` 8653, ``permute`` 8680); ``contiguous`` and dtype
@@ -117,44 +117,18 @@ class device:
 _CPU = device("cpu")
 
 # ---------------------------------------------------------------------------------------------
-# device memory, streams and workspaces (torch is used only for these)
+# device memory, streams and workspaces: the library's own device runtime (runtime.py)
 
-_torch = None
-
-
-def _t():
-    global _torch
-    if _torch is None:
-        import torch
-
-        _torch = torch
-    return _torch
+from . import runtime as _rt  # noqa: E402
+from .runtime import DeviceBuffer, _ensure_device, stream_ptr  # noqa: E402
 
 
-_initialised = set()
-
-
-def _ensure_device(idx: int) -> None:
-    if idx not in _initialised:
-        torch = _t()
-        if not torch.cuda.is_available():
-            raise RuntimeError("CUDA device requested but no GPU is available")
-        torch.cuda.set_device(idx)
-        L.check(L.lib().mt_cuda_set_device(idx), "set_device")
-        _initialised.add(idx)
-
-
-def _alloc(nbytes: int, idx: int):
-    _ensure_device(idx)
-    torch = _t()
-    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=f"cuda:{idx}")
-
-
-def stream_ptr(idx: int):
-    return _t().cuda.current_stream(idx).cuda_stream
+def _alloc(nbytes: int, idx: int) -> DeviceBuffer:
+    return DeviceBuffer(nbytes, idx)
 
 
 _WS: dict = {}
+_WS_RETIRED: list = []
 
 
 def workspace(nbytes: int, idx: int):
@@ -163,6 +137,8 @@ def workspace(nbytes: int, idx: int):
         return None, 0
     buf = _WS.get(idx)
     if buf is None or buf.numel() < nbytes:
+        if buf is not None and idx in _rt.capturing:
+            _WS_RETIRED.append(buf)  # kernels captured earlier in this graph still use it
         buf = _alloc(int(nbytes * 1.25) + 4096, idx)
         _WS[idx] = buf
     return buf.data_ptr(), buf.numel()
@@ -451,6 +427,16 @@ class Tensor:
 
     def cpu(self):
         return self.to("cpu")
+
+    def pin_memory(self):
+        """A contiguous copy of this CPU tensor in page-locked host memory (asynchronous
+        host<->device copies from / into it overlap with the device)."""
+        if self.device.type != "cpu":
+            raise RuntimeError("cannot pin a cuda tensor: only CPU tensors live in host memory")
+        src = self.contiguous()
+        buf = _rt.pinned_array(src.numel(), src._buf.dtype)
+        buf[:src.numel()] = src._buf[src._offset:src._offset + src.numel()]
+        return Tensor(buf, 0, src._shape, _contig_strides(src._shape), src.dtype, src.device)
 
     def float(self):
         return self.to(float32)

@@ -20,9 +20,9 @@ def golden():
 
 def _gpu_available():
     try:
-        import torch
+        from mtorch_b200 import _lib
 
-        return torch.cuda.is_available()
+        return _lib.lib().mt_cuda_device_count() > 0
     except Exception:
         return False
 

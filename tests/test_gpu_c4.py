@@ -35,8 +35,6 @@ def npw(t):
 
 @pytest.fixture(scope="module")
 def c4_run():
-    import torch
-
     mt.manual_seed(0)
     net = U.UNet(device="cuda", dtype="float32")
     mt.manual_seed(1)
@@ -77,11 +75,11 @@ def c4_run():
         ops.scaled_dot_product_attention = orig_sdpa
         up_res.forward, up_samp.forward = fr, fu
     # device time of the whole fp32 step (printed; the bench's `--workload c4` reports it)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev = [mt.cuda.Event() for _ in range(2)]
     ev[0].record()
     U.DDIM(steps=50).step(lat, net(lat, temb, ctx), 999)
     ev[1].record()
-    torch.cuda.synchronize()
+    mt.cuda.synchronize()
     print(f"C4 fp32 UNet step: {ev[0].elapsed_time(ev[1]):.1f} ms")
     return net, rec, out
 
