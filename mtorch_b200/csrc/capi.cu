@@ -136,7 +136,7 @@ int mt_cuda_synchronize(void* stream) {
 }
 
 int mt_cuda_device_status(int clear) {
-  const int vals[2] = {read_status_gemm(clear), read_status_attention(clear)};
+  const int vals[3] = {read_status_gemm(clear), read_status_attention(clear), read_status_norm(clear)};
   for (int v : vals) {
     if (v < 0) return fail(MT_ERR_LAUNCH, "could not read the device status word");
     if (v) return fail(v & 0xff, "a device-side wait expired (site %d)", v >> 8);

@@ -397,9 +397,9 @@ __global__ void __launch_bounds__(kGnThreads, 5) gn_partial_cl_bf16x8_kernel(con
         for (int j = 0; j < 4; ++j) {
           const float2 f = __bfloat1622float2(h[j]);
           s[2 * j] += f.x;
-          q[2 * j] += f.x * f.x;
+          q[2 * j] = __fmaf_rn(f.x, f.x, q[2 * j]);
           s[2 * j + 1] += f.y;
-          q[2 * j + 1] += f.y * f.y;
+          q[2 * j + 1] = __fmaf_rn(f.y, f.y, q[2 * j + 1]);
         }
       }
     }
@@ -451,6 +451,38 @@ __global__ void gn_table_kernel(const float* stats, const void* w, const void* b
   tab[i] = make_float2(a, sh);
 }
 
+// SiLU for results rounded to bf16: x * sigmoid(x) = h + h * tanh(h) with h = x / 2, one MUFU
+// operation (tanh.approx, relative error ~2^-11, below bf16's 2^-8 rounding) instead of two.
+__device__ __forceinline__ float silu_bf16out(float x) {
+  const float h = 0.5f * x;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return __fmaf_rn(h, t, h);
+}
+
+// (a, b) of channel c for y = x * a + b: a = rstd * gamma, b = beta - mean * rstd * gamma, each
+// product and sum rounded on its own (no contraction), so every kernel gets the same bits.
+__device__ __forceinline__ float2 gn_affine(float rstd, float mf, const void* w, const void* b, int wbd, int64_t c) {
+  float a = rstd, sh = __fmul_rn(-mf, rstd);
+  if (w) {
+    const float gm = load_as_f32(w, c, wbd);
+    a = __fmul_rn(a, gm);
+    sh = __fmul_rn(sh, gm);
+  }
+  if (b) sh = __fadd_rn(sh, load_as_f32(b, c, wbd));
+  return make_float2(a, sh);
+}
+
+__device__ __forceinline__ float2 gn_affine_v(float rstd, float mf, bool has_w, float gm, bool has_b, float be) {
+  float a = rstd, sh = __fmul_rn(-mf, rstd);
+  if (has_w) {
+    a = __fmul_rn(a, gm);
+    sh = __fmul_rn(sh, gm);
+  }
+  if (has_b) sh = __fadd_rn(sh, be);
+  return make_float2(a, sh);
+}
+
 // Finalize + affine table in one pass: one warp per (image, group).  Lane l sums chunks l, l+32,
 // ... in double, then a fixed xor-shuffle tree combines the lanes, so the result depends only on
 // the per-image chunking (not on N) and is the same on every run.  The warp then writes the
@@ -478,14 +510,7 @@ __global__ void gn_finalize_table_kernel(const double* part, const void* w, cons
   const float rstd = (float)(1.0 / sqrt(var + eps)), mf = (float)mean;
   const int64_t Cg = C / G;
   for (int64_t c = g * Cg + lane; c < (g + 1) * Cg; c += 32) {
-    float a = rstd, sh = -mf * rstd;
-    if (w) {
-      const float gm = load_as_f32(w, c, wbd);
-      a *= gm;
-      sh *= gm;
-    }
-    if (b) sh += load_as_f32(b, c, wbd);
-    tab[n * C + c] = make_float2(a, sh);
+    tab[n * C + c] = gn_affine(rstd, mf, w, b, wbd, c);
   }
 }
 
@@ -532,10 +557,10 @@ __global__ void __launch_bounds__(256) gn_apply_img_bf16x8_kernel(__nv_bfloat16*
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float2 f = __bfloat1622float2(h[j]);
-      float r0 = f.x * ab[j].x + ab[j].y, r1 = f.y * ab[j].z + ab[j].w;
+      float r0 = __fmaf_rn(f.x, ab[j].x, ab[j].y), r1 = __fmaf_rn(f.y, ab[j].z, ab[j].w);
       if (silu) {
-        r0 = silu_f(r0);
-        r1 = silu_f(r1);
+        r0 = silu_bf16out(r0);
+        r1 = silu_bf16out(r1);
       }
       h[j] = __floats2bfloat162_rn(r0, r1);
     }
@@ -558,8 +583,8 @@ __global__ void gn_apply_cl_bf16x8_tab_kernel(__nv_bfloat16* y, const __nv_bfloa
       float2 f = __bfloat1622float2(h[j]);
       float r0 = f.x * ab.x + ab.y, r1 = f.y * ab.z + ab.w;
       if (silu) {
-        r0 = silu_f(r0);
-        r1 = silu_f(r1);
+        r0 = silu_bf16out(r0);
+        r1 = silu_bf16out(r1);
       }
       h[j] = __floats2bfloat162_rn(r0, r1);
     }
@@ -713,6 +738,360 @@ size_t group_norm_workspace(int64_t N, int64_t C, int64_t HW, int64_t G) {
   return gn_part_bytes(N, G) + gn_stats_bytes(N, G) + (size_t)N * C * sizeof(float2);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Single-read GroupNorm (channels-last bf16, dense): one cooperative persistent launch.  A work
+// item is (image n, chunk k) of gn_chunk_px(C) pixels, at most kGnFusedBytes of activations: the
+// CTA copies the chunk into shared memory with one bulk copy per source (cp.async.bulk, the
+// pixels of a chunk are contiguous in a dense channels-last image), forms its per-group partial
+// sums, publishes them and counts itself in the image's arrival counter, waits (bounded) until all
+// chunks of the image have arrived, combines the image's partials in a fixed order into the
+// (a, b) affine of its channels, normalises the chunk in shared memory and writes it back with a
+// bulk copy.  HBM sees one read and one write of the activation.
+//
+// Items are dealt round-robin (item = blockIdx.x + i * gridDim.x), the chunks of an image are
+// consecutive items, and the grid holds at least `chunks` CTAs, all resident (cooperative launch):
+// no CTA ever holds two chunks of one image, and the CTAs holding the chunks of the lowest image
+// still waited on are all past their earlier items, so every wait completes.
+//
+// The arithmetic is exactly that of the three-launch path (gn_partial_cl_bf16x8_kernel,
+// gn_finalize_table_kernel, gn_apply_img_bf16x8_kernel): the same chunk boundaries, slots of
+// 256 / (C / 8) pixel lanes summed in float in pixel order, double group sums, one warp per group
+// combining the chunks with the same xor tree, the same affine and FMA apply.  So the choice
+// between the two paths — this one while every chunk of the batch fits on the GPU at once, which
+// depends on the batch size — never changes a bit of the result.
+constexpr int kGnFusedBytes = 80 * 1024;
+constexpr int kGnFusedThreads = 256;
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+struct GnFusedParams {
+  const __nv_bfloat16* x;   // first source: C1 channels per pixel, image stride sn (elements)
+  const __nv_bfloat16* x2;  // second source (C - C1 channels, image stride sn2) or null
+  __nv_bfloat16* y;         // dense [N, HW, C]
+  int64_t sn, sn2;
+  int C, C1, HW, G, px, chunks, items;
+  const void* w;
+  const void* b;
+  int wbd;
+  double eps;
+  int silu;
+  double* part;       // [N][chunks][G][2]
+  unsigned* arrived;  // [N], zero at launch
+};
+
+__global__ void __launch_bounds__(kGnFusedThreads) gn_fused_cl_bf16x8_kernel(const GnFusedParams p) {
+  extern __shared__ __align__(128) uint8_t gnf_raw[];
+  uint8_t* data = gnf_raw;  // chunk: [px][C1] then [px][C2], bf16
+  const int C = p.C, C1 = p.C1, C2 = C - C1, V = C / 8, G = p.G, Cg = C / G;
+  const int lanes = V >= kGnThreads ? 1 : kGnThreads / V;  // the slot layout of the partial kernel
+  float* red = reinterpret_cast<float*>(gnf_raw + kGnFusedBytes);  // [2][lanes * C]
+  float* ab = red;                                                  // reused: [C][2] affine
+  double* gstat = reinterpret_cast<double*>(red + 2 * lanes * C);   // [G][2] mean, rstd
+  float* gb = reinterpret_cast<float*>(gstat + 2 * G);              // [2][C] gamma, beta
+  uint64_t* bar = reinterpret_cast<uint64_t*>(gb + 2 * C);
+  __shared__ int s_abort;  // a bounded wait gave up: stop
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+    s_abort = 0;
+  }
+  __syncthreads();
+  const double count = (double)Cg * (double)p.HW;
+  uint32_t phase = 0;
+  for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
+    const int n = item / p.chunks, k = item % p.chunks;
+    const int p0 = k * p.px, np = min(p.px, p.HW - p0);
+    const uint32_t bytes1 = (uint32_t)np * C1 * 2, bytes2 = (uint32_t)np * C2 * 2;
+    const __nv_bfloat16* src1 = p.x + (int64_t)n * p.sn + (int64_t)p0 * C1;
+    const __nv_bfloat16* src2 = p.x2 ? p.x2 + (int64_t)n * p.sn2 + (int64_t)p0 * C2 : nullptr;
+    uint8_t* d2 = data + bytes1;
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bar, bytes1 + bytes2);
+      bulk_g2s(data, src1, bytes1, bar);
+      if (bytes2) bulk_g2s(d2, src2, bytes2, bar);
+    }
+    if (item == (int)blockIdx.x)  // affine parameters, fetched while the chunk is in flight
+      for (int c = tid; c < C; c += kGnFusedThreads) {
+        gb[c] = p.w ? load_as_f32(p.w, c, p.wbd) : 1.f;
+        gb[C + c] = p.b ? load_as_f32(p.b, c, p.wbd) : 0.f;
+      }
+    int ok = mbar_wait(bar, phase, 40, &s_abort) ? 1 : 0;
+    phase ^= 1;
+    // partial sums: thread t owns channel vector t % V of pixel lane t / V (fixed order)
+    for (int t = tid; t < lanes * V; t += kGnFusedThreads) {
+      const int lane = t / V, v = t % V;
+      float s8[8], q8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s8[j] = q8[j] = 0.f;
+      const bool first = v * 8 < C1;
+      const uint8_t* base = first ? data + v * 16 : d2 + (v * 8 - C1) * 2;
+      const int pitch = (first ? C1 : C2) * 2;
+#pragma unroll 4
+      for (int px = lane; px < np; px += lanes) {
+        const uint4 u = *reinterpret_cast<const uint4*>(base + px * pitch);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          s8[2 * j] += f.x;
+          q8[2 * j] = __fmaf_rn(f.x, f.x, q8[2 * j]);
+          s8[2 * j + 1] += f.y;
+          q8[2 * j + 1] = __fmaf_rn(f.y, f.y, q8[2 * j + 1]);
+        }
+      }
+      float4* rs = reinterpret_cast<float4*>(red + lane * C + v * 8);
+      float4* rq = reinterpret_cast<float4*>(red + lanes * C + lane * C + v * 8);
+      rs[0] = make_float4(s8[0], s8[1], s8[2], s8[3]);
+      rs[1] = make_float4(s8[4], s8[5], s8[6], s8[7]);
+      rq[0] = make_float4(q8[0], q8[1], q8[2], q8[3]);
+      rq[1] = make_float4(q8[4], q8[5], q8[6], q8[7]);
+    }
+    __syncthreads();
+    for (int c = tid; c < C; c += kGnFusedThreads) {
+      float s = 0.f, q = 0.f;
+      for (int l = 0; l < lanes; ++l) {
+        s += red[l * C + c];
+        q += red[lanes * C + l * C + c];
+      }
+      red[c] = s;
+      red[lanes * C + c] = q;
+    }
+    __syncthreads();
+    double* part_n = p.part + (int64_t)n * p.chunks * G * 2;
+    for (int g = tid; g < G; g += kGnFusedThreads) {
+      double s = 0.0, q = 0.0;
+      for (int c = g * Cg; c < (g + 1) * Cg; ++c) {
+        s += red[c];
+        q += red[lanes * C + c];
+      }
+      __stcg(part_n + ((int64_t)k * G + g) * 2, s);
+      __stcg(part_n + ((int64_t)k * G + g) * 2 + 1, q);
+    }
+    __syncthreads();
+    // publish, then wait for every chunk of image n (bounded)
+    if (tid == 0) {
+      __threadfence();
+      atomicAdd(&p.arrived[n], 1u);
+      const long long start = clock64();
+      while (true) {
+        unsigned a;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(a) : "l"(&p.arrived[n]) : "memory");
+        if (a >= (unsigned)p.chunks) break;
+        if (s_abort || clock64() - start > kWaitBudgetCycles) {
+          report_device_error(41);
+          s_abort = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
+      __threadfence();
+    }
+    __syncthreads();
+    ok = ok && !s_abort;
+    // group statistics of image n: one warp per group, lane l sums chunks l, l + 32, ... and a
+    // fixed xor tree combines the lanes (the same order as gn_finalize_table_kernel)
+    {
+      const int wid = tid >> 5, lane = tid & 31;
+      constexpr int W = kGnFusedThreads / 32, GPW = 4;  // a warp's groups g0 + W * i, loads in flight together
+      for (int g0 = wid; g0 < G; g0 += W * GPW) {
+        double s[GPW], q[GPW];
+#pragma unroll
+        for (int i = 0; i < GPW; ++i) s[i] = q[i] = 0.0;
+        for (int c = lane; c < p.chunks; c += 32) {
+#pragma unroll
+          for (int i = 0; i < GPW; ++i) {
+            const int g = g0 + W * i;
+            if (g < G) {
+              const double2 v = __ldcg(reinterpret_cast<const double2*>(part_n + ((int64_t)c * G + g) * 2));
+              s[i] += v.x;
+              q[i] += v.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < GPW; ++i) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            s[i] += __shfl_xor_sync(0xffffffffu, s[i], o);
+            q[i] += __shfl_xor_sync(0xffffffffu, q[i], o);
+          }
+          const int g = g0 + W * i;
+          if (lane == 0 && g < G) {
+            const double mean = s[i] / count;
+            double var = q[i] / count - mean * mean;
+            if (var < 0) var = 0;
+            gstat[2 * g] = mean;
+            gstat[2 * g + 1] = 1.0 / sqrt(var + p.eps);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    for (int c = tid; c < C; c += kGnFusedThreads) {
+      const int g = c / Cg;
+      const float rstd = (float)gstat[2 * g + 1], mf = (float)gstat[2 * g];
+      const float2 t = gn_affine_v(rstd, mf, p.w != nullptr, gb[c], p.b != nullptr, gb[C + c]);
+      ab[2 * c] = t.x;
+      ab[2 * c + 1] = t.y;
+    }
+    __syncthreads();
+    // normalise: thread (lane, v) keeps the (a, b) pairs of its 8 channels in registers and walks
+    // pixels lane, lane + lanes, ... (conflict-free 16-byte shared-memory accesses); one source is
+    // normalised in place and stored with a bulk copy, two sources go straight to global memory
+    for (int t = tid; t < lanes * V; t += kGnFusedThreads) {
+      const int lane = t / V, v = t % V;
+      float a8[8], b8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        a8[j] = ab[2 * (v * 8 + j)];
+        b8[j] = ab[2 * (v * 8 + j) + 1];
+      }
+      const bool first = v * 8 < C1;
+      uint8_t* base = first ? data + v * 16 : d2 + (v * 8 - C1) * 2;
+      const int pitch = (first ? C1 : C2) * 2;
+      uint4* dst = reinterpret_cast<uint4*>(p.y + ((int64_t)n * p.HW + p0) * C) + v;
+#pragma unroll 4
+      for (int px = lane; px < np; px += lanes) {
+        uint4 u = *reinterpret_cast<const uint4*>(base + px * pitch);
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          float r0 = __fmaf_rn(f.x, a8[2 * j], b8[2 * j]), r1 = __fmaf_rn(f.y, a8[2 * j + 1], b8[2 * j + 1]);
+          if (p.silu) {
+            r0 = silu_bf16out(r0);
+            r1 = silu_bf16out(r1);
+          }
+          h[j] = __floats2bfloat162_rn(r0, r1);
+        }
+        if (!p.x2)
+          *reinterpret_cast<uint4*>(base + px * pitch) = u;
+        else if (ok)
+          dst[(int64_t)px * V] = u;
+      }
+    }
+    if (!p.x2) {
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0 && ok) {
+        bulk_s2g(p.y + ((int64_t)n * p.HW + p0) * C, data, bytes1);
+        bulk_commit();
+      }
+    }
+    // the next item's copy overwrites `data` and `red`: the store must have read them, and the
+    // generic-proxy accesses above are ordered before that asynchronous write
+    fence_async_smem();
+    if (tid == 0) bulk_wait_read0();
+    __syncthreads();
+    if (!ok) break;
+  }
+  if (tid == 0) bulk_wait0();
+}
+
+MT_STATUS_READER(read_status_norm)
+
+
+// Shared memory of the fused kernel for C channels and G groups.
+static size_t gn_fused_smem(int64_t C, int64_t G) {
+  const int64_t V = C / 8;
+  const int64_t lanes = V >= kGnThreads ? 1 : kGnThreads / V;
+  return kGnFusedBytes + align_up((size_t)2 * lanes * C * sizeof(float), 16) + (size_t)G * 2 * sizeof(double) +
+         (size_t)2 * C * sizeof(float) + 16;
+}
+
+// Launches the fused path when it applies: returns 1 (launched, *rc the status) or 0 (not taken:
+// the chunk exceeds kGnFusedBytes, the CTAs that fit on the GPU at once are fewer than an image's
+// chunks, or MT_GN_FUSED=0).  The decision depends on (C, HW, G) and the device only.
+static int gn_fused_try(__nv_bfloat16* y, const __nv_bfloat16* x, int64_t sn, const __nv_bfloat16* x2, int64_t sn2,
+                        int64_t C1, const void* w, const void* b, int wbd, int64_t N, int64_t C, int64_t HW, int64_t G,
+                        double eps, int silu, double* part, unsigned* arrived, cudaStream_t st, int* rc) {
+  static const bool off = [] {
+    const char* e = getenv("MT_GN_FUSED");
+    return e && e[0] == '0';
+  }();
+  if (off) return 0;
+  // the three-launch path's chunking: ceil(HW / gn_chunk_px(C)) chunks of ceil(HW / chunks) pixels
+  const int64_t chunks = (HW + gn_chunk_px(C) - 1) / gn_chunk_px(C);
+  const int64_t px = (HW + chunks - 1) / chunks;
+  if (px * C * 2 > kGnFusedBytes || chunks > kGnMaxChunks || HW > (1 << 30)) return 0;
+  const size_t smem = gn_fused_smem(C, G);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    if (cudaFuncSetAttribute(gn_fused_cl_bf16x8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    attr_set[dev & 63] = true;
+  }
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gn_fused_cl_bf16x8_kernel, kGnFusedThreads, smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (occ < 1) return 0;
+  // one item per CTA: taken while the whole batch fits on the GPU at once and fills at least
+  // every SM (the three-launch path is faster for more items, which need several rounds, and for
+  // fewer, where its finer-grained launches use more of the GPU)
+  const int64_t resident = (int64_t)occ * num_sms();
+  if (resident < N * chunks || N * chunks < num_sms()) return 0;
+  GnFusedParams p{};
+  p.x = x;
+  p.x2 = x2;
+  p.y = y;
+  p.sn = sn;
+  p.sn2 = sn2;
+  p.C = (int)C;
+  p.C1 = x2 ? (int)C1 : (int)C;
+  p.HW = (int)HW;
+  p.G = (int)G;
+  p.px = (int)px;
+  p.chunks = (int)chunks;
+  p.items = (int)(N * chunks);
+  p.w = w;
+  p.b = b;
+  p.wbd = wbd;
+  p.eps = eps;
+  p.silu = silu;
+  p.part = part;
+  p.arrived = arrived;
+  *rc = cuda_check(cudaMemsetAsync(arrived, 0, (size_t)N * sizeof(unsigned), st), "group_norm counters");
+  if (*rc) return 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)std::min<int64_t>(resident, p.items));
+  cfg.blockDim = dim3(kGnFusedThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gn_fused_cl_bf16x8_kernel, p);
+  *rc = e == cudaSuccess ? check_launch("group_norm fused") : cuda_check(e, "group_norm fused launch");
+  return 1;
+}
+
 // The channels-last bf16 path (dense [N, HW, C] in and out, C % 8 == 0): per-image partial sums,
 // finalize into a per-(image, channel) affine table, apply.  With gn_l2_group_bytes() > 0 the
 // images are processed in groups (statistics, table and apply of one group back to back).  The
@@ -720,6 +1099,13 @@ size_t group_norm_workspace(int64_t N, int64_t C, int64_t HW, int64_t G) {
 static int gn_fast_cl(__nv_bfloat16* y, const __nv_bfloat16* x, int64_t sn, const __nv_bfloat16* x2, int64_t sn2,
                       int64_t C1, const void* w, const void* b, int wbd, int64_t N, int64_t C, int64_t HW, int64_t G,
                       double eps, int silu, double* part, float2* tab, int chunks, cudaStream_t st) {
+  {
+    // the per-image arrival counters of the fused kernel live in the affine-table region
+    int rc = MT_OK;
+    if (gn_fused_try(y, x, sn, x2, sn2, C1, w, b, wbd, N, C, HW, G, eps, silu, part,
+                     reinterpret_cast<unsigned*>(tab), st, &rc))
+      return rc;
+  }
   const int64_t img_bytes = HW * C * 2;
   const int64_t group_bytes = gn_l2_group_bytes();
   const int64_t per = group_bytes > 0 ? std::max<int64_t>(1, group_bytes / img_bytes) : N;

@@ -108,6 +108,7 @@ int sdpa_tc_path(const mt_sdpa_desc& d);
 int read_status_gemm(int clear);
 int run_wait_timeout_selftest(long long budget_cycles, cudaStream_t st);
 int read_status_attention(int clear);
+int read_status_norm(int clear);
 #define MT_STATUS_READER(name)                                                   \
   int name(int clear) {                                                          \
     int v = 0;                                                                   \

@@ -6,6 +6,8 @@ rtol 2e-2 against the fp32 oracle evaluated on the same bf16-rounded inputs.  Be
 error is meaningless for outputs that cancel to ~0, each check also allows an absolute error of
 rtol * max|reference|.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -136,6 +138,30 @@ def test_group_norm_silu(shape, G, layout):
     xb = bf16_round(x)
     gb = mt.group_norm(cu(x, "bfloat16").contiguous(memory_format=mt.channels_last), G, cu(w), cu(b), fuse_silu=True)
     check(gb.numpy(), oracle.silu_f32(oracle.group_norm_f32(xb, G, w, b)), BF16_RTOL)
+
+
+@pytest.mark.parametrize("n,c,h,w,k", [(24, 320, 64, 64, 8), (16, 320, 50, 50, 10), (40, 1280, 16, 16, 20),
+                                       (12, 640, 30, 30, 10), (80, 2560, 8, 8, 37)])
+def test_group_norm_single_read(n, c, h, w, k):
+    """Channels-last bf16 GroupNorm of a batch whose chunks fill the GPU once (k images here) runs
+    as ONE cooperative launch (chunk in shared memory, one read and one write of the activation);
+    the whole batch (n images) takes the three-launch path.  The two paths agree bit for bit
+    (ragged last chunks, one lane per pixel at 2560 channels), so a sample's result never depends
+    on the batch, and both are within the bf16 tolerance of the oracle (reference group_norm,
+    tensor.cpp:18643-18963)."""
+    x = rnd(n, c, h, w, seed=n + c, scale=1.5) + 0.3
+    wt, bs = rnd(c, seed=1), rnd(c, seed=2)
+    xd = cu(x, "bfloat16").contiguous(memory_format=mt.channels_last)
+    lib = mt._lib.lib()
+    got = mt.group_norm(xd, 32, cu(wt), cu(bs), fuse_silu=True).numpy()
+    n0 = lib.mt_cuda_launch_count()
+    part = mt.group_norm(xd[n - k:], 32, cu(wt), cu(bs), fuse_silu=True)
+    if os.environ.get("MT_GN_FUSED", "1") != "0":
+        assert lib.mt_cuda_launch_count() - n0 == 1  # statistics, affine and apply in one kernel
+    np.testing.assert_array_equal(got[n - k:], part.numpy())
+    ref = oracle.silu_f32(oracle.group_norm_f32(bf16_round(x[:2]), 32, wt, bs))
+    check(got[:2], ref, BF16_RTOL)
+    check(part.numpy()[-2:], oracle.silu_f32(oracle.group_norm_f32(bf16_round(x[-2:]), 32, wt, bs)), BF16_RTOL)
 
 
 def test_group_norm_batch_independent():
