@@ -200,6 +200,7 @@ def run_ours(args):
     mt.cuda.set_device(local)
     dist = comm = None
     if world > 1:  # host plumbing over gloo; the device all-gather is NCCL through the C ABI
+        os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")  # single node: loopback rendezvous
         dist = parallel.init("gloo")
         comm = parallel.NcclCommunicator(rank, world, dist.distributed_c10d._get_default_store())
     gb = args.global_batch
