@@ -241,6 +241,96 @@ __global__ void __launch_bounds__(256) layer_norm_bf16_sub_kernel(__nv_bfloat16*
   }
 }
 
+// Persistent variant of layer_norm_bf16_sub_kernel for rows of 5 * LPR vectors: a grid of three
+// CTAs per SM walks row groups (8 warps x 32 / LPR rows) with a stride of the grid, keeps the
+// next group's loads in flight while it reduces and stores the current one, and reads gamma /
+// beta (as fp32) from shared memory filled once per CTA.  The per-row arithmetic is the same
+// sequence as layer_norm_bf16_sub_kernel's.
+template <int VPL, int LPR>
+__global__ void __launch_bounds__(256, 3) layer_norm_bf16_persist_kernel(__nv_bfloat16* y, const __nv_bfloat16* x,
+                                                                      const void* w, const void* b, int wbd,
+                                                                      int64_t rows, int cols, float eps) {
+  extern __shared__ float ln_wb[];  // [2][cols]
+  constexpr int RPW = 32 / LPR;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / LPR, l = lane % LPR;
+  const int nv = cols / 8;
+  for (int c = threadIdx.x; c < cols; c += 256) {
+    ln_wb[c] = w ? load_as_f32(w, c, wbd) : 1.f;
+    ln_wb[cols + c] = b ? load_as_f32(b, c, wbd) : 0.f;
+  }
+  __syncthreads();
+  const int64_t groups = (rows + 8 * RPW - 1) / (8 * RPW);
+  auto load = [&](int64_t g, uint4 (&u)[VPL]) {
+    const int64_t row = (g * 8 + (threadIdx.x >> 5)) * RPW + sub;
+    const uint4* src = reinterpret_cast<const uint4*>(x + row * cols);
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int vi = l + LPR * k;
+      u[k] = (g < groups && row < rows && vi < nv) ? __ldcs(src + vi) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  uint4 cur[VPL], nxt[VPL];
+  int64_t g = blockIdx.x;
+  load(g, cur);
+  for (; g < groups; g += gridDim.x) {
+    load(g + gridDim.x, nxt);
+    const int64_t row = (g * 8 + (threadIdx.x >> 5)) * RPW + sub;
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        s += f.x + f.y;
+      }
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / (float)cols;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k)
+      if (l + LPR * k < nv) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[k]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          q += (f.x - mean) * (f.x - mean);
+          q += (f.y - mean) * (f.y - mean);
+        }
+      }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float inv = rsqrtf(q / (float)cols + eps);
+    if (row < rows) {
+      uint4* dst = reinterpret_cast<uint4*>(y + row * cols);
+#pragma unroll
+      for (int k = 0; k < VPL; ++k) {
+        const int vi = l + LPR * k;
+        if (vi >= nv) continue;
+        const float4* wv = reinterpret_cast<const float4*>(ln_wb + vi * 8);
+        const float4* bv = reinterpret_cast<const float4*>(ln_wb + cols + vi * 8);
+        const float4 w0 = wv[0], w1 = wv[1], b0 = bv[0], b1 = bv[1];
+        const float gw[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const float gb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[k]);
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          o[j] = pack_bf16x2((f.x - mean) * inv * gw[2 * j] + gb[2 * j],
+                             (f.y - mean) * inv * gw[2 * j + 1] + gb[2 * j + 1]);
+        }
+        __stcs(dst + vi, make_uint4(o[0], o[1], o[2], o[3]));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) cur[k] = nxt[k];
+  }
+}
+
 int launch_layer_norm(void* y, int yd, const void* x, int xd, const void* w, const void* b, int wbd, int64_t rows,
                       int64_t cols, double eps, cudaStream_t st) {
   if (rows == 0 || cols == 0) return MT_OK;
@@ -258,6 +348,24 @@ int launch_layer_norm(void* y, int yd, const void* x, int xd, const void* w, con
       const char* e = getenv("MT_LN_V5");
       return !(e && e[0] == '0');
     }();
+    // persistent grid-stride variant of the same mapping (MT_LN_PERSIST=0 turns it off)
+    static const bool persist = [] {
+      const char* e = getenv("MT_LN_PERSIST");
+      return !(e && e[0] == '0');
+    }();
+    if (v5 && persist && nv % 5 == 0 && (nv / 5 == 8 || nv / 5 == 16 || nv / 5 == 32)) {
+      const int lpr = nv / 5, rpc = 8 * (32 / lpr);
+      const int64_t groups = (rows + rpc - 1) / rpc;
+      const size_t sh = 2 * (size_t)cols * sizeof(float);
+      const unsigned grid = (unsigned)std::min<int64_t>(groups, (int64_t)num_sms() * 3);  // 3 resident per SM
+      if (lpr == 8)
+        layer_norm_bf16_persist_kernel<5, 8><<<grid, 256, sh, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+      else if (lpr == 16)
+        layer_norm_bf16_persist_kernel<5, 16><<<grid, 256, sh, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+      else
+        layer_norm_bf16_persist_kernel<5, 32><<<grid, 256, sh, st>>>(yy, xx, w, b, wbd, rows, (int)cols, (float)eps);
+      return check_launch("layer_norm_bf16_persist");
+    }
     if (v5 && nv % 5 == 0 && (nv / 5 == 8 || nv / 5 == 16 || nv / 5 == 32)) {
       const unsigned g8 = (unsigned)((rows + 31) / 32);
       if (nv / 5 == 8)
