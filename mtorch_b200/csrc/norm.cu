@@ -541,6 +541,108 @@ __global__ void __launch_bounds__(kGnThreads, 5) gn_partial_cl_bf16x8_kernel(con
   }
 }
 
+// Persistent variant of gn_partial_cl_bf16x8_kernel for C <= 2048 (one (lane, vector) slot per
+// thread): a grid of four CTAs per SM deals the (image, chunk) items round-robin, and while a
+// CTA reduces one item's slots it already has the next item's first U loads in flight.  Every
+// slot sums the same pixels in the same order as gn_partial_cl_bf16x8_kernel (batch k of U
+// pixels, zeros past the chunk), and the channel / group sums are the same loops, so the
+// partials are bitwise equal to it.
+template <bool TWO = false, int U = 4>
+__global__ void __launch_bounds__(kGnThreads, 4) gn_partial_cl_bf16x8_persist_kernel(
+    const __nv_bfloat16* x, int64_t sn, int64_t C, int64_t HW, int64_t G, int chunks, int items, double* part,
+    const __nv_bfloat16* x2 = nullptr, int64_t sn2 = 0, int64_t C1 = 0) {
+  extern __shared__ float gn_sh[];  // [2][lanes * C]
+  const int64_t per = (HW + chunks - 1) / chunks;
+  const int V = (int)(C / 8);
+  const int lanes = V >= kGnThreads ? 1 : kGnThreads / V;
+  const int64_t slots = (int64_t)lanes * C;
+  const int t = threadIdx.x;
+  const bool act = t < lanes * V;
+  const int lane = t / V, v = t % V;
+  // this thread's channel vector: its source, pitch between pixels and image stride
+  const __nv_bfloat16* src = x + v * 8;
+  int64_t pitch = C, istride = sn;
+  if (TWO) {
+    if (v * 8 < C1) {
+      pitch = C1;
+    } else {
+      src = x2 + (v * 8 - C1);
+      pitch = C - C1;
+      istride = sn2;
+    }
+  }
+  uint4 u[U];
+  auto load_batch = [&](int item, int p) {
+    const int n = item / chunks, chunk = item % chunks;
+    const int64_t p1 = min(HW, chunk * per + per);
+    const __nv_bfloat16* xv = src + (int64_t)n * istride;
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int pp = p + k * lanes;
+      u[k] = pp < p1 ? *reinterpret_cast<const uint4*>(xv + (int64_t)pp * pitch) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  int item = blockIdx.x;
+  if (act && item < items) load_batch(item, (int)((item % chunks) * per) + lane);
+  for (; item < items; item += gridDim.x) {
+    const int n = item / chunks, chunk = item % chunks;
+    const int64_t p0 = chunk * per, p1 = min(HW, p0 + per);
+    if (act) {
+      float s[8], q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[j] = q[j] = 0.f;
+      for (int p = (int)(p0 + lane);;) {
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[k]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            s[2 * j] += f.x;
+            q[2 * j] = __fmaf_rn(f.x, f.x, q[2 * j]);
+            s[2 * j + 1] += f.y;
+            q[2 * j + 1] = __fmaf_rn(f.y, f.y, q[2 * j + 1]);
+          }
+        }
+        p += U * lanes;
+        if (p >= p1) break;
+        load_batch(item, p);
+      }
+      // the next item's first batch goes out before this item's reduction
+      const int nxt = item + gridDim.x;
+      if (nxt < items) load_batch(nxt, (int)((nxt % chunks) * per) + lane);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        gn_sh[lane * C + v * 8 + j] = s[j];
+        gn_sh[slots + lane * C + v * 8 + j] = q[j];
+      }
+    }
+    __syncthreads();
+    for (int64_t c = t; c < C; c += kGnThreads) {
+      float s = 0.f, q = 0.f;
+      for (int64_t l = 0; l < lanes; ++l) {
+        s += gn_sh[l * C + c];
+        q += gn_sh[slots + l * C + c];
+      }
+      gn_sh[c] = s;
+      gn_sh[slots + c] = q;
+    }
+    __syncthreads();
+    const int64_t Cg = C / G;
+    for (int64_t g = t; g < G; g += kGnThreads) {
+      double s = 0.0, q = 0.0;
+      for (int64_t c = g * Cg; c < (g + 1) * Cg; ++c) {
+        s += gn_sh[c];
+        q += gn_sh[slots + c];
+      }
+      double* o = part + (((int64_t)n * chunks + chunk) * G + g) * 2;
+      o[0] = s;
+      o[1] = q;
+    }
+    __syncthreads();
+  }
+}
+
 // Per-(image, channel) affine of the normalisation: y = x * a + b with a = rstd * gamma and
 // b = beta - mean * a, so the apply pass needs no division or group lookup.
 __global__ void gn_table_kernel(const float* stats, const void* w, const void* b, int wbd, int64_t N, int64_t C,
@@ -659,20 +761,30 @@ __global__ void __launch_bounds__(256) gn_apply_img_bf16x8_kernel(__nv_bfloat16*
   for (int j = 0; j < 4; ++j) ab[j] = t[j];  // (a0, b0, a1, b1) for channel pairs 2j, 2j+1
   const int pix_step = stride / C8;
   int pix = i0 / C8;
-  for (int i = i0; i < per_img8; i += stride, pix += pix_step) {
-    uint4 v = TWO ? xi[(int64_t)pix * src_c8 + src_off] : xi[i];
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+  // four 16-byte loads in flight per thread (issued before any of their stores)
+  constexpr int U = 4;
+  for (int64_t i = i0; i < per_img8; i += (int64_t)U * stride, pix += U * pix_step) {
+    uint4 v[U];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 f = __bfloat1622float2(h[j]);
-      float r0 = __fmaf_rn(f.x, ab[j].x, ab[j].y), r1 = __fmaf_rn(f.y, ab[j].z, ab[j].w);
-      if (silu) {
-        r0 = silu_bf16out(r0);
-        r1 = silu_bf16out(r1);
+    for (int k = 0; k < U; ++k)
+      if (i + (int64_t)k * stride < per_img8)
+        v[k] = TWO ? xi[(int64_t)(pix + k * pix_step) * src_c8 + src_off] : xi[i + (int64_t)k * stride];
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      if (i + (int64_t)k * stride >= per_img8) break;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v[k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        float r0 = __fmaf_rn(f.x, ab[j].x, ab[j].y), r1 = __fmaf_rn(f.y, ab[j].z, ab[j].w);
+        if (silu) {
+          r0 = silu_bf16out(r0);
+          r1 = silu_bf16out(r1);
+        }
+        h[j] = __floats2bfloat162_rn(r0, r1);
       }
-      h[j] = __floats2bfloat162_rn(r0, r1);
+      yi[i + (int64_t)k * stride] = v[k];
     }
-    yi[i] = v;
   }
 }
 
@@ -1244,7 +1356,20 @@ static int gn_fast_cl(__nv_bfloat16* y, const __nv_bfloat16* x, int64_t sn, cons
       return e && atoi(e) == 8;
     }();
     const dim3 grid(chunks, (unsigned)nc);
-    if (x2 && u8)
+    static const bool persist = [] {
+      const char* e = getenv("MT_GN_PERSIST");
+      return !(e && e[0] == '0');
+    }();
+    const int64_t items = chunks * nc;
+    if (persist && V <= kGnThreads && items < (1LL << 31)) {
+      const unsigned pg = (unsigned)std::min<int64_t>(items, (int64_t)num_sms() * 4);  // 4 resident per SM
+      if (x2)
+        gn_partial_cl_bf16x8_persist_kernel<true, 4><<<pg, kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks, (int)items,
+                                                                                 part_g, x2g, sn2, C1);
+      else
+        gn_partial_cl_bf16x8_persist_kernel<false, 4><<<pg, kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks,
+                                                                                  (int)items, part_g);
+    } else if (x2 && u8)
       gn_partial_cl_bf16x8_kernel<true, 8><<<grid, kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks, part_g, x2g, sn2, C1);
     else if (x2)
       gn_partial_cl_bf16x8_kernel<true, 4><<<grid, kGnThreads, sh, st>>>(xg, sn, C, HW, G, chunks, part_g, x2g, sn2, C1);
