@@ -359,7 +359,7 @@ def run_ours(args):
     del xg
     roofline_hbm = {"bound": "hbm", "unit": "GB/s", "peak": hbm, "peak_kind": f"{peak_kind} copy bandwidth",
                     "algorithmic_bytes": act_bytes}
-    for key, kms, kname in (("group_norm_silu", gn_ms, "gn_partial + gn_finalize_table + gn_apply_img"),
+    for key, kms, kname in (("group_norm_silu", gn_ms, "gn_partial_persist + gn_finalize_table + gn_apply_img"),
                             ("layer_norm", ln_ms, "layer_norm_bf16_persist_kernel")):
         roofline_hbm[key] = {"kernel": kname, "ms_per_call": kms, "achieved": act_bytes / (kms * 1e-3) / 1e9,
                              "frac": act_bytes / (kms * 1e-3) / 1e9 / hbm}
